@@ -1,0 +1,467 @@
+"""Benchmark of the paged-KV attention path on B200 (the isolated kernel sweep).
+
+    python bench.py [--gpus N --steps K --warmup W] [--batch B] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...   (one rank per GPU; weak scaling)
+
+One step = one decoder layer's paged attention for a batch of B sequences (bf16, 16 heads x 64,
+block 16): the KV append of the step's token (reshape_and_cache), paged self-attention decode
+over contexts drawn U[1, 4096] (seed 2; block tables a random permutation of the pool), and
+cross-attention over 1024 encoder tokens per sequence. Synthetic inputs with the sweep's shapes
+and distributions; the pools (about 13 GB at B=1024) are far larger than L2, so no L2 flush is
+needed between steps.
+
+``value`` = algorithmic HBM bytes per step / device time per step (GB/s), inputs resident in HBM.
+``e2e``   = the same bytes over the time of the public API path with host buffers: every step
+            uploads its inputs from pinned host memory, plans on the host, runs the ops and reads
+            both outputs back.
+``roofline`` = the paged self-attention kernel (main + split combine), timed with CUDA events in
+            the timed region, against the measured HBM copy bandwidth.
+``cpu_baseline`` = the C oracle (the restated vllm_cpu_attn arithmetic; the library itself cannot
+            be installed) on the host cores, on a bounded sample of the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import torch
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+H, D, BS, ENC_LEN, MAX_CTX = 16, 64, 16, 1024, 4096
+DTYPE = torch.bfloat16
+ELEM = 2
+METRIC = "paged-attn HBM GB/s vs 8 TB/s"
+
+
+def load_peaks():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback"
+
+
+def load_traffic():
+    """dram bytes per algorithmic byte of the self-attention kernel, from the committed ncu
+    summary (profiles/paged_decode_traffic.json), if one exists."""
+    path = os.path.join(REPO, "profiles", "paged_decode_traffic.json")
+    try:
+        with open(path) as f:
+            return json.load(f)
+    except (OSError, ValueError):
+        return None
+
+
+# ------------------------------------------------------------------------------------ workload
+
+def make_workload(batch: int, seed: int, device):
+    """Seeded synthetic step of the sweep (host-side metadata + device pools and inputs)."""
+    g = torch.Generator().manual_seed(seed)
+    ctx = torch.randint(1, MAX_CTX + 1, (batch,), generator=g, dtype=torch.int32)
+    nblk = (ctx + BS - 1) // BS
+    n_self = int(nblk.sum())
+    perm = torch.randperm(n_self, generator=g).to(torch.int32)
+    width = int(nblk.max())
+    table = torch.zeros(batch, width, dtype=torch.int32)
+    offs = torch.cumsum(nblk, 0) - nblk
+    for b in range(batch):
+        table[b, : nblk[b]] = perm[offs[b]: offs[b] + nblk[b]]
+    cw = math.ceil(ENC_LEN / BS)
+    n_cross = batch * cw
+    cross_table = torch.randperm(n_cross, generator=g).to(torch.int32).view(batch, cw).contiguous()
+    pos = ctx - 1
+    slots = table[torch.arange(batch), (pos // BS).long()].long() * BS + (pos % BS).long()
+    w = dict(batch=batch, ctx=ctx, table=table, cross_table=cross_table, slots=slots,
+             cross_lens=torch.full((batch,), ENC_LEN, dtype=torch.int32),
+             qsl=torch.arange(batch + 1, dtype=torch.int32), n_self=n_self, n_cross=n_cross)
+    if device is not None:
+        gd = torch.Generator(device=device).manual_seed(seed)
+        rnd = lambda *s: torch.randn(*s, generator=gd, device=device, dtype=DTYPE)  # noqa: E731
+        w.update(k_cache=rnd(n_self, H, BS, D), v_cache=rnd(n_self, H, BS, D),
+                 ck_cache=rnd(n_cross, H, BS, D), cv_cache=rnd(n_cross, H, BS, D),
+                 q=rnd(batch, H, D), k_new=rnd(batch, H, D), v_new=rnd(batch, H, D), qc=rnd(batch, H, D))
+    return w
+
+
+def algorithmic_bytes(w) -> dict:
+    """Minimum HBM bytes of one step (per op), as counted in the design notes."""
+    B, ctx = w["batch"], w["ctx"].long()
+    row = H * D * ELEM
+    nblk = (ctx + BS - 1) // BS
+    self_b = int(2 * ctx.sum()) * row + 2 * B * row + 4 * int(nblk.sum()) + 4 * B + 4 * (B + 1)
+    append_b = 4 * B * row + 8 * B
+    cross_b = 2 * B * ENC_LEN * row + 2 * B * row + 4 * B * math.ceil(ENC_LEN / BS) + 4 * B + 4 * (B + 1)
+    return {"self": self_b, "append": append_b, "cross": cross_b, "total": self_b + append_b + cross_b}
+
+
+# ---------------------------------------------------------------------------------- the step
+
+class Step:
+    """The three ops of one step through the public API (vflorence_b200.paged_ops)."""
+
+    def __init__(self, w, device):
+        from vflorence_b200 import paged_ops as ops
+
+        self.ops, self.w, self.device = ops, w, device
+        self.dev = {k: w[k].to(device) for k in ("table", "cross_table", "slots", "ctx", "cross_lens", "qsl")}
+        self.meta_self = ops.get_scheduler_metadata(w["batch"], H, H, D, w["ctx"], DTYPE, w["qsl"], False,
+                                                    "sm100", BS)
+        self.meta_cross = ops.get_scheduler_metadata(w["batch"], H, H, D, w["cross_lens"], DTYPE, w["qsl"],
+                                                     False, "sm100", BS)
+        self.out = torch.empty_like(w["q"])
+        self.out_c = torch.empty_like(w["qc"])
+        plan_s, plan_c = ops.plan_of(self.meta_self), ops.plan_of(self.meta_cross)
+        self.launches = 1 + (1 + (plan_s.num_splits > 1)) + (1 + (plan_c.num_splits > 1))
+        self.plans = (plan_s, plan_c)
+
+    def append(self, k_new, v_new, slots):
+        self.ops.reshape_and_cache(k_new, v_new, self.w["k_cache"], self.w["v_cache"], slots)
+
+    def self_attn(self, q, out, meta, ctx, qsl, table):
+        self.ops.attention_with_kv_cache(q, self.w["k_cache"], self.w["v_cache"], out, qsl, ctx, D ** -0.5,
+                                         False, table, meta)
+
+    def cross_attn(self, qc, out, meta, lens, qsl, table):
+        self.ops.attention_with_kv_cache(qc, self.w["ck_cache"], self.w["cv_cache"], out, qsl, lens, D ** -0.5,
+                                         False, table, meta)
+
+
+# ------------------------------------------------------------------------------------ clocks
+
+class ClockSampler:
+    """nvidia-smi samples of this GPU during the timed region."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+        phys = device_index
+        if vis:
+            ids = [v.strip() for v in vis.split(",") if v.strip()]
+            if device_index < len(ids) and ids[device_index].isdigit():
+                phys = int(ids[device_index])
+        self.phys = phys
+        self.proc = None
+        self.path = os.path.join(REPO, "gpurun_out", f"clocks_gpu{phys}.csv") if os.path.isdir(
+            os.path.join(REPO, "gpurun_out")) else f"/tmp/vfl_clocks_{os.getpid()}.csv"
+
+    def __enter__(self):
+        try:
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.phys), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=self.fh, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.fh.close()
+
+    def summary(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        rows = []
+        with open(self.path) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) != 8:
+                    continue
+                try:
+                    rows.append((float(parts[0]), float(parts[1]), float(parts[2]), parts[3:]))
+                except ValueError:
+                    continue
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        reasons = sorted({n for r in rows for n, v in zip(names, r[3][1:]) if v.lower().startswith("active")})
+        return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_max_mhz": max(r[1] for r in rows),
+                "samples": len(rows), "power_w_max": max(r[2] for r in rows), "reasons": reasons}
+
+
+# ------------------------------------------------------------------------------- CPU baseline
+
+def cpu_baseline(batch: int, seconds: float = 10.0, sample: int = 32):
+    """The C oracle on the host cores over ``sample`` sequences of the same workload."""
+    sys.path.insert(0, os.path.join(REPO, "oracle"))
+    import oracle
+
+    oracle.build()
+    w = make_workload(batch, 2, None)
+    rows = torch.arange(sample)
+    ctx = w["ctx"][rows]
+    nblk = (ctx + BS - 1) // BS
+    # compact host pools holding exactly the sampled sequences' blocks (values N(0, 1))
+    g = torch.Generator().manual_seed(5)
+    n_self = int(nblk.sum())
+    kc = torch.randn(n_self, H, BS, D, generator=g).to(DTYPE)
+    vc = torch.randn(n_self, H, BS, D, generator=g).to(DTYPE)
+    table = torch.zeros(sample, int(nblk.max()), dtype=torch.int32)
+    pos = 0
+    for i in range(sample):
+        table[i, : nblk[i]] = torch.arange(pos, pos + int(nblk[i]), dtype=torch.int32)
+        pos += int(nblk[i])
+    cw = math.ceil(ENC_LEN / BS)
+    ck = torch.randn(sample * cw, H, BS, D, generator=g).to(DTYPE)
+    cv = torch.randn(sample * cw, H, BS, D, generator=g).to(DTYPE)
+    ctab = torch.arange(sample * cw, dtype=torch.int32).view(sample, cw)
+    q = torch.randn(sample, H, D, generator=g).to(DTYPE)
+    kn, vn = torch.randn(sample, H, D, generator=g).to(DTYPE), torch.randn(sample, H, D, generator=g).to(DTYPE)
+    p = ctx.long() - 1
+    slots = table[torch.arange(sample), (p // BS)].long() * BS + p % BS
+    qsl = torch.arange(sample + 1, dtype=torch.int32)
+    clens = torch.full((sample,), ENC_LEN, dtype=torch.int32)
+    out, outc = torch.empty_like(q), torch.empty_like(q)
+    threads = oracle.max_threads()
+    sub = dict(batch=sample, ctx=ctx)
+    nbytes = algorithmic_bytes(sub)["total"]
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        oracle.reshape_and_cache(kn, vn, kc, vc, slots)
+        oracle.attention(q, kc, vc, out, qsl, ctx, D ** -0.5, False, table, threads)
+        oracle.attention(q, ck, cv, outc, qsl, clens, D ** -0.5, False, ctab, threads)
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            break
+    return {"value": nbytes * reps / el / 1e9, "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"{sample} of the {batch} sequences (self ctx U[1,4096] + cross enc {ENC_LEN}), "
+                      f"{reps} repetitions in {el:.1f} s",
+            "seconds_per_step": el / reps}
+
+
+# -------------------------------------------------------------------------------------- main
+
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def sum_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+def barrier(world: int):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def run_reference(args, world, rank):
+    if rank != 0:
+        return
+    cb = cpu_baseline(args.batch, seconds=max(1.0, 0.05 * (args.steps + args.warmup)), sample=args.cpu_sample)
+    line = {"impl": "reference", "metric": METRIC, "value": cb["value"], "unit": "GB/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": cb["seconds_per_step"] * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic", "config": config_of(args, world),
+            "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
+            "e2e": {"value": cb["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def config_of(args, world):
+    return {"workload": f"cfg5 paged-attention sweep point: {args.batch} seqs/GPU, self ctx U[1,{MAX_CTX}] "
+                        f"+ append + cross enc {ENC_LEN}",
+            "batch_per_gpu": args.batch, "heads": H, "head_dim": D, "block_size": BS,
+            "cross_enc_len": ENC_LEN, "parallelism": f"request-sharded x{world} (no collective)",
+            "l2": "inputs larger than L2 (pools ~13 GB per GPU at batch 1024), no flush"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=400)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--batch", type=int, default=1024)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--cpu-sample", type=int, default=32)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    if args.impl == "reference":
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        rank = int(os.environ.get("RANK", "0"))
+        run_reference(args, world, rank)
+        return
+
+    world, rank, local = dist_setup()
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    from vflorence_b200 import paged_ops as ops
+
+    w = make_workload(args.batch, 2 + rank, device)
+    step = Step(w, device)
+    nb = algorithmic_bytes(w)
+    stream = torch.cuda.current_stream(device)
+    d = step.dev
+
+    def device_step(ev=None):
+        if ev is not None:
+            ev[0].record(stream)
+        step.append(w["k_new"], w["v_new"], d["slots"])
+        if ev is not None:
+            ev[1].record(stream)
+        step.self_attn(w["q"], step.out, step.meta_self, d["ctx"], d["qsl"], d["table"])
+        if ev is not None:
+            ev[2].record(stream)
+        step.cross_attn(w["qc"], step.out_c, step.meta_cross, d["cross_lens"], d["qsl"], d["cross_table"])
+        if ev is not None:
+            ev[3].record(stream)
+
+    for _ in range(args.warmup):
+        device_step()
+    torch.cuda.synchronize()
+    assert ops.read_device_errors(device) == 0
+
+    # ---- device-resident leg
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
+    barrier(world)
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clocks:
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for i in range(args.steps):
+            device_step(evs[i])
+        end.record(stream)
+        torch.cuda.synchronize()
+    barrier(world)
+    elapsed_ms = start.elapsed_time(end)
+    t_self = sum(e[1].elapsed_time(e[2]) for e in evs) / args.steps
+    t_append = sum(e[0].elapsed_time(e[1]) for e in evs) / args.steps
+    t_cross = sum(e[2].elapsed_time(e[3]) for e in evs) / args.steps
+    elapsed_max = max_over_ranks(elapsed_ms, world)
+    total_bytes = sum_over_ranks(float(nb["total"] * args.steps), world)
+    value = total_bytes / (elapsed_max / 1e3) / 1e9
+
+    # ---- e2e leg: public API with host buffers (pinned inputs up, outputs down, host planning)
+    host_in = {k: w[k].cpu().pin_memory() for k in ("q", "k_new", "v_new", "qc")}
+    host_meta = {k: w[k].pin_memory() for k in ("table", "cross_table", "slots", "ctx", "cross_lens", "qsl")}
+    host_out = torch.empty_like(host_in["q"]).pin_memory()
+    host_out_c = torch.empty_like(host_in["qc"]).pin_memory()
+    h2d = sum(t.nbytes for t in host_in.values()) + sum(t.nbytes for t in host_meta.values())
+    d2h = host_out.nbytes + host_out_c.nbytes
+    e2e_steps = max(3, min(args.steps, 100))
+
+    def e2e_step():
+        dv = {k: t.to(device, non_blocking=True) for k, t in {**host_in, **host_meta}.items()}
+        meta_s = ops.get_scheduler_metadata(args.batch, H, H, D, host_meta["ctx"], DTYPE, host_meta["qsl"],
+                                            False, "sm100", BS)
+        meta_c = ops.get_scheduler_metadata(args.batch, H, H, D, host_meta["cross_lens"], DTYPE,
+                                            host_meta["qsl"], False, "sm100", BS)
+        step.append(dv["k_new"], dv["v_new"], dv["slots"])
+        step.self_attn(dv["q"], step.out, meta_s, dv["ctx"], dv["qsl"], dv["table"])
+        step.cross_attn(dv["qc"], step.out_c, meta_c, dv["cross_lens"], dv["qsl"], dv["cross_table"])
+        host_out.copy_(step.out, non_blocking=True)
+        host_out_c.copy_(step.out_c, non_blocking=True)
+        torch.cuda.current_stream(device).synchronize()  # the caller reads the results
+
+    for _ in range(3):
+        e2e_step()
+    barrier(world)
+    torch.cuda.synchronize()
+    s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s2.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e2.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    e2e_ms = max_over_ranks(s2.elapsed_time(e2), world)
+    e2e_bytes = sum_over_ranks(float(nb["total"] * e2e_steps), world)
+    e2e_value = e2e_bytes / (e2e_ms / 1e3) / 1e9
+    assert ops.read_device_errors(device) == 0
+
+    peak, peak_kind = load_peaks()
+    achieved = nb["self"] / (t_self / 1e3) / 1e9
+    traffic_info = load_traffic()
+    traffic = None
+    if traffic_info and traffic_info.get("dram_bytes_per_algorithmic_byte"):
+        traffic = nb["self"] * float(traffic_info["dram_bytes_per_algorithmic_byte"])
+
+    cb = None
+    if rank == 0 and not args.no_cpu_baseline:
+        cb = cpu_baseline(args.batch, seconds=args.cpu_seconds, sample=args.cpu_sample)
+        cb.pop("seconds_per_step", None)
+
+    if rank == 0:
+        plan_s, plan_c = step.plans
+        line = {
+            "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": elapsed_max / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": config_of(args, world),
+            "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "ms_per_step": e2e_ms / e2e_steps, "steps": e2e_steps},
+            "gpu_launches": step.launches * args.steps,
+            "roofline": {"bound": "hbm", "kernel": "paged_attention_kernel<bf16,64,1> + combine (self decode)",
+                         "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
+                         else "fallback 6650 GB/s", "traffic": traffic,
+                         "algorithmic_bytes_per_launch": nb["self"]},
+            "ops_ms": {"append": t_append, "self_decode": t_self, "cross": t_cross},
+            "ops_gbs": {"append": nb["append"] / t_append / 1e6, "self_decode": nb["self"] / t_self / 1e6,
+                        "cross": nb["cross"] / t_cross / 1e6},
+            "plans": {"self": {"splits": plan_s.num_splits, "blocks_per_split": plan_s.blocks_per_split,
+                               "heads_per_cta": plan_s.heads_per_cta, "stages": plan_s.stages},
+                      "cross": {"splits": plan_c.num_splits, "blocks_per_split": plan_c.blocks_per_split}},
+            "clocks": clocks.summary(),
+            "cpu_baseline": cb,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

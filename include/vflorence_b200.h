@@ -1,0 +1,172 @@
+/*
+ * vflorence_b200 C ABI: the paged-KV attention path of the vflorence engine on B200 (sm_100a).
+ *
+ * The reference engine reaches this path through four functions of the external CPU library
+ * `vllm_cpu_attn` plus one torch index op; each entry point below replaces one of them and
+ * names the reference call site it replaces (paths are inside the vflorence project).
+ *
+ * Conventions
+ *   - Plain pointers and sizes only. Every `void* stream` is a cudaStream_t (NULL = legacy
+ *     default stream). Device pointers must belong to the current CUDA device.
+ *   - No entry point allocates device memory, synchronises the stream or keeps a pointer
+ *     after it returns. Scratch space is passed in by the caller (`workspace`).
+ *   - Every entry point returns a vfl_status. On failure nothing was launched and
+ *     vfl_last_error_message() describes the problem (thread-local string).
+ *   - Arguments are validated on the host before any launch. What the host cannot see
+ *     (block ids, slots and context lengths stored in device memory) is bounds-checked by the
+ *     kernels: an out-of-range value is skipped (never dereferenced) and sets a bit in the
+ *     per-device error word read by vfl_read_device_errors().
+ *   - Layouts:
+ *       paged K/V pool  [num_blocks, num_heads, block_size, head_dim], contiguous
+ *       query / output  [num_tokens, num_heads, head_dim], token stride given, head and
+ *                       element strides dense (head stride = head_dim)
+ *       block_table     int32 [num_seqs, table_stride >= table_cols]
+ *       slot_mapping    int64 [num_tokens], slot = block * block_size + offset, < 0 = skip
+ */
+#ifndef VFLORENCE_B200_H_
+#define VFLORENCE_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define VFL_ABI_VERSION 1
+
+typedef enum vfl_status {
+  VFL_OK = 0,
+  VFL_ERR_INVALID_ARGUMENT = 1, /* shape, stride, alignment, dtype or range error */
+  VFL_ERR_UNSUPPORTED = 2,      /* valid for the reference, not built here (e.g. head_dim) */
+  VFL_ERR_WORKSPACE = 3,        /* workspace missing or smaller than the plan needs */
+  VFL_ERR_CUDA = 4              /* a CUDA runtime call failed (launch, attribute, copy) */
+} vfl_status;
+
+typedef enum vfl_dtype {
+  VFL_DTYPE_F32 = 0,  /* torch.float32  */
+  VFL_DTYPE_BF16 = 1  /* torch.bfloat16 */
+} vfl_dtype;
+
+/* Bits of the per-device error word (set by kernels, read by vfl_read_device_errors). */
+#define VFL_DEVERR_BLOCK_ID 0x1u  /* block table entry or copy pair outside [0, num_blocks) */
+#define VFL_DEVERR_SLOT 0x2u      /* slot_mapping entry >= num_blocks * block_size          */
+#define VFL_DEVERR_CONTEXT 0x4u   /* seq_len > table_cols * block_size, or position beyond
+                                     the table; the length was clamped                      */
+#define VFL_DEVERR_TIMEOUT 0x8u   /* a bounded wait on a shared-memory barrier gave up      */
+#define VFL_DEVERR_QUERY 0x10u    /* query_start_loc not non-decreasing / beyond num_tokens  */
+
+/* Launch plan for vfl_attention_with_kv_cache. Built on the host from host-side lengths;
+ * plays the role of vllm_cpu_attn's opaque scheduler metadata. */
+typedef struct vfl_attention_plan {
+  int64_t magic;            /* VFL_PLAN_MAGIC once filled by vfl_plan_attention          */
+  int32_t num_reqs;         /* requests (rows of block_table, entries of seq_lens)       */
+  int32_t num_heads;
+  int32_t head_dim;
+  int32_t block_size;
+  int32_t dtype;            /* vfl_dtype                                                 */
+  int32_t causal;
+  int32_t total_q;          /* query rows = query_start_loc[num_reqs]                    */
+  int32_t max_q_len;        /* longest request in query rows                             */
+  int32_t max_seq_len;      /* longest request in cached tokens                          */
+  int32_t heads_per_cta;    /* heads handled by one CTA (one warp each)                  */
+  int32_t queries_per_cta;  /* query rows of one request handled together (1 or 4)       */
+  int32_t blocks_per_split; /* KV blocks per split-K work item                           */
+  int32_t num_splits;       /* split-K partitions of the longest request                 */
+  int32_t stages;           /* shared-memory pipeline depth (16-token K/V tiles)         */
+  int32_t reserved;
+  int64_t workspace_bytes;  /* scratch the caller must pass (0 = none)                   */
+} vfl_attention_plan;
+
+#define VFL_PLAN_MAGIC 0x31504c4656LL /* "VFLP1" */
+
+/* ---- library ---------------------------------------------------------------------------- */
+
+/* ABI version of the loaded library (VFL_ABI_VERSION at build time). */
+int vfl_abi_version(void);
+
+/* Static description of a status code. */
+const char* vfl_status_string(int status);
+
+/* Message of the last failing call on this host thread ("" if none). */
+const char* vfl_last_error_message(void);
+
+/* Read (and with clear != 0 reset) the current device's error word. Synchronises `stream`. */
+int vfl_read_device_errors(unsigned int* bits, int clear, void* stream);
+
+/* ---- the four vllm_cpu_attn functions -------------------------------------------------------
+ * replaces vllm_cpu_attn.get_isa(dtype, block_size, head_dim)
+ *   (vflorence/engine/model_runner.py:38). Writes "sm100" into buf. Fails with
+ *   VFL_ERR_UNSUPPORTED for a dtype, block size or head_dim the kernels do not cover. */
+int vfl_get_isa(int dtype, int block_size, int head_dim, char* buf, int buf_len);
+
+/* replaces vllm_cpu_attn.get_scheduler_metadata(...)
+ *   (vflorence/layers/attention.py:18-29, vflorence/engine/model_runner.py:308-319).
+ * seq_lens_host / query_start_loc_host are HOST arrays of num_reqs / num_reqs + 1 entries;
+ * query_start_loc_host may be NULL for one query row per request. */
+int vfl_plan_attention(int num_reqs, int num_heads, int num_kv_heads, int head_dim,
+                       int block_size, int dtype, int causal, const int32_t* seq_lens_host,
+                       const int32_t* query_start_loc_host, vfl_attention_plan* plan);
+
+/* replaces vllm_cpu_attn.reshape_and_cache(key, value, k_cache, v_cache, slot_mapping, isa=)
+ *   (vflorence/layers/attention.py:55-57, vflorence/engine/model_runner.py:252-259).
+ * cache[slot // block_size, h, slot % block_size, :] = key[t, h, :] for every token t with
+ * slot = slot_mapping[t] >= 0. key/value token strides are in elements. */
+int vfl_reshape_and_cache(const void* key, const void* value, void* k_cache, void* v_cache,
+                          const int64_t* slot_mapping, int64_t num_tokens, int num_heads,
+                          int head_dim, int block_size, int64_t num_blocks,
+                          int64_t key_token_stride, int64_t value_token_stride, int dtype,
+                          void* stream);
+
+/* replaces vllm_cpu_attn.attention_with_kv_cache(query, k_cache, v_cache, output,
+ *   query_start_loc, seq_lens, scale=, causal=, block_table=, scheduler_metadata=)
+ *   (vflorence/layers/attention.py:61-72 and :98-109).
+ * For request r with query rows [query_start_loc[r], query_start_loc[r+1]) and n = seq_lens[r]
+ * cached tokens, row i attends to the first n tokens (causal: n - (q_end - 1 - i)) of the
+ * pages block_table[r, :]:  out = softmax(scale * q K^T) V, fp32 accumulation.
+ * A request with no visible tokens produces zeros. Rows of several queries that share one
+ * request (beams over one encoder) read each K/V page once. */
+int vfl_attention_with_kv_cache(const vfl_attention_plan* plan, const void* query,
+                                int64_t query_token_stride, const void* k_cache,
+                                const void* v_cache, int64_t num_blocks, void* output,
+                                int64_t output_token_stride, const int32_t* query_start_loc,
+                                const int32_t* seq_lens, const int32_t* block_table,
+                                int64_t table_stride, int32_t table_cols, float scale,
+                                void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- around the four ops --------------------------------------------------------------------
+ * replaces ModelRunner._copy_blocks (vflorence/engine/model_runner.py:162-167):
+ * for every layer l and pair p: k_caches[l][dst_p] = k_caches[l][src_p], same for v_caches,
+ * with gather-then-scatter meaning (all sources are read before any destination is written
+ * requires disjoint source and destination sets, which copy-on-write guarantees; the host
+ * wrapper checks it). block_pairs: device int64 [num_pairs, 2] = (src, dst). block_bytes =
+ * num_heads * block_size * head_dim * element size. One launch for all layers. */
+#define VFL_MAX_COPY_LAYERS 128
+int vfl_copy_blocks(void* const* k_caches, void* const* v_caches, int num_layers,
+                    const int64_t* block_pairs, int num_pairs, int64_t num_blocks,
+                    int64_t block_bytes, void* stream);
+
+/* replaces the per-step list building of ModelRunner._prepare
+ *   (vflorence/engine/model_runner.py:290-306) on the device: for sequence b at position
+ *   p = positions[b] (= num_cached_tokens):
+ *     slot_mapping[b] = block_table[b, p // block_size] * block_size + p % block_size
+ *     context_lens[b] = p + 1
+ *     query_start_loc[b] = b  (and query_start_loc[num_seqs] = num_seqs)
+ *   Any output pointer may be NULL. */
+int vfl_prepare_decode(const int32_t* block_table, int64_t table_stride, int32_t table_cols,
+                       const int32_t* positions, int num_seqs, int block_size,
+                       int64_t* slot_mapping, int32_t* context_lens, int32_t* query_start_loc,
+                       void* stream);
+
+/* replaces the encoder slot computation of ModelRunner._encode
+ *   (vflorence/engine/model_runner.py:240-242): for request g and token t < seq_len,
+ *   slot_mapping[g * seq_len + t] = pages[g, t // block_size] * block_size + t % block_size. */
+int vfl_paged_slots(const int32_t* pages, int64_t pages_stride, int32_t pages_cols,
+                    int num_reqs, int seq_len, int block_size, int64_t* slot_mapping,
+                    void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* VFLORENCE_B200_H_ */

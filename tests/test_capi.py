@@ -1,0 +1,136 @@
+"""The C-ABI library without a GPU: it loads, exports exactly what include/vflorence_b200.h
+declares, and its host-only entry points (get_isa, the planner, argument validation) behave."""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+
+import pytest
+import torch
+
+from conftest import REPO
+
+
+def _declared():
+    text = open(os.path.join(REPO, "include", "vflorence_b200.h")).read()
+    return re.findall(r"^(?:int|const char\*)\s+(vfl_\w+)\(", text, flags=re.M)
+
+
+def test_library_exports_every_declared_symbol(native):
+    from vflorence_b200 import _native
+
+    declared = _declared()
+    assert sorted(declared) == sorted(_native.EXPORTS)
+    for name in declared:
+        assert hasattr(native, name), name
+    assert native.vfl_abi_version() == 1
+
+
+def test_status_strings(native):
+    assert native.vfl_status_string(0) == b"ok"
+    assert b"workspace" in native.vfl_status_string(3)
+
+
+def test_get_isa(native):
+    from vflorence_b200 import paged_ops as ops
+
+    for dt in (torch.float32, torch.bfloat16):
+        for d in sorted(ops.HEAD_DIMS):
+            assert ops.get_isa(dt, 16, d) == "sm100"
+    assert ops.get_isa(torch.bfloat16, 32, 64) == "sm100"
+    for args in ((torch.bfloat16, 16, 512), (torch.bfloat16, 8, 64), (torch.bfloat16, 24, 64)):
+        with pytest.raises(ValueError):
+            ops.get_isa(*args)
+    with pytest.raises(ValueError):
+        ops.get_isa(torch.float16, 16, 64)
+
+
+def _plan(lens, qsl=None, heads=16, d=64, bs=16, dtype=torch.bfloat16, causal=False):
+    from vflorence_b200 import paged_ops as ops
+
+    meta = ops.get_scheduler_metadata(len(lens), heads, heads, d, torch.tensor(lens, dtype=torch.int32),
+                                      dtype, None if qsl is None else torch.tensor(qsl, dtype=torch.int32),
+                                      causal, "sm100", bs)
+    return ops.plan_of(meta)
+
+
+def test_plan_large_batch_splits_long_requests(native):
+    g = torch.Generator().manual_seed(2)
+    lens = torch.randint(1, 4097, (1024,), generator=g).tolist()
+    p = _plan(lens)
+    assert (p.heads_per_cta, p.queries_per_cta, p.stages) == (4, 1, 4)
+    assert p.blocks_per_split * 16 == 256          # items capped at 256 tokens
+    assert p.num_splits == -(-max(lens) // 256)
+    assert p.workspace_bytes >= 1024 * 16 * p.num_splits * (64 + 2) * 4
+    assert p.total_q == 1024 and p.max_seq_len == max(lens)
+
+
+def test_plan_single_long_request_fills_the_gpu(native):
+    p = _plan([4096])
+    ctas = (16 // p.heads_per_cta) * p.num_splits
+    assert ctas >= 148
+
+
+def test_plan_short_batch_needs_no_workspace(native):
+    p = _plan([5, 17, 33], heads=2)
+    assert p.num_splits == 1 and p.workspace_bytes == 0
+    assert p.heads_per_cta == 2
+
+
+def test_plan_grouped_rows(native):
+    p = _plan([577, 577], qsl=[0, 3, 6], heads=12)
+    assert p.queries_per_cta == 4 and p.total_q == 6 and p.max_q_len == 3
+    assert p.heads_per_cta == 4
+
+
+def test_plan_f32_and_wide_heads(native):
+    p = _plan([100], heads=16, d=256, dtype=torch.float32)
+    assert 2 * p.heads_per_cta * 16 * 256 * 4 <= 32 * 1024
+    assert p.stages >= 2
+
+
+def test_plan_rejects_bad_input(native):
+    from vflorence_b200 import paged_ops as ops
+    from vflorence_b200._native import VflError
+
+    with pytest.raises(VflError, match="grouped-query"):
+        ops.get_scheduler_metadata(2, 16, 4, 64, torch.tensor([3, 4], dtype=torch.int32),
+                                   torch.bfloat16, None, False, "sm100", 16)
+    with pytest.raises(VflError, match="< 0"):
+        _plan([3, -1])
+    with pytest.raises(VflError, match="decreases"):
+        _plan([3, 4], qsl=[0, 2, 1])
+    with pytest.raises(ValueError):
+        _plan([3, 4], qsl=[0, 1])
+
+
+def test_attention_rejects_foreign_metadata_without_touching_the_gpu(native):
+    from vflorence_b200 import _native
+
+    plan = _native.AttentionPlan()
+    st = native.vfl_attention_with_kv_cache(ctypes.byref(plan), None, 0, None, None, 0, None, 0, None,
+                                            None, None, 0, 0, 1.0, None, 0, None)
+    assert st == _native.VFL_ERR_INVALID_ARGUMENT
+    assert b"plan" in native.vfl_last_error_message()
+
+
+def test_copy_blocks_host_checks(native):
+    from vflorence_b200 import paged_ops as ops
+
+    assert ops.check_copy_pairs([(0, 2), (1, 3)], 4) == [(0, 2), (1, 3)]
+    for bad in ([(0, 4)], [(0, 2), (1, 2)], [(0, 2), (2, 3)], [(-1, 0)]):
+        with pytest.raises(ValueError):
+            ops.check_copy_pairs(bad, 4)
+
+
+def test_ops_refuse_cpu_tensors(native):
+    from vflorence_b200 import paged_ops as ops
+
+    kc = torch.zeros(4, 2, 16, 64)
+    k = torch.zeros(1, 2, 64)
+    with pytest.raises(ValueError, match="CUDA"):
+        ops.reshape_and_cache(k, k, kc, kc, torch.zeros(1, dtype=torch.int64))
+    with pytest.raises(ValueError, match="CUDA"):
+        ops.copy_blocks([kc], [kc], [(0, 1)])

@@ -1,0 +1,269 @@
+"""Paged attention on the GPU (through the C ABI) against the CPU oracle and the float64 fixtures.
+
+Tolerances (assert_attention_close): float32 1e-5 relative (scaled to the output magnitude),
+bfloat16 2e-2 absolute. At the BASELINE sweep's full size (1024 sequences, contexts up to 4096)
+the oracle checks a sample of rows and size-independent properties cover the rest.
+"""
+
+from __future__ import annotations
+
+import math
+
+import pytest
+import torch
+
+from conftest import assert_attention_close, case_tensors, load_attention_cases
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda", 0)
+CASES = load_attention_cases()
+
+
+def ops():
+    from vflorence_b200 import paged_ops
+
+    return paged_ops
+
+
+def kernel(q, kc, vc, qsl, lens, table, scale, causal=False, *, device_lens=None):
+    o = ops()
+    n, h, bs, d = kc.shape
+    meta = o.get_scheduler_metadata(lens.numel(), h, h, d, lens, kc.dtype, qsl, causal, "sm100", bs)
+    out = torch.full(q.shape, float("nan"), dtype=q.dtype, device=DEV)
+    o.attention_with_kv_cache(q.to(DEV), kc.to(DEV), vc.to(DEV), out, qsl.to(DEV),
+                              (lens if device_lens is None else device_lens).to(DEV), scale, causal,
+                              table.to(DEV), meta)
+    return out.cpu(), o.plan_of(meta)
+
+
+def oracle_attn(oracle_lib, q, kc, vc, qsl, lens, table, scale, causal=False):
+    out = torch.empty_like(q)
+    assert oracle_lib.attention(q, kc, vc, out, qsl, lens, scale, causal, table) == 0
+    return out
+
+
+def random_case(*, num_reqs, heads, head_dim, block_size, max_len, dtype, q_lens=None, seed=0,
+                min_len=0, extra_blocks=3, on_device=False):
+    """Seeded paged case: lengths U[min_len, max_len], block tables a random permutation of the
+    pool, K/V/q N(0, 1) (drawn on the GPU; returned there when ``on_device``)."""
+    g = torch.Generator().manual_seed(seed)
+    gd = torch.Generator(device=DEV).manual_seed(seed)
+    lens = torch.randint(min_len, max_len + 1, (num_reqs,), generator=g, dtype=torch.int32)
+    need = [max(1, math.ceil(int(n) / block_size)) for n in lens]
+    nb = sum(need) + extra_blocks
+    perm = torch.randperm(nb, generator=g).to(torch.int32)
+    table = torch.zeros(num_reqs, max(need), dtype=torch.int32)
+    pos = 0
+    for r, k in enumerate(need):
+        table[r, :k] = perm[pos:pos + k]
+        pos += k
+    kc = torch.randn(nb, heads, block_size, head_dim, generator=gd, device=DEV, dtype=dtype)
+    vc = torch.randn(nb, heads, block_size, head_dim, generator=gd, device=DEV, dtype=dtype)
+    q_lens = q_lens or [1] * num_reqs
+    qsl = torch.tensor([0] + list(torch.tensor(q_lens).cumsum(0).tolist()), dtype=torch.int32)
+    q = torch.randn(int(qsl[-1]), heads, head_dim, generator=gd, device=DEV, dtype=dtype)
+    if not on_device:
+        q, kc, vc = q.cpu(), kc.cpu(), vc.cpu()
+    return q, kc, vc, qsl, lens, table
+
+
+def compact_sample(kc, vc, table, lens, rows, block_size):
+    """CPU copies of only the blocks that ``rows`` read, with their table remapped."""
+    need = [max(1, math.ceil(int(lens[r]) / block_size)) for r in rows.tolist()]
+    ids = torch.cat([table[r, :k] for r, k in zip(rows.tolist(), need)]).long()
+    uniq, inv = torch.unique(ids, return_inverse=True)
+    sub = torch.zeros(len(need), max(need), dtype=torch.int32)
+    pos = 0
+    for i, k in enumerate(need):
+        sub[i, :k] = inv[pos:pos + k].to(torch.int32)
+        pos += k
+    dev_ids = uniq.to(kc.device)
+    return kc[dev_ids].cpu(), vc[dev_ids].cpu(), sub
+
+
+@pytest.mark.parametrize("case", CASES, ids=[c["name"] for c in CASES])
+def test_fixture_cases(oracle_lib, case):
+    t = case_tensors(case)
+    dt = t["q"].dtype
+    got, _ = kernel(t["q"], t["k_cache"], t["v_cache"], t["query_start_loc"], t["seq_lens"],
+                    t["block_table"], case["scale"], bool(case["causal"]))
+    assert_attention_close(got, t["expected"], dt, case["name"] + " vs float64")
+    ref = oracle_attn(oracle_lib, t["q"], t["k_cache"], t["v_cache"], t["query_start_loc"],
+                      t["seq_lens"], t["block_table"], case["scale"], bool(case["causal"]))
+    assert_attention_close(got, ref, dt, case["name"] + " vs oracle")
+
+
+@pytest.mark.parametrize("case", CASES, ids=[c["name"] for c in CASES])
+def test_fixture_cases_other_dtype(oracle_lib, case):
+    other = torch.bfloat16 if case["dtype"] == "f32" else torch.float32
+    t = case_tensors(case, other)
+    got, _ = kernel(t["q"], t["k_cache"], t["v_cache"], t["query_start_loc"], t["seq_lens"],
+                    t["block_table"], case["scale"], bool(case["causal"]))
+    ref = oracle_attn(oracle_lib, t["q"], t["k_cache"], t["v_cache"], t["query_start_loc"],
+                      t["seq_lens"], t["block_table"], case["scale"], bool(case["causal"]))
+    assert_attention_close(got, ref, other, case["name"])
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16], ids=["f32", "bf16"])
+@pytest.mark.parametrize("head_dim", [32, 48, 64, 80, 96, 112, 128, 160, 192, 224, 256])
+@pytest.mark.parametrize("block_size", [16, 32])
+def test_head_dims_and_block_sizes(oracle_lib, dtype, head_dim, block_size):
+    heads = 4 if head_dim <= 128 else 2
+    q, kc, vc, qsl, lens, table = random_case(num_reqs=6, heads=heads, head_dim=head_dim,
+                                              block_size=block_size, max_len=300, dtype=dtype,
+                                              seed=head_dim + block_size)
+    got, _ = kernel(q, kc, vc, qsl, lens, table, head_dim ** -0.5)
+    ref = oracle_attn(oracle_lib, q, kc, vc, qsl, lens, table, head_dim ** -0.5)
+    assert_attention_close(got, ref, dtype, f"D={head_dim} bs={block_size}")
+
+
+@pytest.mark.parametrize("heads", [1, 2, 3, 12, 16])
+def test_head_counts(oracle_lib, heads):
+    q, kc, vc, qsl, lens, table = random_case(num_reqs=5, heads=heads, head_dim=64, block_size=16,
+                                              max_len=200, dtype=torch.bfloat16, seed=heads)
+    got, plan = kernel(q, kc, vc, qsl, lens, table, 0.125)
+    assert heads % plan.heads_per_cta == 0
+    assert_attention_close(got, oracle_attn(oracle_lib, q, kc, vc, qsl, lens, table, 0.125),
+                           torch.bfloat16, f"H={heads}")
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16], ids=["f32", "bf16"])
+def test_grouped_rows_share_pages(oracle_lib, dtype):
+    # beams of one request as several query rows (up to 9 -> three chunks of four)
+    q_lens = [3, 1, 4, 9, 2, 5]
+    q, kc, vc, qsl, lens, table = random_case(num_reqs=6, heads=12, head_dim=64, block_size=16,
+                                              max_len=1024, min_len=300, dtype=dtype, q_lens=q_lens,
+                                              seed=5)
+    got, plan = kernel(q, kc, vc, qsl, lens, table, 0.125)
+    assert plan.queries_per_cta == 4
+    assert_attention_close(got, oracle_attn(oracle_lib, q, kc, vc, qsl, lens, table, 0.125), dtype,
+                           "grouped")
+    # grouped rows equal the per-row (repeated table) computation
+    rows = torch.repeat_interleave(torch.arange(6), torch.tensor(q_lens))
+    got_rows, _ = kernel(q, kc, vc, torch.arange(q.shape[0] + 1, dtype=torch.int32), lens[rows],
+                         table[rows].contiguous(), 0.125)
+    assert_attention_close(got_rows, got, dtype, "grouped vs per-row")
+
+
+def test_causal_rows(oracle_lib):
+    q, kc, vc, qsl, lens, table = random_case(num_reqs=4, heads=2, head_dim=64, block_size=16,
+                                              max_len=90, min_len=1, dtype=torch.float32,
+                                              q_lens=[1, 5, 3, 8], seed=9)
+    got, _ = kernel(q, kc, vc, qsl, lens, table, 0.125, causal=True)
+    ref = oracle_attn(oracle_lib, q, kc, vc, qsl, lens, table, 0.125, causal=True)
+    assert_attention_close(got, ref, torch.float32, "causal")
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16], ids=["f32", "bf16"])
+def test_split_k_long_contexts(oracle_lib, dtype):
+    # few long requests: the planner splits them; results must equal the unsplit oracle
+    q, kc, vc, qsl, lens, table = random_case(num_reqs=3, heads=16, head_dim=64, block_size=16,
+                                              max_len=4096, min_len=2000, dtype=dtype, seed=11)
+    got, plan = kernel(q, kc, vc, qsl, lens, table, 0.125)
+    assert plan.num_splits > 1 and plan.workspace_bytes > 0
+    assert_attention_close(got, oracle_attn(oracle_lib, q, kc, vc, qsl, lens, table, 0.125), dtype,
+                           "split-K")
+
+
+def test_baseline_sweep_b256_against_oracle(oracle_lib):
+    # BASELINE config 5 at batch 256: bf16, 16 heads x 64, block 16, contexts U[1, 4096]
+    q, kc, vc, qsl, lens, table = random_case(num_reqs=256, heads=16, head_dim=64, block_size=16,
+                                              max_len=4096, min_len=1, dtype=torch.bfloat16, seed=2)
+    got, plan = kernel(q, kc, vc, qsl, lens, table, 0.125)
+    ref = oracle_attn(oracle_lib, q, kc, vc, qsl, lens, table, 0.125)
+    assert_attention_close(got, ref, torch.bfloat16, "cfg5 B=256")
+
+
+def test_baseline_sweep_b1024_properties(oracle_lib):
+    o = ops()
+    H, D, bs = 16, 64, 16
+    q, kc, vc, qsl, lens, table = random_case(num_reqs=1024, heads=H, head_dim=D, block_size=bs,
+                                              max_len=4096, min_len=1, dtype=torch.bfloat16, seed=2,
+                                              extra_blocks=0, on_device=True)
+    got, plan = kernel(q, kc, vc, qsl, lens, table, 0.125)
+    assert plan.num_splits > 1
+    # (1) a sample of rows against the oracle
+    g = torch.Generator().manual_seed(0)
+    rows = torch.randperm(1024, generator=g)[:48].sort().values
+    kc_s, vc_s, tab_s = compact_sample(kc, vc, table, lens, rows, bs)
+    ref = oracle_attn(oracle_lib, q[rows.to(DEV)].cpu().contiguous(), kc_s, vc_s,
+                      torch.arange(49, dtype=torch.int32), lens[rows].contiguous(), tab_s, 0.125)
+    assert_attention_close(got[rows], ref, torch.bfloat16, "cfg5 B=1024 sample")
+    # (2) physical placement does not matter: relocate every block, results are bit-identical
+    nb = kc.shape[0]
+    perm = torch.randperm(nb, generator=g)
+    inv = torch.empty_like(perm)
+    inv[perm] = torch.arange(nb)
+    inv_d = inv.to(DEV)
+    got2, _ = kernel(q, kc[inv_d], vc[inv_d], qsl, lens, perm[table.long()].to(torch.int32).contiguous(), 0.125)
+    assert torch.equal(got, got2)
+    # (3) deterministic: a second run gives the same bits
+    got3, _ = kernel(q, kc, vc, qsl, lens, table, 0.125)
+    assert torch.equal(got, got3)
+    assert o.read_device_errors(DEV) == 0
+
+
+def test_constant_values_give_that_value(oracle_lib):
+    q, kc, vc, qsl, lens, table = random_case(num_reqs=8, heads=4, head_dim=64, block_size=16,
+                                              max_len=2000, min_len=1, dtype=torch.float32, seed=4)
+    vc = torch.full_like(vc, 0.375)
+    got, _ = kernel(q, kc, vc, qsl, lens, table, 0.125)
+    assert (got - 0.375).abs().max() <= 1e-6
+
+
+def test_zero_length_rows_and_empty_batches():
+    o = ops()
+    q, kc, vc, qsl, lens, table = random_case(num_reqs=4, heads=2, head_dim=64, block_size=16,
+                                              max_len=40, dtype=torch.bfloat16, seed=1)
+    lens = torch.tensor([0, 5, 0, 40], dtype=torch.int32)
+    got, _ = kernel(q, kc, vc, qsl, lens, table, 0.125)
+    assert torch.all(got[0] == 0) and torch.all(got[2] == 0) and torch.isfinite(got).all()
+    # no requests at all: nothing launched, output untouched
+    meta = o.get_scheduler_metadata(0, 2, 2, 64, torch.zeros(0, dtype=torch.int32), torch.bfloat16,
+                                    None, False, "sm100", 16)
+    out = torch.ones(0, 2, 64, dtype=torch.bfloat16, device=DEV)
+    o.attention_with_kv_cache(out, kc.to(DEV), vc.to(DEV), out, torch.zeros(1, dtype=torch.int32, device=DEV),
+                              torch.zeros(0, dtype=torch.int32, device=DEV), 0.125, False,
+                              torch.zeros(0, 1, dtype=torch.int32, device=DEV), meta)
+
+
+def test_strided_query_from_fused_projection(oracle_lib):
+    # q/k/v chunks of a fused qkv projection: token stride 3 * H * D
+    H, D = 4, 64
+    q0, kc, vc, qsl, lens, table = random_case(num_reqs=7, heads=H, head_dim=D, block_size=16,
+                                               max_len=130, dtype=torch.bfloat16, seed=8)
+    qkv = torch.randn(7, 3 * H * D, dtype=torch.bfloat16, device=DEV)
+    q = qkv[:, : H * D].reshape(7, H, D)
+    assert q.stride(0) == 3 * H * D
+    o = ops()
+    meta = o.get_scheduler_metadata(7, H, H, D, lens, torch.bfloat16, qsl, False, "sm100", 16)
+    out = torch.empty_like(q)
+    o.attention_with_kv_cache(q, kc.to(DEV), vc.to(DEV), out, qsl.to(DEV), lens.to(DEV), 0.125, False,
+                              table.to(DEV), meta)
+    ref = oracle_attn(oracle_lib, q.cpu().contiguous(), kc, vc, qsl, lens, table, 0.125)
+    assert_attention_close(out.cpu(), ref, torch.bfloat16, "strided q")
+
+
+def test_bad_block_ids_are_flagged_not_dereferenced():
+    o = ops()
+    o.read_device_errors(DEV)
+    q, kc, vc, qsl, lens, table = random_case(num_reqs=3, heads=2, head_dim=64, block_size=16,
+                                              max_len=60, min_len=20, dtype=torch.bfloat16, seed=6)
+    table = table.clone()
+    table[1, 0] = kc.shape[0] + 1000
+    table[2, 0] = -7
+    kernel(q, kc, vc, qsl, lens, table, 0.125)
+    assert o.read_device_errors(DEV) & 0x1  # VFL_DEVERR_BLOCK_ID
+    assert o.read_device_errors(DEV) == 0   # cleared by the read
+
+
+def test_device_lengths_beyond_the_plan_are_clamped_and_flagged(oracle_lib):
+    o = ops()
+    o.read_device_errors(DEV)
+    q, kc, vc, qsl, lens, table = random_case(num_reqs=2, heads=2, head_dim=64, block_size=16,
+                                              max_len=40, min_len=40, dtype=torch.float32, seed=7)
+    planned = torch.tensor([20, 30], dtype=torch.int32)
+    got, _ = kernel(q, kc, vc, qsl, planned, table, 0.125, device_lens=torch.tensor([20, 40], dtype=torch.int32))
+    assert o.read_device_errors(DEV) & 0x4  # VFL_DEVERR_CONTEXT
+    ref = oracle_attn(oracle_lib, q, kc, vc, qsl, planned, table, 0.125)
+    assert_attention_close(got, ref, torch.float32, "clamped")

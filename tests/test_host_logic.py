@@ -1,0 +1,58 @@
+"""Host-side bookkeeping around the kernels, checked against the reference engine's recorded
+trace: encoder page allocation (vflorence/engine/model_runner.py:169-177, :232-265), step
+packing (:290-306) and the beam grouping of the cross-attention staging (attention.py:9-39)."""
+
+from __future__ import annotations
+
+import torch
+
+from vflorence_b200.attention import group_rows
+from vflorence_b200.kv_cache import CrossPageAllocator, pack_decode_step
+
+
+def test_cross_pages_replay(engine_trace):
+    for run in engine_trace["runs"]:
+        alloc = CrossPageAllocator(run["num_cross_blocks"])
+        clears = list(run["clears"])
+        for enc in run["encodes"]:
+            # apply the releases that happened before this encode
+            while alloc.free != enc["cross_free_before"]:
+                rid, free_after = clears.pop(0)
+                alloc.release(rid)
+                assert alloc.free == free_after
+            for rids, n in enc["groups"]:
+                pages = alloc.assign(rids, n, run["block_size"])
+                for rid, row in zip(rids, pages):
+                    assert torch.equal(row, enc["cross_pages"][rid][0])
+            assert alloc.free == enc["cross_free_after"]
+        for rid, free_after in clears:
+            alloc.release(rid)
+            assert alloc.free == free_after
+        assert sorted(alloc.free) == list(range(run["num_cross_blocks"])) and not alloc.pages
+
+
+def test_pack_decode_step_layout():
+    host = pack_decode_step([[4, 9], [7], [1, 2, 3]], [20, 3, 40])
+    assert host.tolist() == [4, 9, 0, 7, 0, 0, 1, 2, 3, 20, 3, 40]
+
+
+def test_group_rows_by_shared_pages(engine_trace):
+    a, b, c = torch.tensor([1, 2]), torch.tensor([3]), torch.tensor([4, 5])
+    firsts, offsets = group_rows([a, a, a, b, c, c], [20, 20, 20, 7, 30, 30])
+    assert firsts == [0, 3, 4] and offsets == [0, 3, 4, 6]
+    # equal-valued but distinct tensors stay separate rows (identity marks one request)
+    firsts, offsets = group_rows([a, a.clone()], [20, 20])
+    assert offsets == [0, 1, 2]
+    # in the reference's beam steps, the staged per-row table repeats each request's pages
+    for run in engine_trace["runs"]:
+        for step in run["steps"]:
+            table, lens = step["cross_block_table"], step["cross_seq_lens"]
+            rows = {}
+            for i, rid in enumerate(step["request_ids"]):
+                rows.setdefault(rid, []).append(i)
+            for rid, idx in rows.items():
+                assert all(torch.equal(table[i], table[idx[0]]) for i in idx)
+                assert len({int(lens[i]) for i in idx}) == 1
+            # beams of a request are consecutive rows, which is what group_rows relies on
+            for idx in rows.values():
+                assert idx == list(range(idx[0], idx[0] + len(idx)))

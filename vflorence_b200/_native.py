@@ -1,0 +1,140 @@
+"""ctypes binding of ``libvflorence_b200.so`` (the C ABI declared in ``include/vflorence_b200.h``).
+
+This is the whole Python<->native boundary: plain pointers, sizes and a stream handle go in, a
+status code comes out. A missing or unloadable library raises at first use - there is no
+fallback path.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_lib", "libvflorence_b200.so")
+
+VFL_OK = 0
+VFL_ERR_INVALID_ARGUMENT = 1
+VFL_ERR_UNSUPPORTED = 2
+VFL_ERR_WORKSPACE = 3
+VFL_ERR_CUDA = 4
+
+DTYPE_F32 = 0
+DTYPE_BF16 = 1
+
+DEVERR_BLOCK_ID = 0x1
+DEVERR_SLOT = 0x2
+DEVERR_CONTEXT = 0x4
+DEVERR_TIMEOUT = 0x8
+DEVERR_QUERY = 0x10
+
+PLAN_MAGIC = 0x31504C4656
+MAX_COPY_LAYERS = 128
+
+# Every exported entry point of the C ABI, in header order.
+EXPORTS = (
+    "vfl_abi_version",
+    "vfl_status_string",
+    "vfl_last_error_message",
+    "vfl_read_device_errors",
+    "vfl_get_isa",
+    "vfl_plan_attention",
+    "vfl_reshape_and_cache",
+    "vfl_attention_with_kv_cache",
+    "vfl_copy_blocks",
+    "vfl_prepare_decode",
+    "vfl_paged_slots",
+)
+
+
+class AttentionPlan(ctypes.Structure):
+    """Mirror of ``vfl_attention_plan``."""
+
+    _fields_ = [
+        ("magic", ctypes.c_int64),
+        ("num_reqs", ctypes.c_int32),
+        ("num_heads", ctypes.c_int32),
+        ("head_dim", ctypes.c_int32),
+        ("block_size", ctypes.c_int32),
+        ("dtype", ctypes.c_int32),
+        ("causal", ctypes.c_int32),
+        ("total_q", ctypes.c_int32),
+        ("max_q_len", ctypes.c_int32),
+        ("max_seq_len", ctypes.c_int32),
+        ("heads_per_cta", ctypes.c_int32),
+        ("queries_per_cta", ctypes.c_int32),
+        ("blocks_per_split", ctypes.c_int32),
+        ("num_splits", ctypes.c_int32),
+        ("stages", ctypes.c_int32),
+        ("reserved", ctypes.c_int32),
+        ("workspace_bytes", ctypes.c_int64),
+    ]
+
+
+PLAN_BYTES = ctypes.sizeof(AttentionPlan)
+
+
+class VflError(RuntimeError):
+    """A failing C-ABI call; ``status`` is the vfl_status code."""
+
+    def __init__(self, status: int, message: str):
+        super().__init__(message)
+        self.status = status
+
+
+_lock = threading.Lock()
+_lib = None
+
+
+def _declare(L):
+    vp, i32, i64, f32, sz = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_float, ctypes.c_size_t
+    plan_p = ctypes.POINTER(AttentionPlan)
+    sig = {
+        "vfl_abi_version": (i32, []),
+        "vfl_status_string": (ctypes.c_char_p, [i32]),
+        "vfl_last_error_message": (ctypes.c_char_p, []),
+        "vfl_read_device_errors": (i32, [ctypes.POINTER(ctypes.c_uint), i32, vp]),
+        "vfl_get_isa": (i32, [i32, i32, i32, ctypes.c_char_p, i32]),
+        "vfl_plan_attention": (i32, [i32, i32, i32, i32, i32, i32, i32, vp, vp, plan_p]),
+        "vfl_reshape_and_cache": (i32, [vp, vp, vp, vp, vp, i64, i32, i32, i32, i64, i64, i64, i32, vp]),
+        "vfl_attention_with_kv_cache": (i32, [vp, vp, i64, vp, vp, i64, vp, i64, vp, vp, vp, i64, i32,
+                                              f32, vp, sz, vp]),
+        "vfl_copy_blocks": (i32, [vp, vp, i32, vp, i32, i64, i64, vp]),
+        "vfl_prepare_decode": (i32, [vp, i64, i32, vp, i32, i32, vp, vp, vp, vp]),
+        "vfl_paged_slots": (i32, [vp, i64, i32, i32, i32, i32, vp, vp]),
+    }
+    for name, (res, args) in sig.items():
+        fn = getattr(L, name)
+        fn.restype = res
+        fn.argtypes = args
+
+
+def lib():
+    """The loaded library (loaded once per process)."""
+    global _lib
+    if _lib is None:
+        with _lock:
+            if _lib is None:
+                if not os.path.exists(LIB_PATH):
+                    raise ImportError(
+                        f"vflorence_b200: CUDA library {LIB_PATH} is not built "
+                        "(run `python -m vflorence_b200.build`)")
+                L = ctypes.CDLL(LIB_PATH)
+                _declare(L)
+                if L.vfl_abi_version() != 1:
+                    raise ImportError("vflorence_b200: library ABI version mismatch")
+                _lib = L
+    return _lib
+
+
+def last_error() -> str:
+    return lib().vfl_last_error_message().decode(errors="replace")
+
+
+def check(status: int, what: str = "") -> None:
+    """Raise VflError (ValueError-like statuses included) for a non-zero status."""
+    if status != VFL_OK:
+        L = lib()
+        msg = L.vfl_last_error_message().decode(errors="replace")
+        kind = L.vfl_status_string(status).decode()
+        raise VflError(status, f"vflorence_b200{(' ' + what) if what else ''}: {kind}: {msg}")

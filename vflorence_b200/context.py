@@ -1,0 +1,37 @@
+"""Per-step metadata read by the attention custom ops (mirror of vflorence/utils/context.py:1-30).
+
+One forward at a time: the context is a module global set once per decode step, as in the
+reference. On B200 every tensor in it is a device tensor, and ``cross_staged`` entries carry
+the grouped ``query_start_loc`` of the beams (see ``attention.stage_cross``).
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+
+@dataclass(slots=True)
+class Context:
+    context_lens: torch.Tensor | None = None     # int32 [B], device
+    block_tables: torch.Tensor | None = None     # int32 [B, max_blocks], device, zero padded
+    slot_mapping: torch.Tensor | None = None     # int64 [B], device
+    query_start_loc: torch.Tensor | None = None  # int32 [B + 1], device
+    self_metadata: torch.Tensor | None = None    # host plan (paged_ops.get_scheduler_metadata)
+    isa: str | None = None
+    cross_staged: list | None = None             # per layer: (k, v, table, lens, metadata, qsl)
+
+
+_CONTEXT: Context | None = None
+
+
+def get_context() -> Context:
+    """The active step's Context (None outside a forward)."""
+    return _CONTEXT
+
+
+def set_context(**fields) -> None:
+    """Set the global Context for the current forward; no arguments resets it."""
+    global _CONTEXT
+    _CONTEXT = Context(**fields)

@@ -1,0 +1,205 @@
+// Planner and C-ABI launcher for the paged attention kernels.
+//
+// vfl_plan_attention plays the part of vllm_cpu_attn.get_scheduler_metadata
+// (vflorence/layers/attention.py:18-29, vflorence/engine/model_runner.py:308-319): from the
+// host-side lengths it fixes the CTA shape, the shared-memory pipeline depth and the split-K
+// partition, and the workspace those splits need. It is pure host arithmetic (no CUDA call),
+// sized for B200's 148 SMs.
+#include <cmath>
+
+#include "paged_attention_kernels.cuh"
+
+namespace vfl {
+namespace {
+
+constexpr int kWaves = 4;          // CTAs per SM slot the split-K partition aims for
+constexpr int kMaxSplitTokens = 256;  // upper bound of one work item (keeps the tail short)
+constexpr int kMinSplitTokens = 64;   // below this a split costs more (combine) than it saves
+constexpr int kSmemPerSM = 227 * 1024;
+
+int plan_fail(vfl_attention_plan* plan, int status) {
+  if (plan) plan->magic = 0;
+  return status;
+}
+
+}  // namespace
+}  // namespace vfl
+
+using namespace vfl;
+
+extern "C" {
+
+int vfl_plan_attention(int num_reqs, int num_heads, int num_kv_heads, int head_dim, int block_size,
+                       int dtype, int causal, const int32_t* seq_lens_host,
+                       const int32_t* query_start_loc_host, vfl_attention_plan* plan) {
+  if (plan == nullptr) return fail(VFL_ERR_INVALID_ARGUMENT, "plan is NULL");
+  if (num_reqs < 0 || num_heads <= 0)
+    return plan_fail(plan, fail(VFL_ERR_INVALID_ARGUMENT, "num_reqs %d / num_heads %d", num_reqs, num_heads));
+  if (num_kv_heads != num_heads)
+    return plan_fail(plan, fail(VFL_ERR_UNSUPPORTED,
+                                "num_kv_heads %d != num_heads %d: grouped-query attention is not built "
+                                "(the engine's BART/Florence-2 decoders are multi-head)",
+                                num_kv_heads, num_heads));
+  char isa[8];
+  int st = vfl_get_isa(dtype, block_size, head_dim, isa, sizeof(isa));
+  if (st) return plan_fail(plan, st);
+  if (num_reqs > 0 && seq_lens_host == nullptr)
+    return plan_fail(plan, fail(VFL_ERR_INVALID_ARGUMENT, "seq_lens_host is NULL"));
+
+  int64_t total_q = 0, max_q = 0, max_seq = 0;
+  if (query_start_loc_host && query_start_loc_host[0] < 0)
+    return plan_fail(plan, fail(VFL_ERR_INVALID_ARGUMENT, "query_start_loc[0] < 0"));
+  for (int r = 0; r < num_reqs; ++r) {
+    const int64_t n = seq_lens_host[r];
+    if (n < 0) return plan_fail(plan, fail(VFL_ERR_INVALID_ARGUMENT, "seq_lens[%d] = %lld < 0", r, (long long)n));
+    const int64_t ql = query_start_loc_host ? (int64_t)query_start_loc_host[r + 1] - query_start_loc_host[r] : 1;
+    if (ql < 0)
+      return plan_fail(plan, fail(VFL_ERR_INVALID_ARGUMENT, "query_start_loc decreases at %d", r));
+    max_q = ql > max_q ? ql : max_q;
+    max_seq = n > max_seq ? n : max_seq;
+  }
+  total_q = num_reqs == 0 ? 0 : (query_start_loc_host ? query_start_loc_host[num_reqs] : num_reqs);
+  if (total_q > INT32_MAX / 2)
+    return plan_fail(plan, fail(VFL_ERR_UNSUPPORTED, "too many query rows (%lld)", (long long)total_q));
+
+  const int es = static_cast<int>(dtype_size(dtype));
+  int hpc = 4;
+  while (hpc > 1 && (num_heads % hpc != 0 || 2 * hpc * 16 * head_dim * es > 32 * 1024)) hpc >>= 1;
+  const int stage_bytes = 2 * hpc * 16 * head_dim * es;
+  int stages = kMaxStageBytes / stage_bytes;
+  stages = stages < 2 ? 2 : (stages > 4 ? 4 : stages);
+  const int qpc = max_q <= 1 ? 1 : 4;
+  const int groups = num_heads / hpc;
+  const int smem = kHeaderBytes + stages * stage_bytes;
+  int ctas_per_sm = kSmemPerSM / (smem + 1024);
+  const int thread_cap = 2048 / (hpc * 32);
+  ctas_per_sm = ctas_per_sm < 1 ? 1 : (ctas_per_sm > thread_cap ? thread_cap : ctas_per_sm);
+
+  // split-K: aim for kWaves waves of CTAs over the SMs, items of at most kMaxSplitTokens tokens
+  int64_t work_tiles = 0;
+  for (int r = 0; r < num_reqs; ++r) {
+    const int64_t ql = query_start_loc_host ? (int64_t)query_start_loc_host[r + 1] - query_start_loc_host[r] : 1;
+    work_tiles += ceil_div((int64_t)seq_lens_host[r], (int64_t)16) * groups * ceil_div(ql, (int64_t)qpc);
+  }
+  const int tpb = block_size / 16;
+  const int64_t target = (int64_t)kNumSMs * ctas_per_sm * kWaves;
+  int64_t bps = ceil_div(ceil_div(work_tiles, target), (int64_t)tpb);
+  int64_t bps_cap = kMaxSplitTokens / block_size;
+  bps_cap = bps_cap < 1 ? 1 : (bps_cap > kMaxBlocksPerSplit ? kMaxBlocksPerSplit : bps_cap);
+  int64_t bps_min = kMinSplitTokens / block_size;
+  bps_min = bps_min < 1 ? 1 : (bps_min > bps_cap ? bps_cap : bps_min);
+  bps = bps < bps_min ? bps_min : (bps > bps_cap ? bps_cap : bps);
+  const int64_t max_blocks = ceil_div(max_seq, (int64_t)block_size);
+  int64_t splits = ceil_div(max_blocks, bps);
+  if (splits > 65535) {
+    bps = ceil_div(max_blocks, (int64_t)65535);
+    if (bps > kMaxBlocksPerSplit)
+      return plan_fail(plan, fail(VFL_ERR_UNSUPPORTED, "sequence of %lld tokens is too long", (long long)max_seq));
+    splits = ceil_div(max_blocks, bps);
+  }
+  splits = splits < 1 ? 1 : splits;
+  const int64_t q_chunks = ceil_div(max_q < 1 ? 1 : max_q, (int64_t)qpc);
+  if (q_chunks > 65535 || (int64_t)num_reqs * groups > INT32_MAX)
+    return plan_fail(plan, fail(VFL_ERR_UNSUPPORTED, "launch grid too large"));
+
+  int64_t ws = 0;
+  if (splits > 1) {
+    const int64_t items = total_q * num_heads * splits;
+    ws = ceil_div(items * head_dim * 4, (int64_t)256) * 256 + items * 2 * 4;
+  }
+
+  plan->magic = VFL_PLAN_MAGIC;
+  plan->num_reqs = num_reqs;
+  plan->num_heads = num_heads;
+  plan->head_dim = head_dim;
+  plan->block_size = block_size;
+  plan->dtype = dtype;
+  plan->causal = causal ? 1 : 0;
+  plan->total_q = static_cast<int32_t>(total_q);
+  plan->max_q_len = static_cast<int32_t>(max_q);
+  plan->max_seq_len = static_cast<int32_t>(max_seq);
+  plan->heads_per_cta = hpc;
+  plan->queries_per_cta = qpc;
+  plan->blocks_per_split = static_cast<int32_t>(bps);
+  plan->num_splits = static_cast<int32_t>(splits);
+  plan->stages = stages;
+  plan->reserved = 0;
+  plan->workspace_bytes = ws;
+  return VFL_OK;
+}
+
+int vfl_attention_with_kv_cache(const vfl_attention_plan* plan, const void* query,
+                                int64_t query_token_stride, const void* k_cache,
+                                const void* v_cache, int64_t num_blocks, void* output,
+                                int64_t output_token_stride, const int32_t* query_start_loc,
+                                const int32_t* seq_lens, const int32_t* block_table,
+                                int64_t table_stride, int32_t table_cols, float scale,
+                                void* workspace, size_t workspace_bytes, void* stream) {
+  if (plan == nullptr || plan->magic != VFL_PLAN_MAGIC)
+    return fail(VFL_ERR_INVALID_ARGUMENT, "attention: plan missing or not built by vfl_plan_attention");
+  const int H = plan->num_heads, D = plan->head_dim;
+  if (plan->num_reqs == 0 || plan->total_q == 0) return VFL_OK;
+  const int es = static_cast<int>(dtype_size(plan->dtype));
+  if (!query || !k_cache || !v_cache || !output || !query_start_loc || !seq_lens || !block_table)
+    return fail(VFL_ERR_INVALID_ARGUMENT, "attention: NULL pointer");
+  if (!aligned16(query) || !aligned16(output) || !aligned16(k_cache) || !aligned16(v_cache) ||
+      (query_token_stride * es) % 16 != 0 || (output_token_stride * es) % 16 != 0)
+    return fail(VFL_ERR_INVALID_ARGUMENT, "attention: query/output/caches and token strides must be 16-byte aligned");
+  if (query_token_stride < (int64_t)H * D || output_token_stride < (int64_t)H * D)
+    return fail(VFL_ERR_INVALID_ARGUMENT, "attention: token stride smaller than a token");
+  if (num_blocks <= 0 || table_cols < 0 || table_stride < table_cols)
+    return fail(VFL_ERR_INVALID_ARGUMENT, "attention: bad pool or table sizes");
+  if (plan->workspace_bytes > 0 &&
+      (workspace == nullptr || workspace_bytes < static_cast<size_t>(plan->workspace_bytes) ||
+       (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0))
+    return fail(VFL_ERR_WORKSPACE, "attention: plan needs %lld workspace bytes (256-byte aligned), got %zu",
+                (long long)plan->workspace_bytes, workspace_bytes);
+  if ((int64_t)plan->max_seq_len > (int64_t)table_cols * plan->block_size)
+    return fail(VFL_ERR_INVALID_ARGUMENT, "attention: seq_len %d exceeds the block table (%d blocks of %d)",
+                plan->max_seq_len, table_cols, plan->block_size);
+
+  AttnParams p{};
+  p.q = query;
+  p.q_stride = query_token_stride;
+  p.k_cache = k_cache;
+  p.v_cache = v_cache;
+  p.num_blocks = num_blocks;
+  p.out = output;
+  p.out_stride = output_token_stride;
+  p.qsl = query_start_loc;
+  p.seq_lens = seq_lens;
+  p.table = block_table;
+  p.table_stride = table_stride;
+  p.table_cols = table_cols;
+  p.num_reqs = plan->num_reqs;
+  p.total_q = plan->total_q;
+  p.num_heads = H;
+  p.block_size = plan->block_size;
+  p.causal = plan->causal;
+  p.heads_per_cta = plan->heads_per_cta;
+  p.blocks_per_split = plan->blocks_per_split;
+  p.num_splits = plan->num_splits;
+  p.stages = plan->stages;
+  p.max_seq_len = plan->max_seq_len;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  if (plan->num_splits > 1) {
+    const int64_t items = (int64_t)plan->total_q * H * plan->num_splits;
+    p.ws_acc = static_cast<float*>(workspace);
+    p.ws_ml = reinterpret_cast<float*>(static_cast<char*>(workspace) +
+                                       ceil_div(items * D * 4, (int64_t)256) * 256);
+  }
+  int st = device_error_word(&p.err);
+  if (st) return st;
+
+  const int hpc = plan->heads_per_cta;
+  const int qpc = plan->queries_per_cta;
+  const int q_chunks = static_cast<int>(ceil_div(plan->max_q_len < 1 ? 1 : plan->max_q_len, qpc));
+  dim3 grid(plan->num_reqs * (H / hpc), plan->num_splits, q_chunks);
+  const int threads = hpc * 32;
+  const int smem = kHeaderBytes + plan->stages * 2 * hpc * 16 * D * es;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (plan->dtype == VFL_DTYPE_F32) return launch_paged_attention_f32(p, D, qpc, grid, threads, smem, s);
+  return launch_paged_attention_bf16(p, D, qpc, grid, threads, smem, s);
+}
+
+}  // extern "C"

@@ -1,0 +1,466 @@
+// Paged decode / cross attention for B200 (sm_100a).
+//
+// Work item (one CTA): request r, a group of `heads_per_cta` adjacent heads (one warp each), one
+// split-K range of the request's KV blocks, and up to QPC query rows of the request (QPC = 1
+// for decoder self-attention; 4 for rows that share a request's pages, e.g. beams over one
+// encoder output - those rows read every K/V page once).
+//
+// Data path: the pool layout [num_blocks, H, block_size, D] makes a (block, head-group) 16-token
+// K tile one contiguous chunk, so one elected thread streams tiles into a ring of shared-memory
+// stages with cp.async.bulk (TMA bulk copies completing on mbarriers); warps consume them with
+// 16-byte shared loads. No tensor cores: one query row per head is ~1 flop per byte.
+//
+// Per 16-token tile and head, in a warp:
+//   QK: lanes = (token-in-pass `tip`, 16-element slice `sub`); q slice lives in registers,
+//       pre-scaled by scale*log2(e); partial dots are reduced over the slice lanes by xor shuffles.
+//   online softmax in the exp2 domain (running max m, running sum l).
+//   PV: lanes = (16-byte V chunk `dch`, token subgroup `tsub`); p is fetched from the QK lanes by
+//       shuffle; per-lane fp32 accumulators are reduced over `tsub` once per work item.
+// A work item whose request needs one split writes the normalised output; otherwise it writes
+// (m, l, acc) partials and the combine kernel merges them.
+#pragma once
+
+#include "common.cuh"
+
+namespace vfl {
+
+struct AttnParams {
+  const void* q;
+  int64_t q_stride;  // elements between query rows
+  const void* k_cache;
+  const void* v_cache;
+  int64_t num_blocks;
+  void* out;
+  int64_t out_stride;
+  const int32_t* qsl;       // [num_reqs + 1]
+  const int32_t* seq_lens;  // [num_reqs]
+  const int32_t* table;     // [num_reqs, table_stride]
+  int64_t table_stride;
+  int32_t table_cols;
+  int32_t num_reqs;
+  int32_t total_q;
+  int32_t num_heads;
+  int32_t block_size;
+  int32_t causal;
+  int32_t heads_per_cta;
+  int32_t blocks_per_split;
+  int32_t num_splits;  // workspace stride (max splits of any request)
+  int32_t stages;
+  int32_t max_seq_len;  // planned maximum; longer device lengths are clamped and reported
+  float scale_log2;  // softmax scale * log2(e)
+  float* ws_acc;     // [total_q, H, num_splits, D]
+  float* ws_ml;      // [total_q, H, num_splits, 2]
+  unsigned int* err;
+};
+
+constexpr int kMaxBlocksPerSplit = 64;
+constexpr int kHeaderBytes = 1024;  // block-table slice, barriers, abort flag
+constexpr int kMaxStageBytes = 64 * 1024;
+
+template <typename T, int D, int QPC>
+__global__ void __launch_bounds__(128) paged_attention_kernel(const AttnParams p) {
+  constexpr int VEC = Elem<T>::kVec;         // elements per 16-byte vector
+  constexpr int NCH = 16 / VEC;              // 16-byte chunks in a lane's 16-element QK slice
+  constexpr int TPT_RAW = D / 16;            // slice lanes that hold data
+  constexpr int TPT = next_pow2(TPT_RAW);    // lanes per token in QK
+  constexpr int TPP = 32 / TPT;              // tokens per QK pass
+  constexpr int PASSES = 16 / TPP;           // QK passes per 16-token tile
+  constexpr int DCH = D / VEC;               // 16-byte chunks per K/V row
+  constexpr int DCHP = next_pow2(DCH);
+  constexpr int TSUB = DCHP >= 32 ? 1 : 32 / DCHP;  // token subgroups in PV
+  constexpr int CPL = DCHP >= 32 ? DCHP / 32 : 1;   // V chunks per lane in PV
+  constexpr int TOKPV = 16 / TSUB;                  // tokens per lane per tile in PV
+  constexpr int TILE = 16 * D;                      // elements of one head's 16-token tile
+  static_assert(D % 16 == 0 && TPT <= 32 && TPP <= 16, "head_dim");
+  static_assert(TPP % TSUB == 0, "PV token subgroups must nest in QK passes");
+
+  extern __shared__ __align__(128) uint8_t smem[];
+  int32_t* s_table = reinterpret_cast<int32_t*>(smem);
+  uint64_t* s_bar = reinterpret_cast<uint64_t*>(smem + kMaxBlocksPerSplit * 4);
+  volatile int* s_abort = reinterpret_cast<volatile int*>(smem + kMaxBlocksPerSplit * 4 + 8 * 8);
+  T* s_kv = reinterpret_cast<T*>(smem + kHeaderBytes);
+
+  const int hpc = p.heads_per_cta;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int groups = p.num_heads / hpc;
+  const int r = blockIdx.x / groups;
+  const int h0 = (blockIdx.x - r * groups) * hpc;
+  const int h = h0 + warp;
+  const int split = blockIdx.y;
+  const int bs = p.block_size;
+  const int bps = p.blocks_per_split;
+
+  if (load_volatile(p.err) & VFL_DEVERR_TIMEOUT) return;  // an earlier CTA gave up waiting
+
+  // ---- this CTA's query rows and visible lengths (uniform across the CTA)
+  const int q_begin = __ldg(p.qsl + r);
+  const int q_end = __ldg(p.qsl + r + 1);
+  if (q_begin < 0 || q_end < q_begin || q_end > p.total_q) {
+    if (threadIdx.x == 0 && split == 0 && blockIdx.z == 0) report(p.err, VFL_DEVERR_QUERY);
+    return;
+  }
+  const int q0 = q_begin + blockIdx.z * QPC;
+  const int nq = min(QPC, q_end - q0);
+  if (nq <= 0) return;
+  int L = __ldg(p.seq_lens + r);
+  const int cap = min(p.table_cols * bs, p.max_seq_len);
+  if (L > cap) {
+    if (threadIdx.x == 0 && split == 0 && blockIdx.z == 0) report(p.err, VFL_DEVERR_CONTEXT);
+    L = cap;
+  }
+  L = max(L, 0);
+  const int nblk = ceil_div(L, bs);
+  const int n_splits = ceil_div(nblk, bps);
+  if (split >= max(n_splits, 1)) return;
+
+  int vis[QPC];
+  int vis_max = 0, vis_min = 0x7fffffff;
+#pragma unroll
+  for (int j = 0; j < QPC; ++j) {
+    const int row = q0 + j;
+    int v = 0;
+    if (j < nq) v = p.causal ? L - (q_end - 1 - row) : L;
+    v = max(v, 0);
+    vis[j] = v;
+    vis_max = max(vis_max, v);
+    if (j < nq) vis_min = min(vis_min, v);
+  }
+  const int tpb = bs / 16;  // 16-token tiles per block
+  const int blk_begin = split * bps;
+  const int tile_begin = blk_begin * tpb;
+  const int tile_end = min((blk_begin + bps) * tpb, ceil_div(vis_max, 16));
+  const int ntiles = max(0, tile_end - tile_begin);
+  const int stages = p.stages;
+  const int stage_elems = 2 * hpc * TILE;
+
+  // ---- block-table slice (validated) and barriers
+  const int nb = min(bps, nblk - blk_begin);
+  for (int i = threadIdx.x; i < nb; i += blockDim.x) {
+    int b = __ldg(p.table + r * p.table_stride + blk_begin + i);
+    if (b < 0 || b >= p.num_blocks) {
+      report(p.err, VFL_DEVERR_BLOCK_ID);
+      b = 0;  // read a valid block instead; the error word flags the result as garbage
+    }
+    s_table[i] = b;
+  }
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; ++s) mbar_init(&s_bar[s], 1);
+    *s_abort = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  const uint32_t head_tile_bytes = TILE * sizeof(T);
+  int issued = 0;            // tiles whose copies thread 0 has started
+  auto issue = [&](int i) {  // thread 0 only: start the copy of tile i into stage i % stages
+    issued = i + 1;
+    const int tile = tile_begin + i;
+    const int blk = tile / tpb;
+    const int sub_tile = tile - blk * tpb;
+    const int64_t phys = s_table[blk - blk_begin];
+    const int s = i % stages;
+    T* ks = s_kv + (size_t)s * stage_elems;
+    T* vs = ks + hpc * TILE;
+    mbar_arrive_expect_tx(&s_bar[s], 2u * hpc * head_tile_bytes);
+    const int64_t base = ((phys * p.num_heads + h0) * bs + sub_tile * 16) * D;
+    if (tpb == 1) {  // the head group's tiles are adjacent: one copy each for K and V
+      bulk_copy_g2s(ks, static_cast<const T*>(p.k_cache) + base, hpc * head_tile_bytes, &s_bar[s]);
+      bulk_copy_g2s(vs, static_cast<const T*>(p.v_cache) + base, hpc * head_tile_bytes, &s_bar[s]);
+    } else {
+      for (int w = 0; w < hpc; ++w) {
+        const int64_t off = base + (int64_t)w * bs * D;
+        bulk_copy_g2s(ks + w * TILE, static_cast<const T*>(p.k_cache) + off, head_tile_bytes, &s_bar[s]);
+        bulk_copy_g2s(vs + w * TILE, static_cast<const T*>(p.v_cache) + off, head_tile_bytes, &s_bar[s]);
+      }
+    }
+  };
+  if (threadIdx.x == 0) {
+    const int pre = min(stages, ntiles);
+    for (int i = 0; i < pre; ++i) issue(i);
+  }
+
+  // ---- query slice in registers: chunk c of the registers pairs with shared chunk (c+rot)%NCH
+  const int sub = lane % TPT;
+  const int tip = lane / TPT;
+  const bool qk_on = sub < TPT_RAW;
+  const int rot = (((lane & 7) * NCH) >> 3) % NCH;  // spreads a quarter-warp over all banks
+  float qr[QPC][16];
+#pragma unroll
+  for (int j = 0; j < QPC; ++j) {
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      float f[VEC];
+      if (j < nq && qk_on) {
+        const int cc = (c + rot) % NCH;
+        const T* src = static_cast<const T*>(p.q) + (int64_t)(q0 + j) * p.q_stride + h * D +
+                       sub * 16 + cc * VEC;
+        unpack16(ldg_nc_v4(src), f, T());
+      } else {
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) f[e] = 0.f;
+      }
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) qr[j][c * VEC + e] = f[e] * p.scale_log2;
+    }
+  }
+  int koff[NCH];
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) koff[c] = sub * 16 + ((c + rot) % NCH) * VEC;
+
+  const int dch = DCHP >= 32 ? lane : lane % DCHP;
+  const int tsub = DCHP >= 32 ? 0 : lane / DCHP;
+  bool pv_on[CPL];
+#pragma unroll
+  for (int c = 0; c < CPL; ++c) pv_on[c] = dch + 32 * c < DCH;
+
+  float m[QPC], l[QPC], acc[QPC][CPL * VEC];
+#pragma unroll
+  for (int j = 0; j < QPC; ++j) {
+    m[j] = -INFINITY;
+    l[j] = 0.f;
+#pragma unroll
+    for (int e = 0; e < CPL * VEC; ++e) acc[j][e] = 0.f;
+  }
+
+  // ---- main loop over 16-token tiles
+  bool aborted = false;
+#pragma unroll 1
+  for (int i = 0; i < ntiles; ++i) {
+    const int s = i % stages;
+    if (!mbar_wait_bounded(&s_bar[s], (i / stages) & 1)) {
+      report(p.err, VFL_DEVERR_TIMEOUT);
+      *s_abort = 1;
+    }
+    const T* kt = s_kv + (size_t)s * stage_elems + warp * TILE;
+    const T* vt = kt + hpc * TILE;
+    const int tok0 = (tile_begin + i) * 16;
+    const bool full = tok0 + 16 <= vis_min;
+
+    // QK
+    float sc[QPC][PASSES];
+#pragma unroll
+    for (int ps = 0; ps < PASSES; ++ps) {
+      const int t = ps * TPP + tip;
+      float kf[16];
+#pragma unroll
+      for (int c = 0; c < NCH; ++c) {
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (qk_on) v = *reinterpret_cast<const uint4*>(kt + t * D + koff[c]);
+        unpack16(v, kf + c * VEC, T());
+      }
+#pragma unroll
+      for (int j = 0; j < QPC; ++j) {
+        float dot = 0.f;
+#pragma unroll
+        for (int e = 0; e < 16; ++e) dot = fmaf(qr[j][e], kf[e], dot);
+#pragma unroll
+        for (int o = 1; o < TPT; o <<= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+        sc[j][ps] = (full || tok0 + t < vis[j]) ? dot : -INFINITY;
+      }
+    }
+    // online softmax (exp2 domain)
+#pragma unroll
+    for (int j = 0; j < QPC; ++j) {
+      float mx = sc[j][0];
+#pragma unroll
+      for (int ps = 1; ps < PASSES; ++ps) mx = fmaxf(mx, sc[j][ps]);
+#pragma unroll
+      for (int o = TPT; o < 32; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      const float mnew = fmaxf(m[j], mx);
+      const bool none = mnew == -INFINITY;  // nothing visible yet for this row
+      const float alpha = none ? 1.f : exp2f(m[j] - mnew);
+#pragma unroll
+      for (int ps = 0; ps < PASSES; ++ps) sc[j][ps] = none ? 0.f : exp2f(sc[j][ps] - mnew);
+      m[j] = mnew;
+      l[j] *= alpha;
+#pragma unroll
+      for (int e = 0; e < CPL * VEC; ++e) acc[j][e] *= alpha;
+    }
+    // PV
+#pragma unroll
+    for (int k = 0; k < TOKPV; ++k) {
+      const int ps = (TSUB * k) / TPP;  // compile-time: tsub < TSUB and TSUB divides TPP
+      const int t = tsub + TSUB * k;
+      const int src = (t - ps * TPP) * TPT;
+      float vf[CPL * VEC];
+#pragma unroll
+      for (int c = 0; c < CPL; ++c) {
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (pv_on[c]) v = *reinterpret_cast<const uint4*>(vt + t * D + (dch + 32 * c) * VEC);
+        unpack16(v, vf + c * VEC, T());
+      }
+#pragma unroll
+      for (int j = 0; j < QPC; ++j) {
+        const float pj = __shfl_sync(0xffffffffu, sc[j][ps], src);
+        if (full || tok0 + t < vis[j]) {  // masked tokens may hold anything, even NaN
+          l[j] += pj;
+#pragma unroll
+          for (int e = 0; e < CPL * VEC; ++e) acc[j][e] = fmaf(pj, vf[e], acc[j][e]);
+        }
+      }
+    }
+    __syncthreads();  // every warp is done with stage s
+    if (*s_abort) {
+      aborted = true;
+      break;
+    }
+    if (threadIdx.x == 0 && i + stages < ntiles) {
+      fence_proxy_async_smem();
+      issue(i + stages);
+    }
+  }
+  if (aborted) {
+    // Let copies still in flight land (bounded) before the CTA's shared memory is released.
+    if (threadIdx.x == 0)
+      for (int t = max(0, issued - stages); t < issued; ++t)
+        mbar_wait_bounded(&s_bar[t % stages], (t / stages) & 1);
+    return;
+  }
+
+  // ---- reduce the PV accumulators over token subgroups
+#pragma unroll
+  for (int o = DCHP; o < 32; o <<= 1) {
+#pragma unroll
+    for (int j = 0; j < QPC; ++j) {
+      l[j] += __shfl_xor_sync(0xffffffffu, l[j], o);
+#pragma unroll
+      for (int e = 0; e < CPL * VEC; ++e) acc[j][e] += __shfl_xor_sync(0xffffffffu, acc[j][e], o);
+    }
+  }
+  if (tsub != 0) return;
+  const int S = p.num_splits;
+#pragma unroll
+  for (int j = 0; j < QPC; ++j) {
+    if (j >= nq) break;
+    const int row = q0 + j;
+    if (n_splits <= 1) {
+      const float inv = l[j] > 0.f ? 1.f / l[j] : 0.f;
+#pragma unroll
+      for (int c = 0; c < CPL; ++c) {
+        if (!pv_on[c]) continue;
+        float f[VEC];
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) f[e] = acc[j][c * VEC + e] * inv;
+        T* dst = static_cast<T*>(p.out) + (int64_t)row * p.out_stride + h * D + (dch + 32 * c) * VEC;
+        *reinterpret_cast<uint4*>(dst) = pack16(f, T());
+      }
+    } else {
+      const int64_t item = ((int64_t)row * p.num_heads + h) * S + split;
+#pragma unroll
+      for (int c = 0; c < CPL; ++c) {
+        if (!pv_on[c]) continue;
+        float4* dst = reinterpret_cast<float4*>(p.ws_acc + item * D + (dch + 32 * c) * VEC);
+#pragma unroll
+        for (int e = 0; e < VEC; e += 4)
+          dst[e / 4] = make_float4(acc[j][c * VEC + e], acc[j][c * VEC + e + 1],
+                                   acc[j][c * VEC + e + 2], acc[j][c * VEC + e + 3]);
+      }
+      if (lane == 0) *reinterpret_cast<float2*>(p.ws_ml + item * 2) = make_float2(m[j], l[j]);
+    }
+  }
+}
+
+// One warp per (query row, head) of a request that was split: merges the partials.
+template <typename T, int D>
+__global__ void __launch_bounds__(128) paged_attention_combine_kernel(const AttnParams p) {
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int64_t gw = (int64_t)blockIdx.x * (blockDim.x >> 5) + warp;
+  if (gw >= (int64_t)p.total_q * p.num_heads) return;
+  const int row = static_cast<int>(gw / p.num_heads);
+  const int h = static_cast<int>(gw - (int64_t)row * p.num_heads);
+  // request owning this row: last r with qsl[r] <= row
+  int lo = 0, hi = p.num_reqs - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (__ldg(p.qsl + mid) <= row) lo = mid; else hi = mid - 1;
+  }
+  const int r = lo;
+  if (row < __ldg(p.qsl + r) || row >= __ldg(p.qsl + r + 1)) return;  // row of no request
+  int L = min(__ldg(p.seq_lens + r), min(p.table_cols * p.block_size, p.max_seq_len));
+  L = max(L, 0);
+  const int n_splits = ceil_div(ceil_div(L, p.block_size), p.blocks_per_split);
+  if (n_splits <= 1) return;  // written directly by the main kernel
+  const int S = p.num_splits;
+  const int64_t item0 = ((int64_t)row * p.num_heads + h) * S;
+  const float* ml = p.ws_ml + item0 * 2;
+  float M = -INFINITY;
+  for (int s = lane; s < n_splits; s += 32) M = fmaxf(M, ml[2 * s]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+  float Lsum = 0.f;
+  if (M != -INFINITY)
+    for (int s = lane; s < n_splits; s += 32) Lsum += exp2f(ml[2 * s] - M) * ml[2 * s + 1];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) Lsum += __shfl_xor_sync(0xffffffffu, Lsum, o);
+  const float inv = Lsum > 0.f ? 1.f / Lsum : 0.f;
+  T* out = static_cast<T*>(p.out) + (int64_t)row * p.out_stride + h * D;
+  const float* acc = p.ws_acc + item0 * D;
+  for (int d = lane; d < D; d += 32) {
+    float a = 0.f;
+    if (M != -INFINITY)
+      for (int s = 0; s < n_splits; ++s) {
+        const float w = exp2f(ml[2 * s] - M);
+        a = fmaf(w, acc[(int64_t)s * D + d], a);
+      }
+    const float v = a * inv;
+    if constexpr (sizeof(T) == 4) {
+      out[d] = v;
+    } else {
+      out[d] = __float2bfloat16_rn(v);
+    }
+  }
+}
+
+// Launches the main kernel (and the combine when the plan splits); defined per dtype.
+int launch_paged_attention_f32(const AttnParams& p, int head_dim, int qpc, dim3 grid, int threads,
+                               int smem_bytes, cudaStream_t stream);
+int launch_paged_attention_bf16(const AttnParams& p, int head_dim, int qpc, dim3 grid, int threads,
+                                int smem_bytes, cudaStream_t stream);
+
+template <typename T, int D, int QPC>
+int launch_one(const AttnParams& p, dim3 grid, int threads, int smem_bytes, cudaStream_t stream) {
+  static int smem_done[kMaxDevices];
+  auto kernel = paged_attention_kernel<T, D, QPC>;
+  int st = ensure_smem_attribute(reinterpret_cast<const void*>(kernel), kHeaderBytes + kMaxStageBytes,
+                                 smem_done);
+  if (st) return st;
+  kernel<<<grid, threads, smem_bytes, stream>>>(p);
+  st = cuda_status(cudaGetLastError(), "paged_attention launch");
+  if (st) return st;
+  if (p.num_splits > 1) {
+    const int64_t warps = (int64_t)p.total_q * p.num_heads;
+    const int blocks = static_cast<int>(ceil_div(warps, (int64_t)4));
+    paged_attention_combine_kernel<T, D><<<blocks, 128, 0, stream>>>(p);
+    st = cuda_status(cudaGetLastError(), "paged_attention combine launch");
+  }
+  return st;
+}
+
+template <typename T, int D>
+int launch_qpc(const AttnParams& p, int qpc, dim3 grid, int threads, int smem_bytes, cudaStream_t stream) {
+  if (qpc == 1) return launch_one<T, D, 1>(p, grid, threads, smem_bytes, stream);
+  return launch_one<T, D, 4>(p, grid, threads, smem_bytes, stream);
+}
+
+template <typename T>
+int launch_dtype(const AttnParams& p, int head_dim, int qpc, dim3 grid, int threads, int smem_bytes,
+                 cudaStream_t stream) {
+  switch (head_dim) {
+    case 32: return launch_qpc<T, 32>(p, qpc, grid, threads, smem_bytes, stream);
+    case 48: return launch_qpc<T, 48>(p, qpc, grid, threads, smem_bytes, stream);
+    case 64: return launch_qpc<T, 64>(p, qpc, grid, threads, smem_bytes, stream);
+    case 80: return launch_qpc<T, 80>(p, qpc, grid, threads, smem_bytes, stream);
+    case 96: return launch_qpc<T, 96>(p, qpc, grid, threads, smem_bytes, stream);
+    case 112: return launch_qpc<T, 112>(p, qpc, grid, threads, smem_bytes, stream);
+    case 128: return launch_qpc<T, 128>(p, qpc, grid, threads, smem_bytes, stream);
+    case 160: return launch_qpc<T, 160>(p, qpc, grid, threads, smem_bytes, stream);
+    case 192: return launch_qpc<T, 192>(p, qpc, grid, threads, smem_bytes, stream);
+    case 224: return launch_qpc<T, 224>(p, qpc, grid, threads, smem_bytes, stream);
+    case 256: return launch_qpc<T, 256>(p, qpc, grid, threads, smem_bytes, stream);
+    default: return fail(VFL_ERR_UNSUPPORTED, "head_dim %d not built", head_dim);
+  }
+}
+
+}  // namespace vfl

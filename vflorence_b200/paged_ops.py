@@ -1,0 +1,295 @@
+"""The four ``vllm_cpu_attn`` functions the vflorence engine calls, on B200, plus the two ops
+that sit beside them (copy-on-write block copies and the per-step metadata build).
+
+Drop-in use: ``import vflorence_b200.paged_ops as vllm_cpu_attn``. Signatures and argument
+meaning follow the call sites in vflorence (paths inside that project):
+
+    get_isa                   vflorence/engine/model_runner.py:38
+    get_scheduler_metadata    vflorence/layers/attention.py:18-29, model_runner.py:308-319
+    reshape_and_cache         vflorence/layers/attention.py:55-57, model_runner.py:252-259
+    attention_with_kv_cache   vflorence/layers/attention.py:61-72, :98-109
+    copy_blocks               replaces ModelRunner._copy_blocks, model_runner.py:162-167
+    prepare_decode            replaces the list building of ModelRunner._prepare, :290-306
+    paged_slots               replaces the encoder slot arithmetic of _encode, :240-242
+
+Differences a caller sees:
+  * tensors live on one CUDA device (caches, queries, outputs, block tables, lengths); a CPU
+    tensor is an error, never a silent copy. ``get_scheduler_metadata`` reads its lengths on the
+    host - pass host tensors (the engine has them), or it copies (and synchronises) once.
+  * the metadata is a host int64 tensor holding a ``vfl_attention_plan``; pass the same device
+    lengths to ``attention_with_kv_cache`` as were planned (longer ones are clamped and flagged).
+  * several query rows of one request (``query_start_loc``) attend to the same pages, so beams
+    sharing an encoder output can be one request: its pages are read once for all of them.
+Everything is enqueued on the current CUDA stream; nothing synchronises.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _native as N
+
+HEAD_DIMS = frozenset({32, 48, 64, 80, 96, 112, 128, 160, 192, 224, 256})
+_DTYPES = {torch.float32: N.DTYPE_F32, torch.bfloat16: N.DTYPE_BF16}
+
+
+def _dtype_code(dtype: torch.dtype) -> int:
+    try:
+        return _DTYPES[dtype]
+    except KeyError:
+        raise ValueError(f"vflorence_b200: dtype {dtype} is not supported (float32, bfloat16)") from None
+
+
+def _stream(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _require_cuda(name: str, t: torch.Tensor, device: torch.device | None = None) -> None:
+    if not t.is_cuda:
+        raise ValueError(f"vflorence_b200: {name} must be a CUDA tensor (got {t.device})")
+    if device is not None and t.device != device:
+        raise ValueError(f"vflorence_b200: {name} is on {t.device}, expected {device}")
+
+
+def _require_dense_rows(name: str, t: torch.Tensor) -> None:
+    """[tokens, heads, head_dim] with dense heads and elements (any token stride)."""
+    if t.dim() != 3 or t.stride(2) != 1 or t.stride(1) != t.shape[2]:
+        raise ValueError(f"vflorence_b200: {name} must be [tokens, heads, head_dim] with dense "
+                         f"heads (got shape {tuple(t.shape)}, strides {t.stride()})")
+
+
+def _host_int32(t: torch.Tensor | None) -> torch.Tensor | None:
+    if t is None:
+        return None
+    if t.device.type != "cpu":
+        t = t.cpu()
+    return t.to(torch.int32).contiguous()
+
+
+# ------------------------------------------------------------------------------------- get_isa
+
+def get_isa(dtype: torch.dtype, block_size: int, head_dim: int) -> str:
+    """Kernel family tag for (dtype, block_size, head_dim): ``"sm100"``.
+
+    Raises ValueError for a configuration the B200 kernels do not cover (the reference raises
+    ValueError for an unsupported head_dim, vflorence/engine/model_runner.py:33-37).
+    """
+    buf = ctypes.create_string_buffer(16)
+    st = N.lib().vfl_get_isa(_dtype_code(dtype), int(block_size), int(head_dim), buf, 16)
+    if st != N.VFL_OK:
+        raise ValueError(f"vflorence_b200: {N.last_error()}")
+    return buf.value.decode()
+
+
+# ------------------------------------------------------------------------ scheduler metadata
+
+def get_scheduler_metadata(num_reqs: int, num_heads: int, num_kv_heads: int, head_dim: int,
+                           seq_lens: torch.Tensor, dtype: torch.dtype,
+                           query_start_loc: torch.Tensor | None, causal: bool, isa: str,
+                           block_size: int) -> torch.Tensor:
+    """Launch plan for ``attention_with_kv_cache``: a host int64 tensor holding the plan struct."""
+    lens = _host_int32(seq_lens)
+    if lens.numel() != num_reqs:
+        raise ValueError(f"vflorence_b200: seq_lens has {lens.numel()} entries for {num_reqs} requests")
+    qsl = _host_int32(query_start_loc)
+    if qsl is not None and qsl.numel() != num_reqs + 1:
+        raise ValueError("vflorence_b200: query_start_loc must have num_reqs + 1 entries")
+    meta = torch.zeros(N.PLAN_BYTES // 8, dtype=torch.int64)
+    plan = N.AttentionPlan.from_address(meta.data_ptr())
+    st = N.lib().vfl_plan_attention(int(num_reqs), int(num_heads), int(num_kv_heads), int(head_dim),
+                                    int(block_size), _dtype_code(dtype), int(bool(causal)),
+                                    lens.data_ptr() if num_reqs else None,
+                                    qsl.data_ptr() if qsl is not None else None, ctypes.byref(plan))
+    N.check(st, "get_scheduler_metadata")
+    return meta
+
+
+def plan_of(metadata: torch.Tensor) -> N.AttentionPlan:
+    """View the plan struct stored in a metadata tensor (no copy)."""
+    if (metadata.device.type != "cpu" or metadata.dtype != torch.int64 or not metadata.is_contiguous()
+            or metadata.numel() * 8 < N.PLAN_BYTES):
+        raise ValueError("vflorence_b200: scheduler_metadata must come from get_scheduler_metadata")
+    plan = N.AttentionPlan.from_address(metadata.data_ptr())
+    if plan.magic != N.PLAN_MAGIC:
+        raise ValueError("vflorence_b200: scheduler_metadata must come from get_scheduler_metadata")
+    return plan
+
+
+# ------------------------------------------------------------------------- reshape_and_cache
+
+def reshape_and_cache(key: torch.Tensor, value: torch.Tensor, k_cache: torch.Tensor,
+                      v_cache: torch.Tensor, slot_mapping: torch.Tensor, isa: str | None = None) -> None:
+    """``k_cache[s // bs, h, s % bs] = key[t, h]`` (same for value) for ``s = slot_mapping[t] >= 0``."""
+    dev = k_cache.device
+    for name, t in (("key", key), ("value", value), ("k_cache", k_cache), ("v_cache", v_cache),
+                    ("slot_mapping", slot_mapping)):
+        _require_cuda(name, t, dev)
+    _require_dense_rows("key", key)
+    _require_dense_rows("value", value)
+    if key.shape != value.shape or key.dtype != k_cache.dtype or value.dtype != v_cache.dtype:
+        raise ValueError("vflorence_b200: key/value shapes or dtypes do not match the caches")
+    if k_cache.shape != v_cache.shape or k_cache.dim() != 4 or not (k_cache.is_contiguous() and v_cache.is_contiguous()):
+        raise ValueError("vflorence_b200: caches must be contiguous [num_blocks, heads, block_size, head_dim]")
+    n, h, bs, d = k_cache.shape
+    if key.shape[1:] != (h, d):
+        raise ValueError(f"vflorence_b200: key rows {tuple(key.shape[1:])} do not match the cache ({h}, {d})")
+    if slot_mapping.dtype != torch.int64 or slot_mapping.dim() != 1 or slot_mapping.numel() != key.shape[0]:
+        raise ValueError("vflorence_b200: slot_mapping must be int64 [num_tokens]")
+    slots = slot_mapping if slot_mapping.is_contiguous() else slot_mapping.contiguous()
+    st = N.lib().vfl_reshape_and_cache(key.data_ptr(), value.data_ptr(), k_cache.data_ptr(),
+                                       v_cache.data_ptr(), slots.data_ptr(), key.shape[0], h, d, bs, n,
+                                       key.stride(0), value.stride(0), _dtype_code(k_cache.dtype),
+                                       _stream(dev))
+    N.check(st, "reshape_and_cache")
+
+
+# ------------------------------------------------------------------- attention_with_kv_cache
+
+def attention_with_kv_cache(query: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                            output: torch.Tensor, query_start_loc: torch.Tensor,
+                            seq_lens: torch.Tensor, scale: float, causal: bool,
+                            block_table: torch.Tensor, scheduler_metadata: torch.Tensor) -> None:
+    """``output = softmax(scale * q K^T) V`` per request over its paged tokens (writes ``output``)."""
+    plan = plan_of(scheduler_metadata)
+    dev = k_cache.device
+    for name, t in (("query", query), ("k_cache", k_cache), ("v_cache", v_cache), ("output", output),
+                    ("query_start_loc", query_start_loc), ("seq_lens", seq_lens),
+                    ("block_table", block_table)):
+        _require_cuda(name, t, dev)
+    _require_dense_rows("query", query)
+    _require_dense_rows("output", output)
+    n, h, bs, d = k_cache.shape
+    if (plan.num_heads, plan.head_dim, plan.block_size, plan.dtype) != (h, d, bs, _dtype_code(k_cache.dtype)):
+        raise ValueError("vflorence_b200: scheduler_metadata was planned for another cache shape or dtype")
+    if bool(plan.causal) != bool(causal):
+        raise ValueError("vflorence_b200: scheduler_metadata was planned with another causal flag")
+    if query.dtype != k_cache.dtype or output.dtype != k_cache.dtype or v_cache.shape != k_cache.shape:
+        raise ValueError("vflorence_b200: query/output/cache dtypes or cache shapes differ")
+    if not (k_cache.is_contiguous() and v_cache.is_contiguous()):
+        raise ValueError("vflorence_b200: caches must be contiguous")
+    if query.shape != output.shape or query.shape[1:] != (h, d) or query.shape[0] < plan.total_q:
+        raise ValueError("vflorence_b200: query/output must be [num_tokens >= planned rows, heads, head_dim]")
+    if (query_start_loc.dtype != torch.int32 or seq_lens.dtype != torch.int32 or block_table.dtype != torch.int32
+            or block_table.dim() != 2 or block_table.stride(1) != 1):
+        raise ValueError("vflorence_b200: query_start_loc, seq_lens and block_table must be int32 "
+                         "(block_table [num_reqs, cols] with unit column stride)")
+    if seq_lens.numel() != plan.num_reqs or query_start_loc.numel() != plan.num_reqs + 1 \
+            or block_table.shape[0] < plan.num_reqs:
+        raise ValueError("vflorence_b200: metadata planned for a different number of requests")
+    ws = None
+    if plan.workspace_bytes > 0:
+        ws = torch.empty(plan.workspace_bytes, dtype=torch.uint8, device=dev)
+    st = N.lib().vfl_attention_with_kv_cache(
+        ctypes.byref(plan), query.data_ptr(), query.stride(0), k_cache.data_ptr(), v_cache.data_ptr(), n,
+        output.data_ptr(), output.stride(0), query_start_loc.data_ptr(), seq_lens.data_ptr(),
+        block_table.data_ptr(), block_table.stride(0), block_table.shape[1], float(scale),
+        ws.data_ptr() if ws is not None else None, plan.workspace_bytes if ws is not None else 0,
+        _stream(dev))
+    N.check(st, "attention_with_kv_cache")
+
+
+# ------------------------------------------------------------------------------- copy_blocks
+
+def check_copy_pairs(pairs, num_blocks: int) -> list[tuple[int, int]]:
+    """Validate copy-on-write pairs on the host: in range, unique destinations, and no block
+    both read and written (the gather-then-scatter meaning of index_select + index_copy_)."""
+    pairs = [(int(s), int(d)) for s, d in pairs]
+    srcs = {s for s, _ in pairs}
+    dsts = [d for _, d in pairs]
+    for s, d in pairs:
+        if not (0 <= s < num_blocks and 0 <= d < num_blocks):
+            raise ValueError(f"vflorence_b200: copy pair ({s}, {d}) outside [0, {num_blocks})")
+    if len(set(dsts)) != len(dsts):
+        raise ValueError("vflorence_b200: copy_blocks destinations must be unique")
+    if srcs.intersection(dsts):
+        raise ValueError("vflorence_b200: copy_blocks sources and destinations must be disjoint")
+    return pairs
+
+
+def copy_blocks(k_caches, v_caches, block_pairs) -> None:
+    """For every layer: ``k_caches[l][dst] = k_caches[l][src]`` (and V) for each (src, dst).
+
+    ``block_pairs`` is a list of (src, dst) (validated on the host and uploaded) or a device int64
+    tensor [P, 2] (validated by the kernel only: out-of-range pairs are skipped and flagged).
+    One launch covers all layers and pairs.
+    """
+    k_caches, v_caches = list(k_caches), list(v_caches)
+    if len(k_caches) != len(v_caches) or not k_caches:
+        raise ValueError("vflorence_b200: copy_blocks needs matching, non-empty K and V cache lists")
+    c0 = k_caches[0]
+    dev = c0.device
+    for c in k_caches + v_caches:
+        _require_cuda("cache", c, dev)
+        if c.shape != c0.shape or c.dtype != c0.dtype or not c.is_contiguous():
+            raise ValueError("vflorence_b200: copy_blocks caches must share one contiguous shape and dtype")
+    if isinstance(block_pairs, torch.Tensor):
+        _require_cuda("block_pairs", block_pairs, dev)
+        pairs_t = block_pairs.to(torch.int64).reshape(-1, 2).contiguous()
+    else:
+        pairs = check_copy_pairs(block_pairs, c0.shape[0])
+        if not pairs:
+            return
+        pairs_t = torch.tensor(pairs, dtype=torch.int64).pin_memory().to(dev, non_blocking=True)
+    num_pairs = pairs_t.shape[0]
+    if num_pairs == 0:
+        return
+    L = len(k_caches)
+    block_bytes = c0[0].numel() * c0.element_size()
+    lib = N.lib()
+    for start in range(0, L, N.MAX_COPY_LAYERS):
+        ks, vs = k_caches[start:start + N.MAX_COPY_LAYERS], v_caches[start:start + N.MAX_COPY_LAYERS]
+        kp = (ctypes.c_void_p * len(ks))(*[c.data_ptr() for c in ks])
+        vp = (ctypes.c_void_p * len(vs))(*[c.data_ptr() for c in vs])
+        st = lib.vfl_copy_blocks(kp, vp, len(ks), pairs_t.data_ptr(), num_pairs, c0.shape[0], block_bytes,
+                                 _stream(dev))
+        N.check(st, "copy_blocks")
+
+
+# ---------------------------------------------------------------------------- step metadata
+
+def prepare_decode(block_table: torch.Tensor, positions: torch.Tensor, block_size: int,
+                   slot_mapping: torch.Tensor, context_lens: torch.Tensor,
+                   query_start_loc: torch.Tensor) -> None:
+    """Fill one decode step's slot mapping (int64), context lengths and query_start_loc (int32)
+    from the padded block table and each sequence's position (= cached tokens)."""
+    dev = block_table.device
+    for name, t in (("block_table", block_table), ("positions", positions), ("slot_mapping", slot_mapping),
+                    ("context_lens", context_lens), ("query_start_loc", query_start_loc)):
+        _require_cuda(name, t, dev)
+    b = positions.numel()
+    if (block_table.dtype != torch.int32 or positions.dtype != torch.int32 or block_table.dim() != 2
+            or block_table.stride(1) != 1 or block_table.shape[0] < b or not positions.is_contiguous()):
+        raise ValueError("vflorence_b200: prepare_decode wants int32 block_table [B, M] and positions [B]")
+    if (slot_mapping.dtype != torch.int64 or context_lens.dtype != torch.int32
+            or query_start_loc.dtype != torch.int32 or slot_mapping.numel() < b
+            or context_lens.numel() < b or query_start_loc.numel() < b + 1):
+        raise ValueError("vflorence_b200: prepare_decode output dtypes or sizes are wrong")
+    st = N.lib().vfl_prepare_decode(block_table.data_ptr(), block_table.stride(0), block_table.shape[1],
+                                    positions.data_ptr(), b, int(block_size), slot_mapping.data_ptr(),
+                                    context_lens.data_ptr(), query_start_loc.data_ptr(), _stream(dev))
+    N.check(st, "prepare_decode")
+
+
+def paged_slots(pages: torch.Tensor, seq_len: int, block_size: int) -> torch.Tensor:
+    """Slots of ``seq_len`` tokens for each row of ``pages`` [G, M] (int64 [G * seq_len])."""
+    _require_cuda("pages", pages)
+    if pages.dtype != torch.int32 or pages.dim() != 2 or pages.stride(1) != 1:
+        raise ValueError("vflorence_b200: pages must be int32 [G, M] with unit column stride")
+    out = torch.empty(pages.shape[0] * int(seq_len), dtype=torch.int64, device=pages.device)
+    st = N.lib().vfl_paged_slots(pages.data_ptr(), pages.stride(0), pages.shape[1], pages.shape[0],
+                                 int(seq_len), int(block_size), out.data_ptr(), _stream(pages.device))
+    N.check(st, "paged_slots")
+    return out
+
+
+def read_device_errors(device: torch.device | int | None = None, clear: bool = True) -> int:
+    """VFL_DEVERR_* bits the kernels raised on ``device`` since the last clear (synchronises)."""
+    dev = torch.device("cuda", torch.cuda.current_device() if device is None else
+                       (device if isinstance(device, int) else device.index or 0))
+    bits = ctypes.c_uint(0)
+    with torch.cuda.device(dev):
+        st = N.lib().vfl_read_device_errors(ctypes.byref(bits), int(bool(clear)), _stream(dev))
+    N.check(st, "read_device_errors")
+    return bits.value
