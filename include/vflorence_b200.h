@@ -134,6 +134,24 @@ int vfl_attention_with_kv_cache(const vfl_attention_plan* plan, const void* quer
                                 int64_t table_stride, int32_t table_cols, float scale,
                                 void* workspace, size_t workspace_bytes, void* stream);
 
+/* No counterpart in the reference (vllm_cpu_attn allocates on the host heap as it likes).
+ * The same attention as vfl_attention_with_kv_cache, for callers that cannot allocate device
+ * memory - a C/C++ or FFI host without a device allocator of its own, where every scratch
+ * buffer would be a device-synchronising cudaMalloc, or a process whose device memory a
+ * framework's pool already holds. Takes no workspace: the split-K scratch is a fixed array of
+ * VFL_STATIC_WORKSPACE_BYTES inside the library, which every device that loads the library
+ * keeps until exit. Plans needing more scratch fail with VFL_ERR_WORKSPACE. All calls on a
+ * device share that array: calls that can overlap on the device race, so order them. The
+ * first call on a device looks up the array's address; make it before any stream capture. */
+#define VFL_STATIC_WORKSPACE_BYTES (64u * 1024u * 1024u)
+int vfl_attention_with_kv_cache_no_alloc(const vfl_attention_plan* plan, const void* query,
+                                         int64_t query_token_stride, const void* k_cache,
+                                         const void* v_cache, int64_t num_blocks, void* output,
+                                         int64_t output_token_stride,
+                                         const int32_t* query_start_loc, const int32_t* seq_lens,
+                                         const int32_t* block_table, int64_t table_stride,
+                                         int32_t table_cols, float scale, void* stream);
+
 /* ---- around the four ops --------------------------------------------------------------------
  * replaces ModelRunner._copy_blocks (vflorence/engine/model_runner.py:162-167):
  * for every layer l and pair p: k_caches[l][dst_p] = k_caches[l][src_p], same for v_caches,

@@ -30,6 +30,7 @@ DEVERR_QUERY = 0x10
 
 PLAN_MAGIC = 0x31504C4656
 MAX_COPY_LAYERS = 128
+STATIC_WORKSPACE_BYTES = 64 * 1024 * 1024
 
 # Every exported entry point of the C ABI, in header order.
 EXPORTS = (
@@ -41,6 +42,7 @@ EXPORTS = (
     "vfl_plan_attention",
     "vfl_reshape_and_cache",
     "vfl_attention_with_kv_cache",
+    "vfl_attention_with_kv_cache_no_alloc",
     "vfl_copy_blocks",
     "vfl_prepare_decode",
     "vfl_paged_slots",
@@ -99,6 +101,8 @@ def _declare(L):
         "vfl_reshape_and_cache": (i32, [vp, vp, vp, vp, vp, i64, i32, i32, i32, i64, i64, i64, i32, vp]),
         "vfl_attention_with_kv_cache": (i32, [vp, vp, i64, vp, vp, i64, vp, i64, vp, vp, vp, i64, i32,
                                               f32, vp, sz, vp]),
+        "vfl_attention_with_kv_cache_no_alloc": (i32, [plan_p, vp, i64, vp, vp, i64, vp, i64, vp, vp, vp,
+                                                       i64, i32, f32, vp]),
         "vfl_copy_blocks": (i32, [vp, vp, i32, vp, i32, i64, i64, vp]),
         "vfl_prepare_decode": (i32, [vp, i64, i32, vp, i32, i32, vp, vp, vp, vp]),
         "vfl_paged_slots": (i32, [vp, i64, i32, i32, i32, i32, vp, vp]),
