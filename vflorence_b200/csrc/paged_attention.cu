@@ -72,7 +72,7 @@ int vfl_plan_attention(int num_reqs, int num_heads, int num_kv_heads, int head_d
   const int groups = num_heads / hpc;
   const int smem = kHeaderBytes + stages * stage_bytes;
   int ctas_per_sm = kSmemPerSM / (smem + 1024);
-  const int thread_cap = 2048 / (hpc * 32);
+  const int thread_cap = 2048 / ((hpc + 1) * 32);
   ctas_per_sm = ctas_per_sm < 1 ? 1 : (ctas_per_sm > thread_cap ? thread_cap : ctas_per_sm);
 
   // split-K: aim for kWaves waves of CTAs over the SMs, items of at most kMaxSplitTokens tokens
@@ -195,7 +195,7 @@ int vfl_attention_with_kv_cache(const vfl_attention_plan* plan, const void* quer
   const int qpc = plan->queries_per_cta;
   const int q_chunks = static_cast<int>(ceil_div(plan->max_q_len < 1 ? 1 : plan->max_q_len, qpc));
   dim3 grid(plan->num_reqs * (H / hpc), plan->num_splits, q_chunks);
-  const int threads = hpc * 32;
+  const int threads = (hpc + 1) * 32;  // hpc consumer warps + one producer warp
   const int smem = kHeaderBytes + plan->stages * 2 * hpc * 16 * D * es;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (plan->dtype == VFL_DTYPE_F32) return launch_paged_attention_f32(p, D, qpc, grid, threads, smem, s);

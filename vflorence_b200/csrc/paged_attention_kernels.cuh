@@ -54,11 +54,23 @@ struct AttnParams {
 };
 
 constexpr int kMaxBlocksPerSplit = 64;
-constexpr int kHeaderBytes = 1024;  // block-table slice, barriers, abort flag
+constexpr int kMaxStages = 8;
+constexpr int kHeaderBytes = 1024;  // block-table slice, full/empty barriers, flags
 constexpr int kMaxStageBytes = 64 * 1024;
 
+// Shared-memory header layout.
+struct SmemHeader {
+  int32_t table[kMaxBlocksPerSplit];  // this item's block ids (validated)
+  uint64_t full[kMaxStages];          // stage s holds tile data (TMA transaction bytes)
+  uint64_t empty[kMaxStages];         // every consumer warp is done with stage s
+  int abort;                          // a bounded wait gave up
+  int consumed;                       // tiles consumed before an abort
+};
+static_assert(sizeof(SmemHeader) <= kHeaderBytes, "header");
+
+// Warp roles: warps [0, heads_per_cta) consume (one head each); warp heads_per_cta produces.
 template <typename T, int D, int QPC>
-__global__ void __launch_bounds__(128) paged_attention_kernel(const AttnParams p) {
+__global__ void __launch_bounds__(160) paged_attention_kernel(const AttnParams p) {
   constexpr int VEC = Elem<T>::kVec;         // elements per 16-byte vector
   constexpr int NCH = 16 / VEC;              // 16-byte chunks in a lane's 16-element QK slice
   constexpr int TPT_RAW = D / 16;            // slice lanes that hold data
@@ -75,18 +87,16 @@ __global__ void __launch_bounds__(128) paged_attention_kernel(const AttnParams p
   static_assert(TPP % TSUB == 0, "PV token subgroups must nest in QK passes");
 
   extern __shared__ __align__(128) uint8_t smem[];
-  int32_t* s_table = reinterpret_cast<int32_t*>(smem);
-  uint64_t* s_bar = reinterpret_cast<uint64_t*>(smem + kMaxBlocksPerSplit * 4);
-  volatile int* s_abort = reinterpret_cast<volatile int*>(smem + kMaxBlocksPerSplit * 4 + 8 * 8);
+  SmemHeader& hdr = *reinterpret_cast<SmemHeader*>(smem);
   T* s_kv = reinterpret_cast<T*>(smem + kHeaderBytes);
 
   const int hpc = p.heads_per_cta;
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const bool producer = warp == hpc;
   const int groups = p.num_heads / hpc;
   const int r = blockIdx.x / groups;
   const int h0 = (blockIdx.x - r * groups) * hpc;
-  const int h = h0 + warp;
   const int split = blockIdx.y;
   const int bs = p.block_size;
   const int bps = p.blocks_per_split;
@@ -133,54 +143,83 @@ __global__ void __launch_bounds__(128) paged_attention_kernel(const AttnParams p
   const int ntiles = max(0, tile_end - tile_begin);
   const int stages = p.stages;
   const int stage_elems = 2 * hpc * TILE;
+  const uint32_t head_tile_bytes = TILE * sizeof(T);
 
-  // ---- block-table slice (validated) and barriers
-  const int nb = min(bps, nblk - blk_begin);
-  for (int i = threadIdx.x; i < nb; i += blockDim.x) {
-    int b = __ldg(p.table + r * p.table_stride + blk_begin + i);
-    if (b < 0 || b >= p.num_blocks) {
-      report(p.err, VFL_DEVERR_BLOCK_ID);
-      b = 0;  // read a valid block instead; the error word flags the result as garbage
+  // ---- set-up: the producer stages the block-table slice, thread 0 the barriers
+  if (producer) {
+    const int nb = min(bps, nblk - blk_begin);
+    for (int i = lane; i < nb; i += 32) {
+      int b = __ldg(p.table + r * p.table_stride + blk_begin + i);
+      if (b < 0 || b >= p.num_blocks) {
+        report(p.err, VFL_DEVERR_BLOCK_ID);
+        b = 0;  // read a valid block instead; the error word flags the result as garbage
+      }
+      hdr.table[i] = b;
     }
-    s_table[i] = b;
   }
   if (threadIdx.x == 0) {
-    for (int s = 0; s < stages; ++s) mbar_init(&s_bar[s], 1);
-    *s_abort = 0;
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(&hdr.full[s], 1);
+      mbar_init(&hdr.empty[s], hpc);
+    }
+    hdr.abort = 0;
+    hdr.consumed = 0;
     fence_barrier_init();
   }
   __syncthreads();
 
-  const uint32_t head_tile_bytes = TILE * sizeof(T);
-  int issued = 0;            // tiles whose copies thread 0 has started
-  auto issue = [&](int i) {  // thread 0 only: start the copy of tile i into stage i % stages
-    issued = i + 1;
-    const int tile = tile_begin + i;
-    const int blk = tile / tpb;
-    const int sub_tile = tile - blk * tpb;
-    const int64_t phys = s_table[blk - blk_begin];
-    const int s = i % stages;
-    T* ks = s_kv + (size_t)s * stage_elems;
-    T* vs = ks + hpc * TILE;
-    mbar_arrive_expect_tx(&s_bar[s], 2u * hpc * head_tile_bytes);
-    const int64_t base = ((phys * p.num_heads + h0) * bs + sub_tile * 16) * D;
-    if (tpb == 1) {  // the head group's tiles are adjacent: one copy each for K and V
-      bulk_copy_g2s(ks, static_cast<const T*>(p.k_cache) + base, hpc * head_tile_bytes, &s_bar[s]);
-      bulk_copy_g2s(vs, static_cast<const T*>(p.v_cache) + base, hpc * head_tile_bytes, &s_bar[s]);
-    } else {
-      for (int w = 0; w < hpc; ++w) {
-        const int64_t off = base + (int64_t)w * bs * D;
-        bulk_copy_g2s(ks + w * TILE, static_cast<const T*>(p.k_cache) + off, head_tile_bytes, &s_bar[s]);
-        bulk_copy_g2s(vs + w * TILE, static_cast<const T*>(p.v_cache) + off, head_tile_bytes, &s_bar[s]);
+  if (producer) {
+    // ================= producer: stream tiles into the stage ring ==========================
+    int issued = 0;
+    if (lane == 0) {
+      const uint64_t policy = l2_evict_first_policy();
+      for (int i = 0; i < ntiles; ++i) {
+        const int s = i % stages;
+        if (i >= stages && !mbar_wait_bounded(&hdr.empty[s], ((i / stages) - 1) & 1)) {
+          report(p.err, VFL_DEVERR_TIMEOUT);
+          hdr.abort = 1;
+          break;
+        }
+        if (*reinterpret_cast<volatile int*>(&hdr.abort)) break;
+        fence_proxy_async_smem();
+        const int tile = tile_begin + i;
+        const int blk = tile / tpb;
+        const int sub_tile = tile - blk * tpb;
+        const int64_t phys = hdr.table[blk - blk_begin];
+        T* ks = s_kv + (size_t)s * stage_elems;
+        T* vs = ks + hpc * TILE;
+        mbar_arrive_expect_tx(&hdr.full[s], 2u * hpc * head_tile_bytes);
+        const int64_t base = ((phys * p.num_heads + h0) * bs + sub_tile * 16) * D;
+        if (tpb == 1) {  // the head group's tiles are adjacent: one copy each for K and V
+          bulk_copy_g2s_hint(ks, static_cast<const T*>(p.k_cache) + base, hpc * head_tile_bytes,
+                             &hdr.full[s], policy);
+          bulk_copy_g2s_hint(vs, static_cast<const T*>(p.v_cache) + base, hpc * head_tile_bytes,
+                             &hdr.full[s], policy);
+        } else {
+          for (int w = 0; w < hpc; ++w) {
+            const int64_t off = base + (int64_t)w * bs * D;
+            bulk_copy_g2s_hint(ks + w * TILE, static_cast<const T*>(p.k_cache) + off, head_tile_bytes,
+                               &hdr.full[s], policy);
+            bulk_copy_g2s_hint(vs + w * TILE, static_cast<const T*>(p.v_cache) + off, head_tile_bytes,
+                               &hdr.full[s], policy);
+          }
+        }
+        issued = i + 1;
       }
     }
-  };
-  if (threadIdx.x == 0) {
-    const int pre = min(stages, ntiles);
-    for (int i = 0; i < pre; ++i) issue(i);
+    __syncwarp();
+    __syncthreads();  // pairs with the consumers' barrier below
+    if (lane == 0 && *reinterpret_cast<volatile int*>(&hdr.abort)) {
+      // Let copies still in flight land (bounded) before the CTA's shared memory is released.
+      for (int t = *reinterpret_cast<volatile int*>(&hdr.consumed); t < issued; ++t)
+        mbar_wait_bounded(&hdr.full[t % stages], (t / stages) & 1);
+    }
+    return;
   }
 
-  // ---- query slice in registers: chunk c of the registers pairs with shared chunk (c+rot)%NCH
+  // ================= consumers: one warp per head ==========================================
+  const int h = h0 + warp;
+  // query slice in registers: chunk c of the registers pairs with shared chunk (c+rot)%NCH
   const int sub = lane % TPT;
   const int tip = lane / TPT;
   const bool qk_on = sub < TPT_RAW;
@@ -223,14 +262,18 @@ __global__ void __launch_bounds__(128) paged_attention_kernel(const AttnParams p
     for (int e = 0; e < CPL * VEC; ++e) acc[j][e] = 0.f;
   }
 
-  // ---- main loop over 16-token tiles
   bool aborted = false;
 #pragma unroll 1
   for (int i = 0; i < ntiles; ++i) {
     const int s = i % stages;
-    if (!mbar_wait_bounded(&s_bar[s], (i / stages) & 1)) {
+    if (!mbar_wait_bounded(&hdr.full[s], (i / stages) & 1)) {
       report(p.err, VFL_DEVERR_TIMEOUT);
-      *s_abort = 1;
+      if (lane == 0) {
+        hdr.abort = 1;
+        atomicMax(&hdr.consumed, i);
+      }
+      aborted = true;
+      break;
     }
     const T* kt = s_kv + (size_t)s * stage_elems + warp * TILE;
     const T* vt = kt + hpc * TILE;
@@ -300,23 +343,11 @@ __global__ void __launch_bounds__(128) paged_attention_kernel(const AttnParams p
         }
       }
     }
-    __syncthreads();  // every warp is done with stage s
-    if (*s_abort) {
-      aborted = true;
-      break;
-    }
-    if (threadIdx.x == 0 && i + stages < ntiles) {
-      fence_proxy_async_smem();
-      issue(i + stages);
-    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&hdr.empty[s]);  // this warp is done with stage s
   }
-  if (aborted) {
-    // Let copies still in flight land (bounded) before the CTA's shared memory is released.
-    if (threadIdx.x == 0)
-      for (int t = max(0, issued - stages); t < issued; ++t)
-        mbar_wait_bounded(&s_bar[t % stages], (t / stages) & 1);
-    return;
-  }
+  __syncthreads();  // pairs with the producer's barrier (abort bookkeeping)
+  if (aborted || *reinterpret_cast<volatile int*>(&hdr.abort)) return;
 
   // ---- reduce the PV accumulators over token subgroups
 #pragma unroll
@@ -361,9 +392,11 @@ __global__ void __launch_bounds__(128) paged_attention_kernel(const AttnParams p
   }
 }
 
-// One warp per (query row, head) of a request that was split: merges the partials.
+// One warp per (query row, head) of a request that was split: merges the partials. Lane s
+// holds the weight of split s (32 at a time) and broadcasts it; each lane owns D/32 dims.
 template <typename T, int D>
 __global__ void __launch_bounds__(128) paged_attention_combine_kernel(const AttnParams p) {
+  constexpr int DPL = (D + 31) / 32;  // dims per lane
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int64_t gw = (int64_t)blockIdx.x * (blockDim.x >> 5) + warp;
@@ -384,27 +417,44 @@ __global__ void __launch_bounds__(128) paged_attention_combine_kernel(const Attn
   if (n_splits <= 1) return;  // written directly by the main kernel
   const int S = p.num_splits;
   const int64_t item0 = ((int64_t)row * p.num_heads + h) * S;
-  const float* ml = p.ws_ml + item0 * 2;
+  const float2* ml = reinterpret_cast<const float2*>(p.ws_ml) + item0;
   float M = -INFINITY;
-  for (int s = lane; s < n_splits; s += 32) M = fmaxf(M, ml[2 * s]);
+  for (int s = lane; s < n_splits; s += 32) M = fmaxf(M, ml[s].x);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+  const float* acc = p.ws_acc + item0 * D;
+  float a[DPL];
+#pragma unroll
+  for (int k = 0; k < DPL; ++k) a[k] = 0.f;
   float Lsum = 0.f;
-  if (M != -INFINITY)
-    for (int s = lane; s < n_splits; s += 32) Lsum += exp2f(ml[2 * s] - M) * ml[2 * s + 1];
+  if (M != -INFINITY) {
+    for (int s0 = 0; s0 < n_splits; s0 += 32) {
+      float w = 0.f;
+      if (s0 + lane < n_splits) {
+        const float2 v = ml[s0 + lane];
+        w = exp2f(v.x - M);
+        Lsum = fmaf(w, v.y, Lsum);
+      }
+      const int n = min(32, n_splits - s0);
+#pragma unroll 4
+      for (int j = 0; j < n; ++j) {
+        const float wj = __shfl_sync(0xffffffffu, w, j);
+        const float* src = acc + (int64_t)(s0 + j) * D;
+#pragma unroll
+        for (int k = 0; k < DPL; ++k)
+          if (lane + 32 * k < D) a[k] = fmaf(wj, src[lane + 32 * k], a[k]);
+      }
+    }
+  }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) Lsum += __shfl_xor_sync(0xffffffffu, Lsum, o);
   const float inv = Lsum > 0.f ? 1.f / Lsum : 0.f;
   T* out = static_cast<T*>(p.out) + (int64_t)row * p.out_stride + h * D;
-  const float* acc = p.ws_acc + item0 * D;
-  for (int d = lane; d < D; d += 32) {
-    float a = 0.f;
-    if (M != -INFINITY)
-      for (int s = 0; s < n_splits; ++s) {
-        const float w = exp2f(ml[2 * s] - M);
-        a = fmaf(w, acc[(int64_t)s * D + d], a);
-      }
-    const float v = a * inv;
+#pragma unroll
+  for (int k = 0; k < DPL; ++k) {
+    const int d = lane + 32 * k;
+    if (d >= D) continue;
+    const float v = a[k] * inv;
     if constexpr (sizeof(T) == 4) {
       out[d] = v;
     } else {
