@@ -251,6 +251,117 @@ def cpu_baseline(batch: int, seconds: float = 10.0, sample: int = 32):
             "seconds_per_step": el / reps}
 
 
+# -------------------------------------------------------------------------------------- sweep
+
+def _cross_workload(batch, enc_len, seed, device):
+    g = torch.Generator().manual_seed(seed)
+    cw = math.ceil(enc_len / BS)
+    table = torch.randperm(batch * cw, generator=g).to(torch.int32).view(batch, cw).contiguous()
+    gd = torch.Generator(device=device).manual_seed(seed)
+    rnd = lambda *s: torch.randn(*s, generator=gd, device=device, dtype=DTYPE)  # noqa: E731
+    return dict(table=table, lens=torch.full((batch,), enc_len, dtype=torch.int32),
+                k=rnd(batch * cw, H, BS, D), v=rnd(batch * cw, H, BS, D), q=rnd(batch, H, D))
+
+
+def _time_op(fn, reps, flush):
+    """Mean device time of fn() over reps calls, L2 flushed (256 MB write) before each."""
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
+    for a, b in evs:
+        flush.zero_()
+        a.record()
+        fn()
+        b.record()
+    torch.cuda.synchronize()
+    return sum(a.elapsed_time(b) for a, b in evs) / reps
+
+
+def _cpu_attn_gbs(oracle, q, k, v, lens, table, nbytes, threads):
+    qsl = torch.arange(lens.numel() + 1, dtype=torch.int32)
+    out = torch.empty_like(q)
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        oracle.attention(q, k, v, out, qsl, lens, D ** -0.5, False, table, threads)
+        reps += 1
+        el = time.perf_counter() - t0
+        if el > 0.5:
+            return nbytes * reps / el / 1e9, el / reps
+
+
+def run_sweep(args):
+    """batch 1..1024, self ctx U[1,4096] and cross at 577 / 1024 tokens.
+    One JSON line per point: device GB/s and us per call (L2 flushed before every call), the
+    fraction of the measured HBM bandwidth, and the C oracle on the host cores (a sample of up
+    to 16 sequences of the point)."""
+    from vflorence_b200 import paged_ops as ops
+
+    sys.path.insert(0, os.path.join(REPO, "oracle"))
+    import oracle
+
+    oracle.build()
+    threads = oracle.max_threads()
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    peak, _ = load_peaks()
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=device)
+    row = H * D * ELEM
+    batches = [int(b) for b in args.sweep_batches.split(",")]
+    for B in batches:
+        w = make_workload(B, 2, device)
+        nb = algorithmic_bytes(w)["self"]
+        meta = ops.get_scheduler_metadata(B, H, H, D, w["ctx"], DTYPE, w["qsl"], False, "sm100", BS)
+        d = {k: w[k].to(device) for k in ("table", "ctx", "qsl")}
+        out = torch.empty_like(w["q"])
+        fn = lambda: ops.attention_with_kv_cache(w["q"], w["k_cache"], w["v_cache"], out, d["qsl"],  # noqa: E731
+                                                 d["ctx"], D ** -0.5, False, d["table"], meta)
+        for _ in range(3):
+            fn()
+        reps = max(5, min(200, int(2e9 / max(nb, 1))))
+        ms = _time_op(fn, reps, flush)
+        # CPU oracle on a sample of the same sequences
+        n = min(B, 16)
+        rows = torch.arange(n)
+        need = int(((w["ctx"][rows] + BS - 1) // BS).max())
+        ids = w["table"][rows, :need]
+        uniq, inv = torch.unique(ids.long(), return_inverse=True)
+        kc, vc = w["k_cache"][uniq.to(device)].cpu(), w["v_cache"][uniq.to(device)].cpu()
+        sub = dict(batch=n, ctx=w["ctx"][rows])
+        cpu_gbs, cpu_s = _cpu_attn_gbs(oracle, w["q"][:n].cpu(), kc, vc, w["ctx"][rows].contiguous(),
+                                       inv.to(torch.int32).contiguous(), algorithmic_bytes(sub)["self"], threads)
+        plan = ops.plan_of(meta)
+        print(json.dumps({"point": "self", "batch": B, "ctx": "U[1,4096]", "us": ms * 1e3,
+                          "gbs": nb / ms / 1e6, "frac_of_measured_hbm": nb / ms / 1e6 / peak,
+                          "splits": plan.num_splits, "blocks_per_split": plan.blocks_per_split,
+                          "cpu_oracle_gbs": cpu_gbs, "cpu_threads": threads,
+                          "cpu_sample_seqs": n}), flush=True)
+        del w, kc, vc
+        for enc in (577, 1024):
+            c = _cross_workload(B, enc, 3, device)
+            lens_d, table_d = c["lens"].to(device), c["table"].to(device)
+            qsl = torch.arange(B + 1, dtype=torch.int32)
+            meta_c = ops.get_scheduler_metadata(B, H, H, D, c["lens"], DTYPE, qsl, False, "sm100", BS)
+            qsl_d = qsl.to(device)
+            out_c = torch.empty_like(c["q"])
+            fc = lambda: ops.attention_with_kv_cache(c["q"], c["k"], c["v"], out_c, qsl_d, lens_d,  # noqa: E731
+                                                     D ** -0.5, False, table_d, meta_c)
+            for _ in range(3):
+                fc()
+            nbc = 2 * B * enc * row + 2 * B * row + 4 * B * math.ceil(enc / BS) + 4 * B + 4 * (B + 1)
+            ms_c = _time_op(fc, max(5, min(200, int(2e9 / nbc))), flush)
+            n = min(B, 16)
+            cw = math.ceil(enc / BS)
+            ids = c["table"][:n].long().flatten()
+            kc, vc = c["k"][ids.to(device)].cpu(), c["v"][ids.to(device)].cpu()
+            tab = torch.arange(n * cw, dtype=torch.int32).view(n, cw)
+            sub_b = 2 * n * enc * row + 2 * n * row
+            cpu_gbs, _ = _cpu_attn_gbs(oracle, c["q"][:n].cpu(), kc, vc, c["lens"][:n].contiguous(), tab,
+                                       sub_b, threads)
+            print(json.dumps({"point": "cross", "batch": B, "enc_len": enc, "us": ms_c * 1e3,
+                              "gbs": nbc / ms_c / 1e6, "frac_of_measured_hbm": nbc / ms_c / 1e6 / peak,
+                              "cpu_oracle_gbs": cpu_gbs, "cpu_threads": threads, "cpu_sample_seqs": n}),
+                  flush=True)
+            del c, kc, vc
+
+
 # -------------------------------------------------------------------------------------- main
 
 def dist_setup():
@@ -326,8 +437,13 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--cpu-sample", type=int, default=32)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--sweep", action="store_true", help="BASELINE config-5 batch sweep, one line per point")
+    ap.add_argument("--sweep-batches", default="1,2,4,8,16,32,64,128,256,512,1024")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.sweep:
+        run_sweep(args)
+        return
 
     if args.impl == "reference":
         world = int(os.environ.get("WORLD_SIZE", "1"))

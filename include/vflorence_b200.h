@@ -74,7 +74,8 @@ typedef struct vfl_attention_plan {
   int32_t blocks_per_split; /* KV blocks per split-K work item                           */
   int32_t num_splits;       /* split-K partitions of the longest request                 */
   int32_t stages;           /* shared-memory pipeline depth (16-token K/V tiles)         */
-  int32_t reserved;
+  int32_t merge_in_kernel;  /* split partials merged by the last split CTA (1) or by a
+                               separate combine launch (0)                              */
   int64_t workspace_bytes;  /* scratch the caller must pass (0 = none)                   */
 } vfl_attention_plan;
 

@@ -65,6 +65,17 @@ def test_plan_large_batch_splits_long_requests(native):
     assert p.num_splits == -(-max(lens) // 256)
     assert p.workspace_bytes >= 1024 * 16 * p.num_splits * (64 + 2) * 4
     assert p.total_q == 1024 and p.max_seq_len == max(lens)
+    assert p.merge_in_kernel == 0          # bandwidth-bound: separate combine launch
+
+
+def test_plan_merge_mode_follows_the_work(native):
+    g = torch.Generator().manual_seed(2)
+    small = _plan(torch.randint(1, 4097, (8,), generator=g).tolist())
+    assert small.num_splits > 1 and small.merge_in_kernel == 1   # latency-bound: merge in kernel
+    big = _plan(torch.randint(1, 4097, (256,), generator=g).tolist())
+    assert big.num_splits > 1 and big.merge_in_kernel == 0
+    # the in-kernel merge needs arrival counters, one per (request, head group, query chunk)
+    assert small.workspace_bytes >= 8 * (16 // small.heads_per_cta) * 4
 
 
 def test_plan_single_long_request_fills_the_gpu(native):

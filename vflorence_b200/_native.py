@@ -68,7 +68,7 @@ class AttentionPlan(ctypes.Structure):
         ("blocks_per_split", ctypes.c_int32),
         ("num_splits", ctypes.c_int32),
         ("stages", ctypes.c_int32),
-        ("reserved", ctypes.c_int32),
+        ("merge_in_kernel", ctypes.c_int32),
         ("workspace_bytes", ctypes.c_int64),
     ]
 

@@ -102,10 +102,23 @@ int vfl_plan_attention(int num_reqs, int num_heads, int num_kv_heads, int head_d
   if (q_chunks > 65535 || (int64_t)num_reqs * groups > INT32_MAX)
     return plan_fail(plan, fail(VFL_ERR_UNSUPPORTED, "launch grid too large"));
 
+  // Merge of split partials: when the split work items fit in ~kWaves waves the call is
+  // latency-bound, and the last split CTA of each item merges in the same launch; above that
+  // a separate combine launch is cheaper than every split CTA waiting on an arrival counter.
+  int64_t split_items = 0;
+  for (int r = 0; r < num_reqs; ++r) {
+    const int64_t ql = query_start_loc_host ? (int64_t)query_start_loc_host[r + 1] - query_start_loc_host[r] : 1;
+    split_items += ceil_div(ceil_div((int64_t)seq_lens_host[r], (int64_t)block_size), bps) * groups *
+                   ceil_div(ql, (int64_t)qpc);
+  }
+  const int merge_in_kernel = splits > 1 && split_items <= target ? 1 : 0;
+
+  // workspace: acc partials | (m, l) partials | arrival counters (in-kernel merge only)
   int64_t ws = 0;
   if (splits > 1) {
     const int64_t items = total_q * num_heads * splits;
-    ws = ceil_div(items * head_dim * 4, (int64_t)256) * 256 + items * 2 * 4;
+    ws = ceil_div(items * head_dim * 4, (int64_t)256) * 256 + ceil_div(items * 2 * 4, (int64_t)256) * 256 +
+         (merge_in_kernel ? (int64_t)num_reqs * groups * q_chunks * 4 : 0);
   }
 
   plan->magic = VFL_PLAN_MAGIC;
@@ -123,7 +136,7 @@ int vfl_plan_attention(int num_reqs, int num_heads, int num_kv_heads, int head_d
   plan->blocks_per_split = static_cast<int32_t>(bps);
   plan->num_splits = static_cast<int32_t>(splits);
   plan->stages = stages;
-  plan->reserved = 0;
+  plan->merge_in_kernel = merge_in_kernel;
   plan->workspace_bytes = ws;
   return VFL_OK;
 }
@@ -182,22 +195,29 @@ int vfl_attention_with_kv_cache(const vfl_attention_plan* plan, const void* quer
   p.stages = plan->stages;
   p.max_seq_len = plan->max_seq_len;
   p.scale_log2 = scale * 1.4426950408889634f;
-  if (plan->num_splits > 1) {
-    const int64_t items = (int64_t)plan->total_q * H * plan->num_splits;
-    p.ws_acc = static_cast<float*>(workspace);
-    p.ws_ml = reinterpret_cast<float*>(static_cast<char*>(workspace) +
-                                       ceil_div(items * D * 4, (int64_t)256) * 256);
-  }
   int st = device_error_word(&p.err);
   if (st) return st;
-
   const int hpc = plan->heads_per_cta;
   const int qpc = plan->queries_per_cta;
   const int q_chunks = static_cast<int>(ceil_div(plan->max_q_len < 1 ? 1 : plan->max_q_len, qpc));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (plan->num_splits > 1) {
+    const int64_t items = (int64_t)plan->total_q * H * plan->num_splits;
+    const int64_t acc_bytes = ceil_div(items * D * 4, (int64_t)256) * 256;
+    const int64_t ml_bytes = ceil_div(items * 2 * 4, (int64_t)256) * 256;
+    char* base = static_cast<char*>(workspace);
+    p.ws_acc = reinterpret_cast<float*>(base);
+    p.ws_ml = reinterpret_cast<float*>(base + acc_bytes);
+    if (plan->merge_in_kernel) {
+      p.ws_arrivals = reinterpret_cast<int*>(base + acc_bytes + ml_bytes);
+      const size_t counter_bytes = (size_t)plan->num_reqs * (H / hpc) * q_chunks * 4;
+      st = cuda_status(cudaMemsetAsync(p.ws_arrivals, 0, counter_bytes, s), "cudaMemsetAsync(arrival counters)");
+      if (st) return st;
+    }
+  }
   dim3 grid(plan->num_reqs * (H / hpc), plan->num_splits, q_chunks);
   const int threads = (hpc + 1) * 32;  // hpc consumer warps + one producer warp
   const int smem = kHeaderBytes + plan->stages * 2 * hpc * 16 * D * es;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (plan->dtype == VFL_DTYPE_F32) return launch_paged_attention_f32(p, D, qpc, grid, threads, smem, s);
   return launch_paged_attention_bf16(p, D, qpc, grid, threads, smem, s);
 }

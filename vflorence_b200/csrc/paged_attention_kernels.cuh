@@ -17,7 +17,10 @@
 //   PV: lanes = (16-byte V chunk `dch`, token subgroup `tsub`); p is fetched from the QK lanes by
 //       shuffle; per-lane fp32 accumulators are reduced over `tsub` once per work item.
 // A work item whose request needs one split writes the normalised output; otherwise it writes
-// (m, l, acc) partials and the combine kernel merges them.
+// (m, l, acc) partials, merged either by the last split CTA of the (request, head group) to
+// finish - counted on an arrival counter that the launcher clears; chosen for latency-bound
+// calls - or by a separate combine launch (bandwidth-bound calls, where waiting on the counter
+// would hold every split CTA's SM slot).
 #pragma once
 
 #include "common.cuh"
@@ -50,6 +53,8 @@ struct AttnParams {
   float scale_log2;  // softmax scale * log2(e)
   float* ws_acc;     // [total_q, H, num_splits, D]
   float* ws_ml;      // [total_q, H, num_splits, 2]
+  int* ws_arrivals;  // [num_reqs, H / heads_per_cta, q_chunks], zero at launch; null: the
+                     // combine kernel merges the partials instead
   unsigned int* err;
 };
 
@@ -65,12 +70,77 @@ struct SmemHeader {
   uint64_t empty[kMaxStages];         // every consumer warp is done with stage s
   int abort;                          // a bounded wait gave up
   int consumed;                       // tiles consumed before an abort
+  int is_last;                        // this CTA is the last split of its item to finish
 };
 static_assert(sizeof(SmemHeader) <= kHeaderBytes, "header");
 
+// Merges the split-K partials of one (query row, head) into the output: one warp, lane s holds
+// the weight of split s (32 at a time) and broadcasts it; each lane owns D/32 dims. Partials are
+// read through L2 (other CTAs wrote them).
+template <typename T, int D>
+__device__ __forceinline__ void merge_splits(const AttnParams& p, int row, int h, int n_splits, int lane) {
+  constexpr int DPL = (D + 31) / 32;
+  const int64_t item0 = ((int64_t)row * p.num_heads + h) * p.num_splits;
+  const float2* ml = reinterpret_cast<const float2*>(p.ws_ml) + item0;
+  float M = -INFINITY;
+  for (int s = lane; s < n_splits; s += 32) M = fmaxf(M, __ldcg(ml + s).x);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+  const float* acc = p.ws_acc + item0 * D;
+  float a[DPL];
+#pragma unroll
+  for (int k = 0; k < DPL; ++k) a[k] = 0.f;
+  float Lsum = 0.f;
+  if (M != -INFINITY) {
+    for (int s0 = 0; s0 < n_splits; s0 += 32) {
+      float w = 0.f;
+      if (s0 + lane < n_splits) {
+        const float2 v = __ldcg(ml + s0 + lane);
+        w = exp2f(v.x - M);
+        Lsum = fmaf(w, v.y, Lsum);
+      }
+      const int n = min(32, n_splits - s0);
+#pragma unroll 4
+      for (int j = 0; j < n; ++j) {
+        const float wj = __shfl_sync(0xffffffffu, w, j);
+        const float* src = acc + (int64_t)(s0 + j) * D;
+#pragma unroll
+        for (int k = 0; k < DPL; ++k)
+          if (lane + 32 * k < D) a[k] = fmaf(wj, __ldcg(src + lane + 32 * k), a[k]);
+      }
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) Lsum += __shfl_xor_sync(0xffffffffu, Lsum, o);
+  const float inv = Lsum > 0.f ? 1.f / Lsum : 0.f;
+  T* out = static_cast<T*>(p.out) + (int64_t)row * p.out_stride + h * D;
+#pragma unroll
+  for (int k = 0; k < DPL; ++k) {
+    const int d = lane + 32 * k;
+    if (d >= D) continue;
+    const float v = a[k] * inv;
+    if constexpr (sizeof(T) == 4) {
+      out[d] = v;
+    } else {
+      out[d] = __float2bfloat16_rn(v);
+    }
+  }
+}
+
+// atomicAdd(1) with acquire-release semantics at GPU scope; returns the previous count.
+__device__ __forceinline__ int arrive_acq_rel(int* counter) {
+  int prev;
+  asm volatile("atom.add.acq_rel.gpu.global.s32 %0, [%1], 1;" : "=r"(prev) : "l"(counter) : "memory");
+  return prev;
+}
+
+__device__ __forceinline__ void consumer_barrier(int consumers) {
+  asm volatile("bar.sync 1, %0;" ::"r"(consumers * 32) : "memory");
+}
+
 // Warp roles: warps [0, heads_per_cta) consume (one head each); warp heads_per_cta produces.
 template <typename T, int D, int QPC>
-__global__ void __launch_bounds__(160) paged_attention_kernel(const AttnParams p) {
+__global__ void __launch_bounds__(160, QPC == 1 ? 3 : 2) paged_attention_kernel(const AttnParams p) {
   constexpr int VEC = Elem<T>::kVec;         // elements per 16-byte vector
   constexpr int NCH = 16 / VEC;              // 16-byte chunks in a lane's 16-element QK slice
   constexpr int TPT_RAW = D / 16;            // slice lanes that hold data
@@ -359,13 +429,13 @@ __global__ void __launch_bounds__(160) paged_attention_kernel(const AttnParams p
       for (int e = 0; e < CPL * VEC; ++e) acc[j][e] += __shfl_xor_sync(0xffffffffu, acc[j][e], o);
     }
   }
-  if (tsub != 0) return;
   const int S = p.num_splits;
+  if (n_splits <= 1) {  // the whole request in this CTA: normalise and store
+    if (tsub != 0) return;
 #pragma unroll
-  for (int j = 0; j < QPC; ++j) {
-    if (j >= nq) break;
-    const int row = q0 + j;
-    if (n_splits <= 1) {
+    for (int j = 0; j < QPC; ++j) {
+      if (j >= nq) break;
+      const int row = q0 + j;
       const float inv = l[j] > 0.f ? 1.f / l[j] : 0.f;
 #pragma unroll
       for (int c = 0; c < CPL; ++c) {
@@ -376,8 +446,15 @@ __global__ void __launch_bounds__(160) paged_attention_kernel(const AttnParams p
         T* dst = static_cast<T*>(p.out) + (int64_t)row * p.out_stride + h * D + (dch + 32 * c) * VEC;
         *reinterpret_cast<uint4*>(dst) = pack16(f, T());
       }
-    } else {
-      const int64_t item = ((int64_t)row * p.num_heads + h) * S + split;
+    }
+    return;
+  }
+  // split request: store this split's (m, l, acc) partials ...
+  if (tsub == 0) {
+#pragma unroll
+    for (int j = 0; j < QPC; ++j) {
+      if (j >= nq) break;
+      const int64_t item = ((int64_t)(q0 + j) * p.num_heads + h) * S + split;
 #pragma unroll
       for (int c = 0; c < CPL; ++c) {
         if (!pv_on[c]) continue;
@@ -390,80 +467,42 @@ __global__ void __launch_bounds__(160) paged_attention_kernel(const AttnParams p
       if (lane == 0) *reinterpret_cast<float2*>(p.ws_ml + item * 2) = make_float2(m[j], l[j]);
     }
   }
+  if (p.ws_arrivals == nullptr) return;  // the combine launch merges
+  // ... and the last split of (request, head group, query chunk) to arrive merges them all:
+  // CTA barrier, then one thread publishes the CTA's writes (release) with its arrival; the
+  // last arriver acquires everyone's partials before the CTA barrier that releases its warps.
+  consumer_barrier(hpc);
+  if (threadIdx.x == 0) {
+    int* arrivals = p.ws_arrivals + ((int64_t)r * groups + h0 / hpc) * gridDim.z + blockIdx.z;
+    hdr.is_last = arrive_acq_rel(arrivals) == n_splits - 1;
+  }
+  consumer_barrier(hpc);
+  if (!hdr.is_last) return;
+  for (int j = 0; j < nq && j < QPC; ++j) merge_splits<T, D>(p, q0 + j, h, n_splits, lane);
 }
 
-// One warp per (query row, head) of a request that was split: merges the partials. Lane s
-// holds the weight of split s (32 at a time) and broadcasts it; each lane owns D/32 dims.
+// Separate merge launch: one warp per (query row, head) of a request that was split.
 template <typename T, int D>
 __global__ void __launch_bounds__(128) paged_attention_combine_kernel(const AttnParams p) {
-  constexpr int DPL = (D + 31) / 32;  // dims per lane
-  const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int64_t gw = (int64_t)blockIdx.x * (blockDim.x >> 5) + warp;
+  const int64_t gw = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (gw >= (int64_t)p.total_q * p.num_heads) return;
   const int row = static_cast<int>(gw / p.num_heads);
   const int h = static_cast<int>(gw - (int64_t)row * p.num_heads);
-  // request owning this row: last r with qsl[r] <= row
-  int lo = 0, hi = p.num_reqs - 1;
+  int lo = 0, hi = p.num_reqs - 1;  // request owning this row: last r with qsl[r] <= row
   while (lo < hi) {
     const int mid = (lo + hi + 1) >> 1;
     if (__ldg(p.qsl + mid) <= row) lo = mid; else hi = mid - 1;
   }
-  const int r = lo;
-  if (row < __ldg(p.qsl + r) || row >= __ldg(p.qsl + r + 1)) return;  // row of no request
-  int L = min(__ldg(p.seq_lens + r), min(p.table_cols * p.block_size, p.max_seq_len));
+  if (row < __ldg(p.qsl + lo) || row >= __ldg(p.qsl + lo + 1)) return;  // row of no request
+  int L = min(__ldg(p.seq_lens + lo), min(p.table_cols * p.block_size, p.max_seq_len));
   L = max(L, 0);
   const int n_splits = ceil_div(ceil_div(L, p.block_size), p.blocks_per_split);
   if (n_splits <= 1) return;  // written directly by the main kernel
-  const int S = p.num_splits;
-  const int64_t item0 = ((int64_t)row * p.num_heads + h) * S;
-  const float2* ml = reinterpret_cast<const float2*>(p.ws_ml) + item0;
-  float M = -INFINITY;
-  for (int s = lane; s < n_splits; s += 32) M = fmaxf(M, ml[s].x);
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-  const float* acc = p.ws_acc + item0 * D;
-  float a[DPL];
-#pragma unroll
-  for (int k = 0; k < DPL; ++k) a[k] = 0.f;
-  float Lsum = 0.f;
-  if (M != -INFINITY) {
-    for (int s0 = 0; s0 < n_splits; s0 += 32) {
-      float w = 0.f;
-      if (s0 + lane < n_splits) {
-        const float2 v = ml[s0 + lane];
-        w = exp2f(v.x - M);
-        Lsum = fmaf(w, v.y, Lsum);
-      }
-      const int n = min(32, n_splits - s0);
-#pragma unroll 4
-      for (int j = 0; j < n; ++j) {
-        const float wj = __shfl_sync(0xffffffffu, w, j);
-        const float* src = acc + (int64_t)(s0 + j) * D;
-#pragma unroll
-        for (int k = 0; k < DPL; ++k)
-          if (lane + 32 * k < D) a[k] = fmaf(wj, src[lane + 32 * k], a[k]);
-      }
-    }
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) Lsum += __shfl_xor_sync(0xffffffffu, Lsum, o);
-  const float inv = Lsum > 0.f ? 1.f / Lsum : 0.f;
-  T* out = static_cast<T*>(p.out) + (int64_t)row * p.out_stride + h * D;
-#pragma unroll
-  for (int k = 0; k < DPL; ++k) {
-    const int d = lane + 32 * k;
-    if (d >= D) continue;
-    const float v = a[k] * inv;
-    if constexpr (sizeof(T) == 4) {
-      out[d] = v;
-    } else {
-      out[d] = __float2bfloat16_rn(v);
-    }
-  }
+  merge_splits<T, D>(p, row, h, n_splits, lane);
 }
 
-// Launches the main kernel (and the combine when the plan splits); defined per dtype.
+// Launches the kernel; defined per dtype.
 int launch_paged_attention_f32(const AttnParams& p, int head_dim, int qpc, dim3 grid, int threads,
                                int smem_bytes, cudaStream_t stream);
 int launch_paged_attention_bf16(const AttnParams& p, int head_dim, int qpc, dim3 grid, int threads,
@@ -478,14 +517,10 @@ int launch_one(const AttnParams& p, dim3 grid, int threads, int smem_bytes, cuda
   if (st) return st;
   kernel<<<grid, threads, smem_bytes, stream>>>(p);
   st = cuda_status(cudaGetLastError(), "paged_attention launch");
-  if (st) return st;
-  if (p.num_splits > 1) {
-    const int64_t warps = (int64_t)p.total_q * p.num_heads;
-    const int blocks = static_cast<int>(ceil_div(warps, (int64_t)4));
-    paged_attention_combine_kernel<T, D><<<blocks, 128, 0, stream>>>(p);
-    st = cuda_status(cudaGetLastError(), "paged_attention combine launch");
-  }
-  return st;
+  if (st || p.num_splits <= 1 || p.ws_arrivals != nullptr) return st;
+  const int64_t warps = (int64_t)p.total_q * p.num_heads;
+  paged_attention_combine_kernel<T, D><<<static_cast<int>(ceil_div(warps, (int64_t)4)), 128, 0, stream>>>(p);
+  return cuda_status(cudaGetLastError(), "paged_attention combine launch");
 }
 
 template <typename T, int D>

@@ -12,10 +12,12 @@
 //     keeps that much memory until the process exits. A plan whose workspace_bytes is larger
 //     is rejected with VFL_ERR_WORKSPACE before anything is launched.
 //   * Every call on a device uses the same array, and it keeps whatever the last call left in
-//     it. Nothing in it has to start at zero: each split-K partial the merge step reads was
-//     written earlier in the same call. Calls whose kernels can overlap on one device (for
-//     example on two streams without an ordering between them) race on the array and give
-//     wrong results; order them on one stream or with events.
+//     it. The only part that must start at zero - the per-request arrival counters that pick
+//     the CTA which merges the split-K partials - is cleared by every call on its stream before
+//     its kernel runs; each partial the merge reads was written earlier in the same call. Calls
+//     whose kernels can overlap on one device (for example on two streams without an ordering
+//     between them) race on the array and give wrong results; order them on one stream or with
+//     events.
 //   * The first call on each device looks up the array's device address (cudaGetSymbolAddress,
 //     with that device current) and caches it; make that first call before any stream capture.
 #include <atomic>
