@@ -162,6 +162,22 @@ __device__ __forceinline__ uint4 ldg_nc_v4(const void* p) {
   return v;
 }
 
+// d{0,1} += a{0,1} * b{0,1} as one packed two-lane fp32 FMA (sm_100 f32x2 arithmetic).
+__device__ __forceinline__ void fma2(float& d0, float& d1, float a0, float a1, float b0, float b1) {
+  asm("{\n\t.reg .b64 a, b, c;\n\t"
+      "mov.b64 a, {%2, %3};\n\tmov.b64 b, {%4, %5};\n\tmov.b64 c, {%0, %1};\n\t"
+      "fma.rn.f32x2 c, a, b, c;\n\tmov.b64 {%0, %1}, c;\n\t}"
+      : "+f"(d0), "+f"(d1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
+
+// 2^x with the hardware approximation (one MUFU op; subnormal results flush to zero).
+__device__ __forceinline__ float exp2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 // ------------------------------------------------------------------ element conversion
 
 template <typename T>

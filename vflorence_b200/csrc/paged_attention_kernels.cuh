@@ -364,15 +364,19 @@ __global__ void __launch_bounds__(160, QPC == 1 ? 3 : 2) paged_attention_kernel(
       }
 #pragma unroll
       for (int j = 0; j < QPC; ++j) {
-        float dot = 0.f;
+        float d0 = 0.f, d1 = 0.f;
 #pragma unroll
-        for (int e = 0; e < 16; ++e) dot = fmaf(qr[j][e], kf[e], dot);
+        for (int e = 0; e < 16; e += 2) fma2(d0, d1, qr[j][e], qr[j][e + 1], kf[e], kf[e + 1]);
+        float dot = d0 + d1;
 #pragma unroll
         for (int o = 1; o < TPT; o <<= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
         sc[j][ps] = (full || tok0 + t < vis[j]) ? dot : -INFINITY;
       }
     }
-    // online softmax (exp2 domain)
+    // online softmax in the exp2 domain. The running reference m only moves when the tile's
+    // maximum exceeds it by more than kRescaleSlack (so p = 2^(s - m) <= 2^kRescaleSlack stays
+    // far from overflow); acc and l always share that reference, so the result is unchanged.
+    constexpr float kRescaleSlack = 8.f;
 #pragma unroll
     for (int j = 0; j < QPC; ++j) {
       float mx = sc[j][0];
@@ -380,15 +384,16 @@ __global__ void __launch_bounds__(160, QPC == 1 ? 3 : 2) paged_attention_kernel(
       for (int ps = 1; ps < PASSES; ++ps) mx = fmaxf(mx, sc[j][ps]);
 #pragma unroll
       for (int o = TPT; o < 32; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-      const float mnew = fmaxf(m[j], mx);
-      const bool none = mnew == -INFINITY;  // nothing visible yet for this row
-      const float alpha = none ? 1.f : exp2f(m[j] - mnew);
+      if (mx > m[j] + kRescaleSlack) {  // warp-uniform
+        const float alpha = m[j] == -INFINITY ? 0.f : exp2_approx(m[j] - mx);
+        m[j] = mx;
+        l[j] *= alpha;
 #pragma unroll
-      for (int ps = 0; ps < PASSES; ++ps) sc[j][ps] = none ? 0.f : exp2f(sc[j][ps] - mnew);
-      m[j] = mnew;
-      l[j] *= alpha;
+        for (int e = 0; e < CPL * VEC; ++e) acc[j][e] *= alpha;
+      }
+      const bool none = m[j] == -INFINITY;  // nothing visible yet for this row
 #pragma unroll
-      for (int e = 0; e < CPL * VEC; ++e) acc[j][e] *= alpha;
+      for (int ps = 0; ps < PASSES; ++ps) sc[j][ps] = none ? 0.f : exp2_approx(sc[j][ps] - m[j]);
     }
     // PV
 #pragma unroll
@@ -409,7 +414,7 @@ __global__ void __launch_bounds__(160, QPC == 1 ? 3 : 2) paged_attention_kernel(
         if (full || tok0 + t < vis[j]) {  // masked tokens may hold anything, even NaN
           l[j] += pj;
 #pragma unroll
-          for (int e = 0; e < CPL * VEC; ++e) acc[j][e] = fmaf(pj, vf[e], acc[j][e]);
+          for (int e = 0; e < CPL * VEC; e += 2) fma2(acc[j][e], acc[j][e + 1], pj, pj, vf[e], vf[e + 1]);
         }
       }
     }
