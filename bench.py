@@ -200,6 +200,15 @@ class ClockSampler:
 
 # ------------------------------------------------------------------------------- CPU baseline
 
+def host_threads() -> int:
+    """Every host core this process may run on (torchrun exports OMP_NUM_THREADS=1; the CPU
+    baseline deliberately ignores that)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
 def cpu_baseline(batch: int, seconds: float = 10.0, sample: int = 32):
     """The C oracle on the host cores over ``sample`` sequences of the same workload."""
     sys.path.insert(0, os.path.join(REPO, "oracle"))
@@ -231,7 +240,7 @@ def cpu_baseline(batch: int, seconds: float = 10.0, sample: int = 32):
     qsl = torch.arange(sample + 1, dtype=torch.int32)
     clens = torch.full((sample,), ENC_LEN, dtype=torch.int32)
     out, outc = torch.empty_like(q), torch.empty_like(q)
-    threads = oracle.max_threads()
+    threads = host_threads()
     sub = dict(batch=sample, ctx=ctx)
     nbytes = algorithmic_bytes(sub)["total"]
     reps, t0 = 0, time.perf_counter()
@@ -298,7 +307,7 @@ def run_sweep(args):
     import oracle
 
     oracle.build()
-    threads = oracle.max_threads()
+    threads = host_threads()
     device = torch.device("cuda", 0)
     torch.cuda.set_device(device)
     peak, _ = load_peaks()
@@ -379,26 +388,6 @@ def dist_setup():
     return world, rank, local
 
 
-def max_over_ranks(x: float, world: int) -> float:
-    if world == 1:
-        return x
-    import torch.distributed as dist
-
-    t = torch.tensor([x], dtype=torch.float64, device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    return float(t.item())
-
-
-def sum_over_ranks(x: float, world: int) -> float:
-    if world == 1:
-        return x
-    import torch.distributed as dist
-
-    t = torch.tensor([x], dtype=torch.float64, device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.SUM)
-    return float(t.item())
-
-
 def barrier(world: int):
     if world > 1:
         import torch.distributed as dist
@@ -455,6 +444,7 @@ def main():
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
     from vflorence_b200 import paged_ops as ops
+    from vflorence_b200.sharding import max_over_ranks, sum_over_ranks
 
     w = make_workload(args.batch, 2 + rank, device)
     step = Step(w, device)
@@ -496,8 +486,8 @@ def main():
     t_self = sum(e[1].elapsed_time(e[2]) for e in evs) / args.steps
     t_append = sum(e[0].elapsed_time(e[1]) for e in evs) / args.steps
     t_cross = sum(e[2].elapsed_time(e[3]) for e in evs) / args.steps
-    elapsed_max = max_over_ranks(elapsed_ms, world)
-    total_bytes = sum_over_ranks(float(nb["total"] * args.steps), world)
+    elapsed_max = max_over_ranks(elapsed_ms)
+    total_bytes = sum_over_ranks(float(nb["total"] * args.steps))
     value = total_bytes / (elapsed_max / 1e3) / 1e9
 
     # ---- e2e leg: public API with host buffers (pinned inputs up, outputs down, host planning)
@@ -533,8 +523,8 @@ def main():
     e2.record(stream)
     torch.cuda.synchronize()
     barrier(world)
-    e2e_ms = max_over_ranks(s2.elapsed_time(e2), world)
-    e2e_bytes = sum_over_ranks(float(nb["total"] * e2e_steps), world)
+    e2e_ms = max_over_ranks(s2.elapsed_time(e2))
+    e2e_bytes = sum_over_ranks(float(nb["total"] * e2e_steps))
     e2e_value = e2e_bytes / (e2e_ms / 1e3) / 1e9
     assert ops.read_device_errors(device) == 0
 
@@ -546,7 +536,7 @@ def main():
         traffic = nb["self"] * float(traffic_info["dram_bytes_per_algorithmic_byte"])
 
     cb = None
-    if rank == 0 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:  # reported at N=1 only
         cb = cpu_baseline(args.batch, seconds=args.cpu_seconds, sample=args.cpu_sample)
         cb.pop("seconds_per_step", None)
         cb.pop("seconds_per_full_step", None)
