@@ -316,6 +316,7 @@ def engine_trace(reference_root: str, out_path: str):
                       max_decoder_len=w["max_decoder_len"])
             assert llm.config.block_size == 16
             params = SamplingParams(**w["params"])
+            effective = params.with_defaults(llm._sampling_params)
             outs = llm.generate([Request(r) for r in reqs], params, use_tqdm=False)
             tokens = [o.completion_token_ids for o in outs]
             hf_tokens = []
@@ -335,6 +336,9 @@ def engine_trace(reference_root: str, out_path: str):
             assert all(match), (tokens, hf_tokens)
             trace["runs"].append({
                 "name": w["name"], "config": {k: v for k, v in w.items() if k != "snapshot_calls"},
+                "sampling": {f: getattr(effective, f) for f in effective.__slots__},
+                "model_config": cfg.to_dict(),
+                "decoder_start_token_id": cfg.decoder_start_token_id,
                 "block_size": llm.config.block_size, "num_blocks": llm.config.num_blocks,
                 "num_cross_blocks": llm.config.num_cross_blocks,
                 "num_heads": 2, "head_dim": 64, "num_layers": cfg.decoder_layers,
@@ -343,6 +347,7 @@ def engine_trace(reference_root: str, out_path: str):
                 "clears": cur["clears"],
                 "attention_snapshots": snap["out"],
             })
+    trace["model_state"] = {k: v.clone() for k, v in hf.state_dict().items()}
     torch.save(trace, out_path)
     print(f"wrote {out_path}: {os.path.getsize(out_path)} bytes")
 

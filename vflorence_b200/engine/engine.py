@@ -1,0 +1,252 @@
+"""Continuous-batching decode engine on the paged path (one GPU).
+
+One step (the same order as the reference engine, vflorence/engine/llm_engine.py:57-63):
+  1. admit waiting requests while their beams fit in ``max_num_seqs``;
+  2. make room for every running sequence's next token (BlockManager; copy-on-write pairs);
+  3. encode the step's new requests (grouped by prompt length and image shape) and page their
+     encoder K/V into the cross pool, once per request;
+  4. copy-on-write copies (one launch), device-side step metadata (one upload, one kernel),
+     cross staging (memoised on the batch's request ids), then one decoder forward;
+  5. greedy argmax or beam candidates on the GPU; forks, finishes and frees on the host.
+"""
+
+from __future__ import annotations
+
+import math
+from collections import deque
+from dataclasses import dataclass, field
+
+import torch
+
+from ..block_manager import BlockManager
+from ..context import set_context
+from ..kv_cache import PagedKVCache
+from .model import PagedSeq2Seq
+from .sampling import LogitsRules, SamplingParams, select_beam_candidates
+
+
+@dataclass
+class Request:
+    input_ids: list[int]
+    pixel_values: torch.Tensor | None = None
+
+
+@dataclass(eq=False)
+class _Seq:
+    request_id: int
+    token_ids: list[int]
+    encoder_ids: list[int]
+    params: SamplingParams
+    pixel_values: torch.Tensor | None = None
+    block_table: list[int] = field(default_factory=list)
+    num_cached_tokens: int = 0
+    cum_logprob: float = 0.0
+    prompt_len: int = 1
+
+    @property
+    def num_generated(self) -> int:
+        return len(self.token_ids) - self.prompt_len
+
+    def finished(self, eos: set[int]) -> bool:
+        return self.token_ids[-1] in eos or self.num_generated >= self.params.max_tokens
+
+    def score(self) -> float:
+        return self.cum_logprob / (max(self.num_generated, 1) ** self.params.length_penalty)
+
+    def child(self, token: int, cum_logprob: float) -> "_Seq":
+        return _Seq(self.request_id, [*self.token_ids, token], self.encoder_ids, self.params,
+                    self.pixel_values, [], self.num_cached_tokens, cum_logprob, self.prompt_len)
+
+
+class Engine:
+    def __init__(self, hf_model, *, max_num_seqs: int, max_decoder_len: int, max_encoder_len: int,
+                 block_size: int = 16, num_blocks: int | None = None, decoder_start_token_id: int | None = None,
+                 record_steps: bool = False):
+        self.model = PagedSeq2Seq(hf_model)
+        m = self.model
+        self.device, self.dtype = m.device, m.dtype
+        self.block_size = block_size
+        self.max_num_seqs = max_num_seqs
+        self.max_decoder_len = max_decoder_len
+        self.max_encoder_len = max_encoder_len
+        self.num_blocks = num_blocks or max_num_seqs * math.ceil(max_decoder_len / block_size)
+        num_cross = max_num_seqs * math.ceil(max_encoder_len / block_size)
+        self.kv = PagedKVCache(num_layers=len(m.layers), num_heads=m.num_heads, head_dim=m.head_dim,
+                               block_size=block_size, num_blocks=self.num_blocks, num_cross_blocks=num_cross,
+                               dtype=self.dtype, device=self.device)
+        self.kv.bind(m.layers)
+        self.blocks = BlockManager(self.num_blocks, block_size)
+        cfg = hf_model.config.get_text_config()
+        self.start_token = cfg.decoder_start_token_id if decoder_start_token_id is None else decoder_start_token_id
+        self.waiting: deque[_Seq] = deque()
+        self.running: list[_Seq] = []
+        self.finished_beams: dict[int, list[_Seq]] = {}
+        self.outputs: dict[int, list[int]] = {}
+        self._next_id = 0
+        self._rules: tuple[SamplingParams, LogitsRules] | None = None
+        self.record = [] if record_steps else None
+
+    # -------------------------------------------------------------------------------- requests
+    def add_request(self, request: Request, params: SamplingParams) -> int:
+        if len(request.input_ids) > self.max_encoder_len:
+            raise ValueError(f"encoder prompt has {len(request.input_ids)} tokens (max {self.max_encoder_len})")
+        if params.max_tokens > self.max_decoder_len:
+            raise ValueError(f"max_tokens {params.max_tokens} exceeds max_decoder_len {self.max_decoder_len}")
+        if params.num_beams > self.max_num_seqs:
+            raise ValueError("num_beams exceeds max_num_seqs")
+        if self.waiting or self.running:
+            other = (self.waiting or self.running)[0].params
+            if other != params:
+                raise ValueError("all active requests must share the same SamplingParams")
+        rid = self._next_id
+        self._next_id += 1
+        self.waiting.append(_Seq(rid, [self.start_token], list(request.input_ids), params, request.pixel_values))
+        return rid
+
+    def is_finished(self) -> bool:
+        return not self.waiting and not self.running
+
+    @torch.inference_mode()
+    def generate(self, requests, params: SamplingParams) -> list[list[int]]:
+        ids = [self.add_request(r, params) for r in requests]
+        try:
+            while not self.is_finished():
+                self.step()
+        except BaseException:
+            self.abort()
+            raise
+        return [self.outputs.pop(i) for i in ids]
+
+    def abort(self) -> None:
+        self.waiting.clear()
+        self.running.clear()
+        self.finished_beams.clear()
+        self.blocks.reset()
+        self.kv.reset()
+        set_context()
+
+    # ------------------------------------------------------------------------------------ step
+    @torch.inference_mode()
+    def step(self) -> list[int]:
+        seqs, copies = self._schedule()
+        if not seqs:
+            return []
+        fresh = [s for s in seqs if s.num_cached_tokens == 0]
+        if fresh:
+            self._encode(fresh)
+        self.kv.copy_blocks(copies)
+        tables = [s.block_table for s in seqs]
+        positions = [s.num_cached_tokens for s in seqs]
+        if self.record is not None:
+            self.record.append({"request_ids": [s.request_id for s in seqs], "positions": list(positions),
+                                "block_tables": [list(t) for t in tables], "copies": list(copies)})
+        st = self.kv.prepare_decode(tables, positions)
+        staged = self.kv.stage_cross(self.model.layers, [s.request_id for s in seqs])
+        set_context(context_lens=st.context_lens, block_tables=st.block_tables, slot_mapping=st.slot_mapping,
+                    query_start_loc=st.query_start_loc, self_metadata=st.self_metadata, isa=self.kv.isa,
+                    cross_staged=staged)
+        try:
+            ids = torch.tensor([s.token_ids[-1] for s in seqs], dtype=torch.long).pin_memory()
+            logits = self.model.decode(ids.to(self.device, non_blocking=True), st.positions.long())
+        finally:
+            set_context()
+        for s in seqs:
+            s.num_cached_tokens += 1
+        if seqs[0].params.num_beams == 1:
+            return self._finish_greedy(seqs, logits)
+        return self._finish_beam(seqs, logits)
+
+    def _schedule(self):
+        used = sum({s.request_id: s.params.num_beams for s in self.running}.values())
+        while self.waiting and used + self.waiting[0].params.num_beams <= self.max_num_seqs:
+            s = self.waiting.popleft()
+            self.running.append(s)
+            used += s.params.num_beams
+        seqs = list(self.running)
+        if self.blocks.required_new_blocks(seqs) > self.blocks.num_free_blocks:
+            raise RuntimeError("KV cache is full; increase num_blocks")
+        copies = [c for s in seqs if (c := self.blocks.ensure_capacity(s)) is not None]
+        return seqs, copies
+
+    def _encode(self, fresh) -> None:
+        groups: dict = {}
+        for s in fresh:
+            key = (len(s.encoder_ids), None if s.pixel_values is None else tuple(s.pixel_values.shape))
+            groups.setdefault(key, []).append(s)
+        for (enc_len, px), group in groups.items():
+            ids = torch.tensor([s.encoder_ids for s in group], dtype=torch.long).to(self.device)
+            pix = None
+            if px is not None:
+                pix = torch.stack([s.pixel_values for s in group]).to(self.device)
+            hidden = self.model.encode(ids, pix)
+            slots = self.kv.page_requests([s.request_id for s in group], enc_len)
+            for layer in range(len(self.model.layers)):
+                k, v = self.model.cross_kv(layer, hidden)
+                self.kv.write_encoder_kv(layer, k, v, slots)
+
+    def _rules_for(self, params: SamplingParams) -> LogitsRules:
+        if self._rules is None or self._rules[0] is not params:
+            self._rules = (params, LogitsRules(params, self.model.vocab_size, self.device))
+        return self._rules[1]
+
+    def _finish(self, seq: _Seq, tokens: list[int]) -> None:
+        self.outputs[seq.request_id] = tokens
+        self.kv.clear_request(seq.request_id)
+
+    def _remove(self, seq: _Seq) -> None:
+        self.running.remove(seq)
+        self.blocks.deallocate(seq)
+
+    def _finish_greedy(self, seqs, logits) -> list[int]:
+        params = seqs[0].params
+        rules = self._rules_for(params)
+        scores = rules(logits.float(), [s.token_ids for s in seqs])
+        picks = scores.argmax(dim=-1).tolist()
+        eos = set(params.eos_ids())
+        done = []
+        for s, t in zip(seqs, picks):
+            s.token_ids.append(t)
+            if s.finished(eos):
+                self._remove(s)
+                self._finish(s, s.token_ids[s.prompt_len:])
+                done.append(s.request_id)
+        return done
+
+    def _finish_beam(self, seqs, logits) -> list[int]:
+        params = seqs[0].params
+        rules = self._rules_for(params)
+        scores = rules(torch.log_softmax(logits.float(), dim=-1), [s.token_ids for s in seqs])
+        keep = params.beams_to_keep()
+        top_s, top_i = torch.topk(scores, min(keep, scores.shape[-1]), dim=-1)
+        top_s += torch.tensor([s.cum_logprob for s in seqs], dtype=torch.float32, device=self.device).unsqueeze(-1)
+        cands = select_beam_candidates(seqs, top_s.tolist(), top_i.tolist(), keep)
+        eos = set(params.eos_ids())
+        nb = params.num_beams
+        done = []
+        for rid, cand in cands.items():
+            finished = self.finished_beams.setdefault(rid, [])
+            running = []
+            for rank, (row, token, cum) in enumerate(cand):
+                if rank >= nb and len(running) >= nb:
+                    break
+                child = seqs[row].child(token, cum)
+                if child.finished(eos):
+                    if rank < nb:
+                        finished.append(child)
+                elif len(running) < nb:
+                    running.append((seqs[row], child))
+            finished.sort(key=lambda c: c.score(), reverse=True)
+            del finished[nb:]
+            best_running = max((c.score() for _, c in running), default=float("-inf"))
+            stop = len(finished) >= nb and (params.early_stopping or finished[-1].score() >= best_running)
+            if not running or stop:
+                self.finished_beams.pop(rid, None)
+                self._finish(finished[0], finished[0].token_ids[finished[0].prompt_len:])
+                done.append(rid)
+            else:
+                for parent, child in running:
+                    self.blocks.fork(parent, child)
+                    self.running.append(child)
+        for s in seqs:
+            self._remove(s)
+        return done

@@ -1,0 +1,112 @@
+"""An encoder-decoder model on the paged path.
+
+Wraps a HuggingFace transformers BART-family model (``BartForConditionalGeneration``, or the
+language model inside ``Florence2ForConditionalGeneration``). The encoder, the vision tower and
+every projection run as stock torch modules on the GPU. The decoder is re-driven one token per
+sequence: its self-attention goes through ``vflorence::self_attention`` (KV append + paged
+decode) and its cross-attention through ``vflorence::cross_attention`` (paged encoder K/V), the
+ops the reference's decoder calls (vflorence/models/bart.py:106-146). The q/k/v projections of
+each decoder layer are fused into one GEMM and the encoder k/v projections into another, and the
+kernels take the strided q/k/v views of the fused outputs directly.
+"""
+
+from __future__ import annotations
+
+from types import SimpleNamespace
+
+import torch
+import torch.nn.functional as F
+from transformers.activations import ACT2FN
+
+from ..attention import decoder_cross_attention, decoder_self_attention
+
+
+class _Layer:
+    """One decoder layer's weights, plus the attribute slots PagedKVCache.bind fills."""
+
+    def __init__(self, hf_layer):
+        sa, ca = hf_layer.self_attn, hf_layer.encoder_attn
+        cat = lambda *ms: torch.cat([m.weight for m in ms], 0)  # noqa: E731
+        catb = lambda *ms: torch.cat([m.bias for m in ms], 0) if ms[0].bias is not None else None  # noqa: E731
+        self.w_qkv, self.b_qkv = cat(sa.q_proj, sa.k_proj, sa.v_proj), catb(sa.q_proj, sa.k_proj, sa.v_proj)
+        self.self_out = sa.out_proj
+        self.ln_self = hf_layer.self_attn_layer_norm
+        self.cross_q = ca.q_proj
+        self.w_kv, self.b_kv = cat(ca.k_proj, ca.v_proj), catb(ca.k_proj, ca.v_proj)
+        self.cross_out = ca.out_proj
+        self.ln_cross = hf_layer.encoder_attn_layer_norm
+        self.fc1, self.fc2 = hf_layer.fc1, hf_layer.fc2
+        self.ln_final = hf_layer.final_layer_norm
+        self.self_attn = SimpleNamespace(k_cache=None, v_cache=None)
+        self.encoder_attn = SimpleNamespace(k_cache=None, v_cache=None)
+
+
+class PagedSeq2Seq:
+    def __init__(self, hf_model):
+        cfg = hf_model.config
+        self.is_florence2 = cfg.model_type == "florence2"
+        lm_cfg = cfg.get_text_config()
+        self.hf = hf_model
+        lm = hf_model.model.language_model if self.is_florence2 else hf_model.model
+        self.lm = lm
+        dec = lm.decoder
+        self.embed_tokens = dec.embed_tokens
+        self.pos_weight = dec.embed_positions.weight
+        self.pos_offset = getattr(dec.embed_positions, "offset", 2)
+        self.ln_embed = dec.layernorm_embedding
+        self.layers = [_Layer(layer) for layer in dec.layers]
+        self.num_heads = lm_cfg.decoder_attention_heads
+        self.d_model = lm_cfg.d_model
+        self.head_dim = self.d_model // self.num_heads
+        self.scale = self.head_dim ** -0.5
+        for L in self.layers:
+            for attn in (L.self_attn, L.encoder_attn):
+                attn.num_heads, attn.head_dim = self.num_heads, self.head_dim
+        self.act = ACT2FN[lm_cfg.activation_function]
+        self.lm_head = hf_model.lm_head
+        self.final_logits_bias = getattr(hf_model, "final_logits_bias", None)
+        self.vocab_size = self.lm_head.out_features
+        self.dtype = self.pos_weight.dtype
+        self.device = self.pos_weight.device
+        self.image_token_id = getattr(cfg, "image_token_id", None)
+
+    # ------------------------------------------------------------------------------- encoder
+    @torch.inference_mode()
+    def encode(self, input_ids: torch.Tensor, pixel_values: torch.Tensor | None = None) -> torch.Tensor:
+        """Encoder hidden states [G, S, d_model] for a group of equal-length prompts."""
+        if pixel_values is None:
+            return self.lm.encoder(input_ids=input_ids).last_hidden_state
+        feats = self.hf.model.get_image_features(pixel_values.to(self.dtype)).pooler_output
+        embeds = self.lm.get_input_embeddings()(input_ids)
+        mask = (input_ids == self.image_token_id).unsqueeze(-1).expand_as(embeds)
+        embeds = embeds.masked_scatter(mask, feats.to(embeds.dtype))
+        return self.lm.encoder(inputs_embeds=embeds).last_hidden_state
+
+    def cross_kv(self, layer: int, hidden: torch.Tensor):
+        """Encoder K/V of one decoder layer as [G*S, H, head_dim] views of one fused GEMM."""
+        L = self.layers[layer]
+        kv = F.linear(hidden.reshape(-1, self.d_model), L.w_kv, L.b_kv)
+        k, v = kv.chunk(2, dim=-1)
+        shape = (kv.shape[0], self.num_heads, self.head_dim)
+        return k.reshape(shape), v.reshape(shape)
+
+    # ------------------------------------------------------------------------------- decoder
+    @torch.inference_mode()
+    def decode(self, input_ids: torch.Tensor, positions: torch.Tensor) -> torch.Tensor:
+        """One decoder step: logits [B, vocab] for one new token per sequence. The per-step
+        Context (slot mapping, block tables, cross staging) must be set."""
+        B = input_ids.shape[0]
+        h = self.embed_tokens(input_ids) + F.embedding(positions + self.pos_offset, self.pos_weight)
+        h = self.ln_embed(h)
+        shape = (B, self.num_heads, self.head_dim)
+        for i, L in enumerate(self.layers):
+            q, k, v = (t.reshape(shape) for t in F.linear(h, L.w_qkv, L.b_qkv).chunk(3, dim=-1))
+            a = decoder_self_attention(q, k, v, L.self_attn.k_cache, L.self_attn.v_cache, self.scale)
+            h = L.ln_self(h + L.self_out(a.reshape(B, self.d_model)))
+            c = decoder_cross_attention(L.cross_q(h).reshape(shape), i, self.scale)
+            h = L.ln_cross(h + L.cross_out(c.reshape(B, self.d_model)))
+            h = L.ln_final(h + L.fc2(self.act(L.fc1(h))))
+        logits = self.lm_head(h)
+        if self.final_logits_bias is not None:
+            logits = logits + self.final_logits_bias
+        return logits

@@ -1,0 +1,160 @@
+"""Decoding rules of the engine: transformers' logits rules and beam bookkeeping, restated.
+
+The decisions must equal the reference engine's (vflorence/layers/logits_processor.py,
+vflorence/engine/model_runner.py:343-410, vflorence/engine/scheduler.py:83-127), which follow
+HuggingFace ``generate``:
+
+* rules, in this order: repetition penalty, no-repeat n-gram ban, minimum length (EOS banned
+  while the decoder sequence is shorter than ``min_length``), forced BOS at the first generated
+  position, forced EOS at the last one, token suppression, begin-suppression at the first
+  generated position. Lengths count the decoder start token.
+* greedy: argmax of the processed logits.
+* beam search: processed log-probs, top ``K = max(2, 1 + #eos) * num_beams`` per row plus the
+  row's cumulative log-prob, a request's rows merged and sorted (stable) by score, the best K
+  kept. A candidate ending in EOS (or reaching max_tokens) is finished only when its rank is
+  below num_beams; at most num_beams continue. Finished hypotheses are ranked by
+  ``cum_logprob / max(generated, 1) ** length_penalty``; a request stops when nothing runs, or
+  when num_beams hypotheses are finished and either early_stopping is set or the worst kept
+  finished score beats the best running one.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+
+import torch
+
+NEG_INF = float("-inf")
+
+
+@dataclass
+class SamplingParams:
+    max_tokens: int = 64
+    num_beams: int = 1
+    repetition_penalty: float = 1.0
+    eos_token_id: int | list[int] | None = None
+    length_penalty: float = 1.0
+    no_repeat_ngram_size: int = 0
+    min_length: int = 0
+    forced_bos_token_id: int | None = None
+    forced_eos_token_id: int | list[int] | None = None
+    suppress_tokens: list[int] | None = None
+    begin_suppress_tokens: list[int] | None = None
+    early_stopping: bool = False
+    extra: dict = field(default_factory=dict)
+
+    def __post_init__(self):
+        if type(self.max_tokens) is not int or self.max_tokens < 1:
+            raise ValueError("max_tokens must be an integer >= 1")
+        if type(self.num_beams) is not int or self.num_beams < 1:
+            raise ValueError("num_beams must be an integer >= 1")
+        if self.no_repeat_ngram_size < 0 or self.min_length < 0:
+            raise ValueError("no_repeat_ngram_size and min_length must be >= 0")
+        if not self.repetition_penalty > 0:
+            raise ValueError("repetition_penalty must be positive")
+
+    @classmethod
+    def from_dict(cls, d: dict) -> "SamplingParams":
+        known = {f for f in cls.__dataclass_fields__ if f != "extra"}
+        return cls(**{k: v for k, v in d.items() if k in known and v is not None})
+
+    def eos_ids(self) -> list[int]:
+        e = self.eos_token_id
+        if e is None:
+            return []
+        return [e] if isinstance(e, int) else sorted(set(e))
+
+    def beams_to_keep(self) -> int:
+        return max(2, 1 + len(self.eos_ids())) * self.num_beams
+
+
+def _as_list(x):
+    if x is None:
+        return []
+    return [x] if isinstance(x, int) else list(x)
+
+
+class LogitsRules:
+    """Applies the enabled rules to a [rows, vocab] float tensor in place."""
+
+    def __init__(self, params: SamplingParams, vocab_size: int, device):
+        self.p = params
+        self.vocab = vocab_size
+        self.max_length = 1 + params.max_tokens      # decoder start token + generated tokens
+        self.begin_index = 1 + int(params.forced_bos_token_id is not None)
+        keep = lambda ids: [i for i in ids if 0 <= i < vocab_size]  # noqa: E731
+        self.eos = torch.tensor(keep(params.eos_ids()), dtype=torch.long, device=device)
+        self.suppress = torch.tensor(keep(_as_list(params.suppress_tokens)), dtype=torch.long, device=device)
+        self.begin_suppress = torch.tensor(keep(_as_list(params.begin_suppress_tokens)), dtype=torch.long,
+                                           device=device)
+        self.forced_bos = keep(_as_list(params.forced_bos_token_id))
+        self.forced_eos = keep(_as_list(params.forced_eos_token_id))
+        self.needs_history = params.repetition_penalty != 1.0 or params.no_repeat_ngram_size > 0
+
+    def __call__(self, scores: torch.Tensor, histories: list[list[int]]) -> torch.Tensor:
+        p = self.p
+        lengths = [len(h) for h in histories]
+        hist = None
+        if self.needs_history:
+            width = max(lengths)
+            hist = torch.tensor([[-1] * (width - len(h)) + h for h in histories], dtype=torch.long,
+                                device=scores.device)
+        if p.repetition_penalty != 1.0:  # every token already in the row's history (not padding)
+            rows, cols = torch.where(hist >= 0)
+            tokens = hist[rows, cols]
+            seen = scores[rows, tokens]
+            scores[rows, tokens] = torch.where(seen < 0, seen * p.repetition_penalty,
+                                               seen / p.repetition_penalty)
+        if p.no_repeat_ngram_size > 0:
+            self._ban_repeated_ngrams(scores, hist, lengths)
+        if p.min_length > 0 and self.eos.numel():
+            rows = [i for i, n in enumerate(lengths) if n < p.min_length]
+            if rows:
+                r = torch.tensor(rows, device=scores.device)
+                scores[r.unsqueeze(1), self.eos.unsqueeze(0)] = NEG_INF
+        if self.forced_bos:
+            self._force(scores, [i for i, n in enumerate(lengths) if n == 1], self.forced_bos)
+        if self.forced_eos:
+            self._force(scores, [i for i, n in enumerate(lengths) if n == self.max_length - 1], self.forced_eos)
+        if self.suppress.numel():
+            scores[:, self.suppress] = NEG_INF
+        if self.begin_suppress.numel():
+            rows = [i for i, n in enumerate(lengths) if n == self.begin_index]
+            if rows:
+                r = torch.tensor(rows, device=scores.device)
+                scores[r.unsqueeze(1), self.begin_suppress.unsqueeze(0)] = NEG_INF
+        return scores
+
+    @staticmethod
+    def _force(scores, rows, ids):
+        """Make ``ids`` the only choice of each row in ``rows``: score 0 for them, -inf else."""
+        if not rows:
+            return
+        r = torch.tensor(rows, device=scores.device)
+        scores[r] = NEG_INF
+        scores[r.unsqueeze(1), torch.tensor(ids, device=scores.device).unsqueeze(0)] = 0.0
+
+    def _ban_repeated_ngrams(self, scores, hist, lengths):
+        n = self.p.no_repeat_ngram_size
+        width = hist.shape[1]
+        if width < n:
+            return
+        windows = hist.unfold(1, n, 1)                 # [rows, width - n + 1, n]
+        tail = hist[:, width - (n - 1):] if n > 1 else hist[:, :0]
+        match = (windows[:, :, : n - 1] == tail.unsqueeze(1)).all(-1) & (windows >= 0).all(-1)
+        ok = torch.tensor([ln + 1 >= n for ln in lengths], device=scores.device)
+        match &= ok.unsqueeze(1)
+        rows, cols = match.nonzero(as_tuple=True)
+        if rows.numel():
+            scores[rows, windows[rows, cols, n - 1]] = NEG_INF
+
+
+def select_beam_candidates(seqs, top_scores, top_ids, keep: int):
+    """Per request: its rows' (row, token, score) candidates, best ``keep`` first (stable)."""
+    by_req: dict[int, list] = {}
+    for row, (seq, scores, ids) in enumerate(zip(seqs, top_scores, top_ids)):
+        by_req.setdefault(seq.request_id, []).extend((row, t, s) for t, s in zip(ids, scores))
+    for cands in by_req.values():
+        cands.sort(key=lambda c: c[2], reverse=True)
+        del cands[keep:]
+    return by_req
