@@ -371,6 +371,127 @@ def run_sweep(args):
             del c, kc, vc
 
 
+# ---------------------------------------------------------------------------- decode (engine)
+
+def decode_config(name: str):
+    """model shape, dtype, sampling and synthetic requests."""
+    from transformers import BartConfig
+
+    bart_large = dict(vocab_size=50265, d_model=1024, encoder_layers=12, decoder_layers=12,
+                      encoder_attention_heads=16, decoder_attention_heads=16, encoder_ffn_dim=4096,
+                      decoder_ffn_dim=4096, max_position_embeddings=1024, activation_function="gelu",
+                      decoder_start_token_id=2, eos_token_id=2, bos_token_id=0, pad_token_id=1,
+                      init_std=0.02)
+    if name == "cfg1":
+        return dict(kind="bart", text=bart_large, dtype=torch.float32, num_requests=8, lens=(200, 1000),
+                    ids=(4, 50264), id_seed=0, params=dict(max_tokens=64, num_beams=1, eos_token_id=[]),
+                    max_num_seqs=8, max_decoder_len=64, max_encoder_len=1000)
+    if name == "cfg2":
+        return dict(kind="bart", text=bart_large, dtype=torch.bfloat16, num_requests=32, lens=(300, 1024),
+                    ids=(4, 50264), id_seed=1,
+                    params=dict(max_tokens=142, num_beams=4, length_penalty=2.0, no_repeat_ngram_size=3,
+                                eos_token_id=[]),
+                    max_num_seqs=128, max_decoder_len=144, max_encoder_len=1024)
+    florence_text = dict(bart_large, vocab_size=51290)
+    if name == "cfg3":
+        text = dict(florence_text, d_model=768, encoder_layers=6, decoder_layers=6, encoder_attention_heads=12,
+                    decoder_attention_heads=12, encoder_ffn_dim=3072, decoder_ffn_dim=3072)
+        vision = dict(embed_dim=[128, 256, 512, 1024], num_heads=[4, 8, 16, 32], num_groups=[4, 8, 16, 32],
+                      depths=[1, 1, 9, 1], projection_dim=768)
+        return dict(kind="florence2", text=text, vision=vision, dtype=torch.bfloat16, num_requests=64,
+                    prompt=(3, 10), ids=(4, 51289), id_seed=3,
+                    params=dict(max_tokens=256, num_beams=3, eos_token_id=[]),
+                    max_num_seqs=192, max_decoder_len=256, max_encoder_len=592)
+    if name == "cfg4":
+        vision = dict(embed_dim=[256, 512, 1024, 2048], num_heads=[8, 16, 32, 64], num_groups=[8, 16, 32, 64],
+                      depths=[1, 1, 9, 1], projection_dim=1024)
+        return dict(kind="florence2", text=florence_text, vision=vision, dtype=torch.bfloat16, num_requests=512,
+                    prompt=(3, 10), ids=(4, 51289), id_seed=4,
+                    params=dict(max_tokens=256, num_beams=3, eos_token_id=[]),
+                    max_num_seqs=256, max_decoder_len=1024, max_encoder_len=592)
+    raise ValueError(name)
+
+
+def build_decode_model(cfg, device):
+    from transformers import BartConfig, BartForConditionalGeneration
+
+    torch.manual_seed(0)
+    with torch.device(device):
+        if cfg["kind"] == "bart":
+            model = BartForConditionalGeneration(BartConfig(**cfg["text"]))
+        else:
+            from transformers import Florence2Config, Florence2ForConditionalGeneration
+
+            fc = Florence2Config(text_config=cfg["text"], vision_config=cfg["vision"], image_token_id=51289)
+            model = Florence2ForConditionalGeneration(fc)
+    return model.to(cfg["dtype"]).eval()
+
+
+def decode_requests(cfg, device):
+    from vflorence_b200.engine import Request
+
+    g = torch.Generator().manual_seed(cfg["id_seed"])
+    reqs = []
+    for i in range(cfg["num_requests"]):
+        if cfg["kind"] == "bart":
+            n = int(torch.randint(cfg["lens"][0], cfg["lens"][1] + 1, (1,), generator=g))
+            reqs.append(Request(torch.randint(*cfg["ids"], (n,), generator=g).tolist()))
+        else:
+            n = int(torch.randint(cfg["prompt"][0], cfg["prompt"][1] + 1, (1,), generator=g))
+            prompt = torch.randint(*cfg["ids"], (n,), generator=g).tolist()
+            px = torch.randn(3, 768, 768, generator=g)
+            reqs.append(Request([51289] * cfg["image_tokens"] + prompt, px))
+    return reqs
+
+
+def run_decode(args):
+    """End-to-end decode tokens/s of the engine around the paged path on one BASELINE config:
+    completion tokens of all requests / wall time of the whole job (max over ranks). Synthetic:
+    random-init weights of the config's shape, seeded ids and N(0,1) images; EOS is disabled so
+    every request decodes exactly max_tokens tokens (random weights have no natural stop)."""
+    from vflorence_b200.engine import Engine, SamplingParams
+    from vflorence_b200.sharding import assign_requests, max_over_ranks, sum_over_ranks
+
+    world, rank, local = dist_setup()
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    cfg = decode_config(args.decode)
+    model = build_decode_model(cfg, device)
+    if cfg["kind"] == "florence2":
+        with torch.inference_mode():
+            px = torch.zeros(1, 3, 768, 768, device=device, dtype=cfg["dtype"])
+            cfg["image_tokens"] = model.model.get_image_features(px).pooler_output.shape[1]
+    reqs = decode_requests(cfg, device)
+    costs = [len(r.input_ids) + cfg["params"]["num_beams"] * cfg["params"]["max_tokens"] for r in reqs]
+    mine = [reqs[i] for i in assign_requests(costs, world)[rank]]
+    params = SamplingParams.from_dict(cfg["params"])
+    eng = Engine(model, max_num_seqs=cfg["max_num_seqs"], max_decoder_len=cfg["max_decoder_len"],
+                 max_encoder_len=cfg["max_encoder_len"], block_size=BS)
+    # warm-up on a few of this rank's requests (allocator, library set-up)
+    eng.generate(mine[: max(1, min(2, len(mine)))], SamplingParams.from_dict(dict(cfg["params"], max_tokens=4)))
+    barrier(world)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    outs = eng.generate(mine, params)
+    torch.cuda.synchronize()
+    elapsed = time.perf_counter() - t0
+    barrier(world)
+    tokens = sum(len(o) for o in outs)
+    total_tokens = sum_over_ranks(float(tokens))
+    wall = max_over_ranks(elapsed)
+    if rank == 0:
+        print(json.dumps({"metric": "decode tokens/s", "config": args.decode, "value": total_tokens / wall,
+                          "unit": "tokens/s", "n_gpus": world, "requests": cfg["num_requests"],
+                          "completion_tokens": int(total_tokens), "wall_s": wall,
+                          "params": cfg["params"], "dtype": str(cfg["dtype"]).replace("torch.", ""),
+                          "max_num_seqs": cfg["max_num_seqs"], "data": "synthetic (random-init weights)"}),
+              flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
 # -------------------------------------------------------------------------------------- main
 
 def dist_setup():
@@ -428,10 +549,15 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--sweep", action="store_true", help="BASELINE config-5 batch sweep, one line per point")
     ap.add_argument("--sweep-batches", default="1,2,4,8,16,32,64,128,256,512,1024")
+    ap.add_argument("--decode", choices=["cfg1", "cfg2", "cfg3", "cfg4"], default=None,
+                    help="end-to-end decode tokens/s of the engine on a BASELINE config")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.sweep:
         run_sweep(args)
+        return
+    if args.decode:
+        run_decode(args)
         return
 
     if args.impl == "reference":

@@ -88,6 +88,9 @@ class Engine:
 
     # -------------------------------------------------------------------------------- requests
     def add_request(self, request: Request, params: SamplingParams) -> int:
+        vocab = self.model.lm.get_input_embeddings().num_embeddings
+        if any(not 0 <= t < vocab for t in request.input_ids):
+            raise ValueError(f"encoder prompt holds token ids outside [0, {vocab})")
         if len(request.input_ids) > self.max_encoder_len:
             raise ValueError(f"encoder prompt has {len(request.input_ids)} tokens (max {self.max_encoder_len})")
         if params.max_tokens > self.max_decoder_len:
