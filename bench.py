@@ -466,9 +466,12 @@ def run_decode(args):
     mine = [reqs[i] for i in assign_requests(costs, world)[rank]]
     params = SamplingParams.from_dict(cfg["params"])
     eng = Engine(model, max_num_seqs=cfg["max_num_seqs"], max_decoder_len=cfg["max_decoder_len"],
-                 max_encoder_len=cfg["max_encoder_len"], block_size=BS)
-    # warm-up on a few of this rank's requests (allocator, library set-up)
+                 max_encoder_len=cfg["max_encoder_len"], block_size=BS, cuda_graphs=not args.eager)
+    # warm-up on a few of this rank's requests (allocator, library set-up); graphs for every
+    # batch size this run can reach are captured up front, as a server does at start-up
     eng.generate(mine[: max(1, min(2, len(mine)))], SamplingParams.from_dict(dict(cfg["params"], max_tokens=4)))
+    if eng.graphs is not None:
+        eng.graphs.capture(min(cfg["max_num_seqs"], len(mine) * params.num_beams), params.num_beams)
     barrier(world)
     torch.cuda.synchronize()
     t0 = time.perf_counter()
@@ -484,7 +487,8 @@ def run_decode(args):
                           "unit": "tokens/s", "n_gpus": world, "requests": cfg["num_requests"],
                           "completion_tokens": int(total_tokens), "wall_s": wall,
                           "params": cfg["params"], "dtype": str(cfg["dtype"]).replace("torch.", ""),
-                          "max_num_seqs": cfg["max_num_seqs"], "data": "synthetic (random-init weights)"}),
+                          "max_num_seqs": cfg["max_num_seqs"], "cuda_graphs": not args.eager,
+                          "data": "synthetic (random-init weights)"}),
               flush=True)
     if world > 1:
         import torch.distributed as dist
@@ -551,6 +555,7 @@ def main():
     ap.add_argument("--sweep-batches", default="1,2,4,8,16,32,64,128,256,512,1024")
     ap.add_argument("--decode", choices=["cfg1", "cfg2", "cfg3", "cfg4"], default=None,
                     help="end-to-end decode tokens/s of the engine on a BASELINE config")
+    ap.add_argument("--eager", action="store_true", help="decode without CUDA graphs")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.sweep:

@@ -171,6 +171,7 @@ int vfl_copy_blocks(void* const* k_caches, void* const* v_caches, int num_layers
  *     slot_mapping[b] = block_table[b, p // block_size] * block_size + p % block_size
  *     context_lens[b] = p + 1
  *     query_start_loc[b] = b  (and query_start_loc[num_seqs] = num_seqs)
+ *   A negative position marks a padding row (fixed-size batches): slot -1, context length 0.
  *   Any output pointer may be NULL. */
 int vfl_prepare_decode(const int32_t* block_table, int64_t table_stride, int32_t table_cols,
                        const int32_t* positions, int num_seqs, int block_size,

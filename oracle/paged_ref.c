@@ -210,9 +210,14 @@ void oracle_prepare_decode(const int32_t* block_table, int64_t table_stride,
                            int32_t* query_start_loc) {
   for (int b = 0; b < num_seqs; ++b) {
     const int32_t pos = positions[b];
+    query_start_loc[b] = b;
+    if (pos < 0) { /* padding row */
+      slot_mapping[b] = -1;
+      context_lens[b] = 0;
+      continue;
+    }
     slot_mapping[b] = (int64_t)block_table[(int64_t)b * table_stride + pos / block_size] * block_size + pos % block_size;
     context_lens[b] = pos + 1;
-    query_start_loc[b] = b;
   }
   query_start_loc[num_seqs] = num_seqs;
 }

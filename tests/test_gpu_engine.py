@@ -30,8 +30,9 @@ def hf_model(engine_trace):
     return _hf_model(engine_trace)
 
 
+@pytest.mark.parametrize("graphs", [False, True], ids=["eager", "cuda_graphs"])
 @pytest.mark.parametrize("run_name", ["greedy", "beam2", "beam4"])
-def test_engine_replays_reference(engine_trace, hf_model, run_name):
+def test_engine_replays_reference(engine_trace, hf_model, run_name, graphs):
     from vflorence_b200.engine import Engine, Request, SamplingParams
 
     run = next(r for r in engine_trace["runs"] if r["name"] == run_name)
@@ -39,7 +40,7 @@ def test_engine_replays_reference(engine_trace, hf_model, run_name):
     params = SamplingParams.from_dict(run["sampling"])
     eng = Engine(hf_model, max_num_seqs=cfg["max_num_seqs"], max_decoder_len=cfg["max_decoder_len"],
                  max_encoder_len=hf_model.config.max_position_embeddings, block_size=16,
-                 num_blocks=run["num_blocks"], record_steps=True)
+                 num_blocks=run["num_blocks"], record_steps=True, cuda_graphs=graphs)
     assert eng.kv.num_cross_blocks == run["num_cross_blocks"]
     tokens = eng.generate([Request(r) for r in run["requests"]], params)
     assert tokens == run["tokens"]

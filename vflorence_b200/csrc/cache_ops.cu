@@ -90,9 +90,14 @@ __global__ void prepare_decode_kernel(const int32_t* __restrict__ table, int64_t
   if (b == num_seqs) return;
   const int32_t pos = positions[b];
   const int32_t col = pos / block_size;
+  if (pos < 0) {  // padding row of a fixed-size batch: nothing to append, nothing to attend
+    if (context_lens != nullptr) context_lens[b] = 0;
+    if (slot_mapping != nullptr) slot_mapping[b] = -1;
+    return;
+  }
   if (context_lens != nullptr) context_lens[b] = pos + 1;
   if (slot_mapping != nullptr) {
-    if (pos < 0 || col >= table_cols) {
+    if (col >= table_cols) {
       report(err, VFL_DEVERR_CONTEXT);
       slot_mapping[b] = -1;  // the append then skips this token
     } else {

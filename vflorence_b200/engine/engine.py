@@ -61,7 +61,7 @@ class _Seq:
 class Engine:
     def __init__(self, hf_model, *, max_num_seqs: int, max_decoder_len: int, max_encoder_len: int,
                  block_size: int = 16, num_blocks: int | None = None, decoder_start_token_id: int | None = None,
-                 record_steps: bool = False):
+                 record_steps: bool = False, cuda_graphs: bool = False):
         self.model = PagedSeq2Seq(hf_model)
         m = self.model
         self.device, self.dtype = m.device, m.dtype
@@ -85,6 +85,11 @@ class Engine:
         self._next_id = 0
         self._rules: tuple[SamplingParams, LogitsRules] | None = None
         self.record = [] if record_steps else None
+        self.graphs = None
+        if cuda_graphs:
+            from .graphs import GraphedDecoder
+
+            self.graphs = GraphedDecoder(self)
 
     # -------------------------------------------------------------------------------- requests
     def add_request(self, request: Request, params: SamplingParams) -> int:
@@ -143,16 +148,18 @@ class Engine:
         if self.record is not None:
             self.record.append({"request_ids": [s.request_id for s in seqs], "positions": list(positions),
                                 "block_tables": [list(t) for t in tables], "copies": list(copies)})
-        st = self.kv.prepare_decode(tables, positions)
-        staged = self.kv.stage_cross(self.model.layers, [s.request_id for s in seqs])
-        set_context(context_lens=st.context_lens, block_tables=st.block_tables, slot_mapping=st.slot_mapping,
-                    query_start_loc=st.query_start_loc, self_metadata=st.self_metadata, isa=self.kv.isa,
-                    cross_staged=staged)
-        try:
-            ids = torch.tensor([s.token_ids[-1] for s in seqs], dtype=torch.long).pin_memory()
-            logits = self.model.decode(ids.to(self.device, non_blocking=True), st.positions.long())
-        finally:
-            set_context()
+        logits = self.graphs.run(seqs) if self.graphs is not None else None
+        if logits is None:  # eager step
+            st = self.kv.prepare_decode(tables, positions)
+            staged = self.kv.stage_cross(self.model.layers, [s.request_id for s in seqs])
+            set_context(context_lens=st.context_lens, block_tables=st.block_tables, slot_mapping=st.slot_mapping,
+                        query_start_loc=st.query_start_loc, self_metadata=st.self_metadata, isa=self.kv.isa,
+                        cross_staged=staged)
+            try:
+                ids = torch.tensor([s.token_ids[-1] for s in seqs], dtype=torch.long).pin_memory()
+                logits = self.model.decode(ids.to(self.device, non_blocking=True), st.positions.long())
+            finally:
+                set_context()
         for s in seqs:
             s.num_cached_tokens += 1
         if seqs[0].params.num_beams == 1:
