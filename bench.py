@@ -444,18 +444,17 @@ def decode_requests(cfg, device):
     return reqs
 
 
-def run_decode(args):
+def decode_measure(name: str, world: int, rank: int, local: int, eager: bool = False) -> dict:
     """End-to-end decode tokens/s of the engine around the paged path on one BASELINE config:
-    completion tokens of all requests / wall time of the whole job (max over ranks). Synthetic:
+    completion tokens of all requests / wall time of the whole job (max over ranks). The
+    requests are dealt to the ranks whole (strong scaling: the job is fixed). Synthetic:
     random-init weights of the config's shape, seeded ids and N(0,1) images; EOS is disabled so
     every request decodes exactly max_tokens tokens (random weights have no natural stop)."""
     from vflorence_b200.engine import Engine, SamplingParams
     from vflorence_b200.sharding import assign_requests, max_over_ranks, sum_over_ranks
 
-    world, rank, local = dist_setup()
     device = torch.device("cuda", local)
-    torch.cuda.set_device(device)
-    cfg = decode_config(args.decode)
+    cfg = decode_config(name)
     model = build_decode_model(cfg, device)
     if cfg["kind"] == "florence2":
         with torch.inference_mode():
@@ -466,7 +465,7 @@ def run_decode(args):
     mine = [reqs[i] for i in assign_requests(costs, world)[rank]]
     params = SamplingParams.from_dict(cfg["params"])
     eng = Engine(model, max_num_seqs=cfg["max_num_seqs"], max_decoder_len=cfg["max_decoder_len"],
-                 max_encoder_len=cfg["max_encoder_len"], block_size=BS, cuda_graphs=not args.eager)
+                 max_encoder_len=cfg["max_encoder_len"], block_size=BS, cuda_graphs=not eager)
     # warm-up on a few of this rank's requests (allocator, library set-up); graphs for every
     # batch size this run can reach are captured up front, as a server does at start-up
     eng.generate(mine[: max(1, min(2, len(mine)))], SamplingParams.from_dict(dict(cfg["params"], max_tokens=4)))
@@ -482,14 +481,19 @@ def run_decode(args):
     tokens = sum(len(o) for o in outs)
     total_tokens = sum_over_ranks(float(tokens))
     wall = max_over_ranks(elapsed)
+    return {"metric": "decode tokens/s", "config": name, "value": total_tokens / wall, "unit": "tokens/s",
+            "n_gpus": world, "scaling": "strong", "requests": cfg["num_requests"],
+            "completion_tokens": int(total_tokens), "wall_s": wall, "params": cfg["params"],
+            "dtype": str(cfg["dtype"]).replace("torch.", ""), "max_num_seqs": cfg["max_num_seqs"],
+            "cuda_graphs": not eager, "data": "synthetic (random-init weights)"}
+
+
+def run_decode(args):
+    world, rank, local = dist_setup()
+    torch.cuda.set_device(torch.device("cuda", local))
+    line = decode_measure(args.decode, world, rank, local, args.eager)
     if rank == 0:
-        print(json.dumps({"metric": "decode tokens/s", "config": args.decode, "value": total_tokens / wall,
-                          "unit": "tokens/s", "n_gpus": world, "requests": cfg["num_requests"],
-                          "completion_tokens": int(total_tokens), "wall_s": wall,
-                          "params": cfg["params"], "dtype": str(cfg["dtype"]).replace("torch.", ""),
-                          "max_num_seqs": cfg["max_num_seqs"], "cuda_graphs": not args.eager,
-                          "data": "synthetic (random-init weights)"}),
-              flush=True)
+        print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist
 
@@ -556,6 +560,8 @@ def main():
     ap.add_argument("--decode", choices=["cfg1", "cfg2", "cfg3", "cfg4"], default=None,
                     help="end-to-end decode tokens/s of the engine on a BASELINE config")
     ap.add_argument("--eager", action="store_true", help="decode without CUDA graphs")
+    ap.add_argument("--decode-config", default="cfg4", choices=["cfg1", "cfg2", "cfg3", "cfg4", "none"],
+                    help="engine config measured after the kernel leg of the default run ('none' skips it)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.sweep:
@@ -666,6 +672,17 @@ def main():
     if traffic_info and traffic_info.get("dram_bytes_per_algorithmic_byte"):
         traffic = nb["self"] * float(traffic_info["dram_bytes_per_algorithmic_byte"])
 
+    plan_s, plan_c = step.plans
+    launches = step.launches * args.steps
+    decode = None
+    if args.decode_config != "none":
+        del w, step, d, host_in, host_meta, host_out, host_out_c
+        torch.cuda.empty_cache()
+        try:
+            decode = decode_measure(args.decode_config, world, rank, local)
+        except Exception as exc:  # the kernel line stands even if the engine leg fails
+            decode = {"config": args.decode_config, "error": f"{type(exc).__name__}: {exc}"[:300]}
+
     cb = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:  # reported at N=1 only
         cb = cpu_baseline(args.batch, seconds=args.cpu_seconds, sample=args.cpu_sample)
@@ -673,7 +690,6 @@ def main():
         cb.pop("seconds_per_full_step", None)
 
     if rank == 0:
-        plan_s, plan_c = step.plans
         line = {
             "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": elapsed_max / args.steps, "higher_is_better": True,
@@ -681,7 +697,7 @@ def main():
             "config": config_of(args, world),
             "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "ms_per_step": e2e_ms / e2e_steps, "steps": e2e_steps},
-            "gpu_launches": step.launches * args.steps,
+            "gpu_launches": launches,
             "roofline": {"bound": "hbm", "kernel": "paged_attention_kernel<bf16,64,1> + combine (self decode)",
                          "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                          "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
@@ -695,6 +711,7 @@ def main():
                       "cross": {"splits": plan_c.num_splits, "blocks_per_split": plan_c.blocks_per_split}},
             "clocks": clocks.summary(),
             "cpu_baseline": cb,
+            "decode": decode,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
