@@ -70,7 +70,8 @@ typedef struct vfl_attention_plan {
   int32_t max_q_len;        /* longest request in query rows                             */
   int32_t max_seq_len;      /* longest request in cached tokens                          */
   int32_t heads_per_cta;    /* heads handled by one CTA (one warp each)                  */
-  int32_t queries_per_cta;  /* query rows of one request handled together (1 or 4)       */
+  int32_t queries_per_cta;  /* query rows of one request handled together: 1 or 4 (CUDA-core
+                               kernel), 8 (tensor-core kernel: bf16, head_dim 64)          */
   int32_t blocks_per_split; /* KV blocks per split-K work item                           */
   int32_t num_splits;       /* split-K partitions of the longest request                 */
   int32_t stages;           /* shared-memory pipeline depth (16-token K/V tiles)         */

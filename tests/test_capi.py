@@ -60,7 +60,7 @@ def test_plan_large_batch_splits_long_requests(native):
     g = torch.Generator().manual_seed(2)
     lens = torch.randint(1, 4097, (1024,), generator=g).tolist()
     p = _plan(lens)
-    assert (p.heads_per_cta, p.queries_per_cta, p.stages) == (4, 1, 4)
+    assert (p.heads_per_cta, p.queries_per_cta, p.stages) == (4, 8, 4)   # bf16 x 64: tensor cores
     assert p.blocks_per_split * 16 == 256          # items capped at 256 tokens
     assert p.num_splits == -(-max(lens) // 256)
     assert p.workspace_bytes >= 1024 * 16 * p.num_splits * (64 + 2) * 4
@@ -92,8 +92,13 @@ def test_plan_short_batch_needs_no_workspace(native):
 
 def test_plan_grouped_rows(native):
     p = _plan([577, 577], qsl=[0, 3, 6], heads=12)
-    assert p.queries_per_cta == 4 and p.total_q == 6 and p.max_q_len == 3
+    assert p.queries_per_cta == 8 and p.total_q == 6 and p.max_q_len == 3   # tensor-core kernel
     assert p.heads_per_cta == 4
+    # CUDA-core kernel (fp32, or other head dims): 1 row per CTA for decode, 4 for grouped rows
+    f = _plan([577, 577], qsl=[0, 3, 6], heads=12, dtype=torch.float32)
+    assert f.queries_per_cta == 4
+    assert _plan([577, 577], heads=12, dtype=torch.float32).queries_per_cta == 1
+    assert _plan([577, 577], heads=12, d=128).queries_per_cta == 1
 
 
 def test_plan_f32_and_wide_heads(native):

@@ -6,6 +6,7 @@
 // partition, and the workspace those splits need. It is pure host arithmetic (no CUDA call),
 // sized for B200's 148 SMs.
 #include <cmath>
+#include <mutex>
 
 #include "paged_attention_kernels.cuh"
 
@@ -20,6 +21,67 @@ constexpr int kSmemPerSM = 227 * 1024;
 int plan_fail(vfl_attention_plan* plan, int status) {
   if (plan) plan->magic = 0;
   return status;
+}
+
+// The tensor-core kernel covers bfloat16 pools with head_dim 64 (the BART / Florence-2 shape).
+bool use_tensor_cores(int dtype, int head_dim) { return dtype == VFL_DTYPE_BF16 && head_dim == 64; }
+
+// ---- TMA tensor maps of the K/V pools (driver entry point through the runtime; cached)
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+struct MapEntry {
+  const void* base;
+  uint64_t rows;
+  uint32_t box_rows;
+  CUtensorMap map;
+};
+constexpr int kMapCache = 32;
+MapEntry g_maps[kMapCache];
+int g_map_next = 0;
+std::mutex g_map_mutex;
+
+int encode_fn(EncodeTiledFn* out) {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  static cudaError_t err = cudaSuccess;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    err = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q);
+    if (err == cudaSuccess && q == cudaDriverEntryPointSuccess) fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  });
+  if (fn == nullptr)
+    return fail(VFL_ERR_CUDA, "cuTensorMapEncodeTiled unavailable (%s)", cudaGetErrorString(err));
+  *out = fn;
+  return VFL_OK;
+}
+
+// [rows, 64] bf16 pool, 128-byte swizzle, box 64 x box_rows.
+int pool_tensor_map(const void* base, uint64_t rows, uint32_t box_rows, CUtensorMap* out) {
+  std::lock_guard<std::mutex> lock(g_map_mutex);
+  for (const MapEntry& e : g_maps)
+    if (e.base == base && e.rows == rows && e.box_rows == box_rows) {
+      *out = e.map;
+      return VFL_OK;
+    }
+  EncodeTiledFn fn = nullptr;
+  int st = encode_fn(&fn);
+  if (st) return st;
+  CUtensorMap map;
+  const cuuint64_t dims[2] = {64, rows};
+  const cuuint64_t strides[1] = {64 * 2};
+  const cuuint32_t box[2] = {64, box_rows};
+  const cuuint32_t elem_strides[2] = {1, 1};
+  const CUresult r = fn(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+                        elem_strides, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(VFL_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  g_maps[g_map_next] = MapEntry{base, rows, box_rows, map};
+  g_map_next = (g_map_next + 1) % kMapCache;
+  *out = map;
+  return VFL_OK;
 }
 
 }  // namespace
@@ -68,9 +130,10 @@ int vfl_plan_attention(int num_reqs, int num_heads, int num_kv_heads, int head_d
   const int stage_bytes = 2 * hpc * 16 * head_dim * es;
   int stages = kMaxStageBytes / stage_bytes;
   stages = stages < 2 ? 2 : (stages > 4 ? 4 : stages);
-  const int qpc = max_q <= 1 ? 1 : 4;
+  const bool tc = use_tensor_cores(dtype, head_dim);
+  const int qpc = tc ? kTcRows : (max_q <= 1 ? 1 : 4);
   const int groups = num_heads / hpc;
-  const int smem = kHeaderBytes + stages * stage_bytes;
+  const int smem = (tc ? kTcHeaderBytes : kHeaderBytes) + stages * stage_bytes;
   int ctas_per_sm = kSmemPerSM / (smem + 1024);
   const int thread_cap = 2048 / ((hpc + 1) * 32);
   ctas_per_sm = ctas_per_sm < 1 ? 1 : (ctas_per_sm > thread_cap ? thread_cap : ctas_per_sm);
@@ -217,7 +280,18 @@ int vfl_attention_with_kv_cache(const vfl_attention_plan* plan, const void* quer
   }
   dim3 grid(plan->num_reqs * (H / hpc), plan->num_splits, q_chunks);
   const int threads = (hpc + 1) * 32;  // hpc consumer warps + one producer warp
-  const int smem = kHeaderBytes + plan->stages * 2 * hpc * 16 * D * es;
+  const bool tc = plan->queries_per_cta == kTcRows;
+  const int smem = (tc ? kTcHeaderBytes : kHeaderBytes) + plan->stages * 2 * hpc * 16 * D * es;
+  if (tc) {
+    const uint64_t rows = (uint64_t)num_blocks * H * plan->block_size;
+    const uint32_t box_rows = plan->block_size == 16 ? 16u * hpc : 16u;
+    CUtensorMap kmap, vmap;
+    st = pool_tensor_map(k_cache, rows, box_rows, &kmap);
+    if (st) return st;
+    st = pool_tensor_map(v_cache, rows, box_rows, &vmap);
+    if (st) return st;
+    return launch_paged_attention_tc(p, kmap, vmap, grid, threads, smem, s);
+  }
   if (plan->dtype == VFL_DTYPE_F32) return launch_paged_attention_f32(p, D, qpc, grid, threads, smem, s);
   return launch_paged_attention_bf16(p, D, qpc, grid, threads, smem, s);
 }

@@ -1,9 +1,25 @@
-// bfloat16 instantiations of the paged attention kernels (split from f32 to compile in parallel).
-#include "paged_attention_kernels.cuh"
+// bfloat16 instantiations of the paged attention kernels (split from f32 to compile in parallel),
+// including the tensor-core variant for head_dim 64.
+#include "paged_attention_tc.cuh"
 
 namespace vfl {
 int launch_paged_attention_bf16(const AttnParams& p, int head_dim, int qpc, dim3 grid, int threads,
                                 int smem_bytes, cudaStream_t stream) {
   return launch_dtype<__nv_bfloat16>(p, head_dim, qpc, grid, threads, smem_bytes, stream);
+}
+
+int launch_paged_attention_tc(const AttnParams& p, const CUtensorMap& kmap, const CUtensorMap& vmap, dim3 grid,
+                              int threads, int smem_bytes, cudaStream_t stream) {
+  static int smem_done[kMaxDevices];
+  int st = ensure_smem_attribute(reinterpret_cast<const void*>(paged_attention_tc_kernel),
+                                 kTcHeaderBytes + kMaxStageBytes, smem_done);
+  if (st) return st;
+  paged_attention_tc_kernel<<<grid, threads, smem_bytes, stream>>>(p, kmap, vmap);
+  st = cuda_status(cudaGetLastError(), "paged_attention (tensor cores) launch");
+  if (st || p.num_splits <= 1 || p.ws_arrivals != nullptr) return st;
+  const int64_t warps = (int64_t)p.total_q * p.num_heads;
+  paged_attention_combine_kernel<__nv_bfloat16, 64>
+      <<<static_cast<int>(ceil_div(warps, (int64_t)4)), 128, 0, stream>>>(p);
+  return cuda_status(cudaGetLastError(), "paged_attention combine launch");
 }
 }  // namespace vfl

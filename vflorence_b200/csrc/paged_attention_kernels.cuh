@@ -23,6 +23,8 @@
 // would hold every split CTA's SM slot).
 #pragma once
 
+#include <cuda.h>
+
 #include "common.cuh"
 
 namespace vfl {
@@ -506,6 +508,12 @@ __global__ void __launch_bounds__(128) paged_attention_combine_kernel(const Attn
   if (n_splits <= 1) return;  // written directly by the main kernel
   merge_splits<T, D>(p, row, h, n_splits, lane);
 }
+
+// Tensor-core variant (paged_attention_tc.cuh): bf16, head_dim 64, up to kTcRows rows per CTA.
+constexpr int kTcHeaderBytes = 2048;  // SmemHeader + one 8x16 bf16 P tile per consumer warp
+constexpr int kTcRows = 8;            // query rows per CTA (the mma N dimension)
+int launch_paged_attention_tc(const AttnParams& p, const CUtensorMap& kmap, const CUtensorMap& vmap, dim3 grid,
+                              int threads, int smem_bytes, cudaStream_t stream);
 
 // Launches the kernel; defined per dtype.
 int launch_paged_attention_f32(const AttnParams& p, int head_dim, int qpc, dim3 grid, int threads,

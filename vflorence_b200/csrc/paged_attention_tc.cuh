@@ -1,0 +1,339 @@
+// Tensor-core variant of the paged attention kernel: bfloat16, head_dim 64, up to 8 query rows
+// of one request per CTA (decode rows, or the beams of a request sharing its encoder pages).
+//
+// Same work decomposition, producer ring, split-K partials and merge as paged_attention_kernel
+// (paged_attention_kernels.cuh); what changes is how a 16-token tile is consumed:
+//   * the producer fills the stages with 2-D TMA tensor copies using the 128-byte swizzle, so a
+//     tile's 16-byte chunks are spread over all banks (chunk c of row r lands at c ^ (r mod 8));
+//   * S[16 tokens x 8 rows] = K_tile . Q^T with mma.m16n8k16 (bf16 in, fp32 accumulate), K as
+//     the A operand through ldmatrix, Q held in registers as the B operand;
+//   * online softmax on the fp32 accumulators (exp2 domain, lazy rescaling); P is rounded to
+//     bf16, staged in shared memory, and O^T[64 x 8] += V^T . P^T with V through ldmatrix.trans.
+// One mma.m16n8k16 does 2048 multiply-adds, so a tile costs ~8 mma + ~8 ldmatrix instead of
+// ~100 CUDA-core instructions per query row: the beams of a request come almost for free.
+// The sum l accumulates the same bf16-rounded p that multiplies V, so the normalisation matches.
+#pragma once
+
+#include <cuda.h>
+
+#include "paged_attention_kernels.cuh"
+
+namespace vfl {
+
+constexpr int kTcPTileOffset = 1024;  // P tiles after the SmemHeader
+static_assert(sizeof(SmemHeader) <= kTcPTileOffset && kTcPTileOffset + 4 * kTcRows * 16 * 2 <= kTcHeaderBytes,
+              "tc header");
+
+__device__ __forceinline__ uint32_t swz(uint32_t tile_base, int row, int chunk) {
+  const uint32_t row_addr = tile_base + row * 128;
+  return row_addr + ((chunk ^ ((row_addr >> 7) & 7)) << 4);
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+
+__device__ __forceinline__ void mma_bf16_16x8x16(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar,
+                                            uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint "
+      "[%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2_bits(__nv_bfloat16 lo, __nv_bfloat16 hi) {
+  return (uint32_t)__bfloat16_as_ushort(lo) | ((uint32_t)__bfloat16_as_ushort(hi) << 16);
+}
+
+// kmap / vmap: the K and V pools as 2-D [num_blocks * H * block_size rows, 64 columns] bf16 with
+// the 128-byte swizzle; box = 64 columns x (16 * heads_per_cta rows if block_size == 16, else 16).
+__global__ void __launch_bounds__(160, 3) paged_attention_tc_kernel(const AttnParams p,
+                                                                     const __grid_constant__ CUtensorMap kmap,
+                                                                     const __grid_constant__ CUtensorMap vmap) {
+  constexpr int D = 64;
+  constexpr int TILE = 16 * D;  // elements of one head's 16-token tile (2 KiB)
+  using T = __nv_bfloat16;
+
+  extern __shared__ __align__(1024) uint8_t smem[];
+  SmemHeader& hdr = *reinterpret_cast<SmemHeader*>(smem);
+  T* s_kv = reinterpret_cast<T*>(smem + kTcHeaderBytes);
+
+  const int hpc = p.heads_per_cta;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const bool producer = warp == hpc;
+  const int groups = p.num_heads / hpc;
+  const int r = blockIdx.x / groups;
+  const int h0 = (blockIdx.x - r * groups) * hpc;
+  const int split = blockIdx.y;
+  const int bs = p.block_size;
+  const int bps = p.blocks_per_split;
+
+  if (load_volatile(p.err) & VFL_DEVERR_TIMEOUT) return;
+
+  const int q_begin = __ldg(p.qsl + r);
+  const int q_end = __ldg(p.qsl + r + 1);
+  if (q_begin < 0 || q_end < q_begin || q_end > p.total_q) {
+    if (threadIdx.x == 0 && split == 0 && blockIdx.z == 0) report(p.err, VFL_DEVERR_QUERY);
+    return;
+  }
+  const int q0 = q_begin + blockIdx.z * kTcRows;
+  const int nq = min(kTcRows, q_end - q0);
+  if (nq <= 0) return;
+  int L = __ldg(p.seq_lens + r);
+  const int cap = min(p.table_cols * bs, p.max_seq_len);
+  if (L > cap) {
+    if (threadIdx.x == 0 && split == 0 && blockIdx.z == 0) report(p.err, VFL_DEVERR_CONTEXT);
+    L = cap;
+  }
+  L = max(L, 0);
+  const int nblk = ceil_div(L, bs);
+  const int n_splits = ceil_div(nblk, bps);
+  if (split >= max(n_splits, 1)) return;
+  // visible tokens of row q0 + j (causal rows see fewer); vis_max bounds the CTA's tiles
+  auto visible = [&](int j) { return j < nq ? max(p.causal ? L - (q_end - 1 - (q0 + j)) : L, 0) : 0; };
+  const int vis_max = visible(nq - 1) > visible(0) ? visible(nq - 1) : visible(0);
+  const int tpb = bs / 16;
+  const int blk_begin = split * bps;
+  const int tile_begin = blk_begin * tpb;
+  const int tile_end = min((blk_begin + bps) * tpb, ceil_div(vis_max, 16));
+  const int ntiles = max(0, tile_end - tile_begin);
+  const int stages = p.stages;
+  const int stage_elems = 2 * hpc * TILE;
+  const uint32_t head_tile_bytes = TILE * sizeof(T);
+
+  if (producer) {
+    const int nb = min(bps, nblk - blk_begin);
+    for (int i = lane; i < nb; i += 32) {
+      int b = __ldg(p.table + r * p.table_stride + blk_begin + i);
+      if (b < 0 || b >= p.num_blocks) {
+        report(p.err, VFL_DEVERR_BLOCK_ID);
+        b = 0;
+      }
+      hdr.table[i] = b;
+    }
+  }
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(&hdr.full[s], 1);
+      mbar_init(&hdr.empty[s], hpc);
+    }
+    hdr.abort = 0;
+    hdr.consumed = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  if (producer) {
+    int issued = 0;
+    if (lane == 0) {
+      const uint64_t policy = l2_evict_first_policy();
+      for (int i = 0; i < ntiles; ++i) {
+        const int s = i % stages;
+        if (i >= stages && !mbar_wait_bounded(&hdr.empty[s], ((i / stages) - 1) & 1)) {
+          report(p.err, VFL_DEVERR_TIMEOUT);
+          hdr.abort = 1;
+          break;
+        }
+        if (*reinterpret_cast<volatile int*>(&hdr.abort)) break;
+        fence_proxy_async_smem();
+        const int tile = tile_begin + i;
+        const int blk = tile / tpb;
+        const int sub_tile = tile - blk * tpb;
+        const int64_t phys = hdr.table[blk - blk_begin];
+        T* ks = s_kv + (size_t)s * stage_elems;
+        T* vs = ks + hpc * TILE;
+        mbar_arrive_expect_tx(&hdr.full[s], 2u * hpc * head_tile_bytes);
+        const int row0 = static_cast<int>((phys * p.num_heads + h0) * bs + sub_tile * 16);
+        if (tpb == 1) {  // the head group's tiles are adjacent rows: one box of 16 * hpc rows
+          tma_load_2d(ks, &kmap, 0, row0, &hdr.full[s], policy);
+          tma_load_2d(vs, &vmap, 0, row0, &hdr.full[s], policy);
+        } else {
+          for (int w = 0; w < hpc; ++w) {
+            tma_load_2d(ks + w * TILE, &kmap, 0, row0 + w * bs, &hdr.full[s], policy);
+            tma_load_2d(vs + w * TILE, &vmap, 0, row0 + w * bs, &hdr.full[s], policy);
+          }
+        }
+        issued = i + 1;
+      }
+    }
+    __syncwarp();
+    __syncthreads();
+    if (lane == 0 && *reinterpret_cast<volatile int*>(&hdr.abort)) {
+      for (int t = *reinterpret_cast<volatile int*>(&hdr.consumed); t < issued; ++t)
+        mbar_wait_bounded(&hdr.full[t % stages], (t / stages) & 1);
+    }
+    return;
+  }
+
+  // ================= consumers: one warp per head, mma fragments ==========================
+  const int h = h0 + warp;
+  const int g = lane >> 2;   // mma row group
+  const int tq = lane & 3;   // mma thread-in-group
+  // B operand of S = K.Q^T: query row g, dims 16kk + 2tq (+1) and 16kk + 8 + 2tq (+1)
+  uint32_t bq[4][2];
+#pragma unroll
+  for (int kk = 0; kk < 4; ++kk) {
+    bq[kk][0] = bq[kk][1] = 0u;
+    if (g < nq) {
+      const T* src = static_cast<const T*>(p.q) + (int64_t)(q0 + g) * p.q_stride + h * D + kk * 16 + 2 * tq;
+      bq[kk][0] = __ldg(reinterpret_cast<const unsigned int*>(src));
+      bq[kk][1] = __ldg(reinterpret_cast<const unsigned int*>(src + 8));
+    }
+  }
+  // this thread's two query columns 2tq, 2tq+1
+  int vis_c[2];
+  vis_c[0] = visible(2 * tq);
+  vis_c[1] = visible(2 * tq + 1);
+  const bool col_on[2] = {2 * tq < nq, 2 * tq + 1 < nq};
+  float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
+  float o[4][4];  // O^T m-tiles: [dim 16mt + g (+8)][query 2tq (+1)]
+#pragma unroll
+  for (int mt = 0; mt < 4; ++mt)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) o[mt][e] = 0.f;
+  // this warp's P tile: [8 query rows][16 tokens] bf16
+  T* p_tile = reinterpret_cast<T*>(smem + kTcPTileOffset) + warp * (kTcRows * 16);
+  const uint32_t p_tile_u32 = smem_u32(p_tile);
+  // ldmatrix row/chunk of this lane: K (A = K rows) and V^T (A = V^T via .trans)
+  const int mat = lane >> 3;
+  const int k_row = (lane & 7) + (mat & 1) * 8, k_chunk_hi = mat >> 1;
+  const int v_row = (lane & 7) + (mat >> 1) * 8, v_chunk_hi = mat & 1;
+
+  bool aborted = false;
+#pragma unroll 1
+  for (int i = 0; i < ntiles; ++i) {
+    const int s = i % stages;
+    if (!mbar_wait_bounded(&hdr.full[s], (i / stages) & 1)) {
+      report(p.err, VFL_DEVERR_TIMEOUT);
+      if (lane == 0) {
+        hdr.abort = 1;
+        atomicMax(&hdr.consumed, i);
+      }
+      aborted = true;
+      break;
+    }
+    const uint32_t kt = smem_u32(s_kv + (size_t)s * stage_elems + warp * TILE);
+    const uint32_t vt = kt + hpc * TILE * sizeof(T);
+    const int tok0 = (tile_begin + i) * 16;
+
+    // S[token g, g+8][query 2tq, 2tq+1]
+    float sc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+      uint32_t a[4];
+      ldsm_x4(swz(kt, k_row, 2 * kk + k_chunk_hi), a);
+      mma_bf16_16x8x16(sc, a, bq[kk][0], bq[kk][1]);
+    }
+    // online softmax per query column (exp2 domain, lazy rescale as in the CUDA-core kernel)
+    constexpr float kRescaleSlack = 8.f;
+    __nv_bfloat16 pb[4];
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const bool v0 = col_on[e] && tok0 + g < vis_c[e];
+      const bool v1 = col_on[e] && tok0 + g + 8 < vis_c[e];
+      const float s0 = v0 ? sc[e] * p.scale_log2 : -INFINITY;
+      const float s1 = v1 ? sc[e + 2] * p.scale_log2 : -INFINITY;
+      float mx = fmaxf(s0, s1);
+#pragma unroll
+      for (int off = 4; off < 32; off <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+      if (mx > m[e] + kRescaleSlack) {
+        const float alpha = m[e] == -INFINITY ? 0.f : exp2_approx(m[e] - mx);
+        m[e] = mx;
+        l[e] *= alpha;
+#pragma unroll
+        for (int mt = 0; mt < 4; ++mt) {
+          o[mt][e] *= alpha;
+          o[mt][e + 2] *= alpha;
+        }
+      }
+      const bool none = m[e] == -INFINITY;
+      pb[e] = __float2bfloat16_rn(none ? 0.f : exp2_approx(s0 - m[e]));
+      pb[e + 2] = __float2bfloat16_rn(none ? 0.f : exp2_approx(s1 - m[e]));
+      l[e] += __bfloat162float(pb[e]) + __bfloat162float(pb[e + 2]);
+    }
+    // P -> shared [query][token], then the PV B fragments: query g, tokens 2tq (+1), 2tq+8 (+9)
+    p_tile[(2 * tq) * 16 + g] = pb[0];
+    p_tile[(2 * tq + 1) * 16 + g] = pb[1];
+    p_tile[(2 * tq) * 16 + g + 8] = pb[2];
+    p_tile[(2 * tq + 1) * 16 + g + 8] = pb[3];
+    __syncwarp();
+    uint32_t bp0, bp1;
+    asm volatile("ld.shared.b32 %0, [%1];" : "=r"(bp0) : "r"(p_tile_u32 + (g * 16 + 2 * tq) * 2));
+    asm volatile("ld.shared.b32 %0, [%1];" : "=r"(bp1) : "r"(p_tile_u32 + (g * 16 + 2 * tq + 8) * 2));
+    // O^T += V^T . P^T over the tile's 16 tokens, four 16-dim m-tiles
+#pragma unroll
+    for (int mt = 0; mt < 4; ++mt) {
+      uint32_t a[4];
+      ldsm_x4_trans(swz(vt, v_row, 2 * mt + v_chunk_hi), a);
+      mma_bf16_16x8x16(o[mt], a, bp0, bp1);
+    }
+    __syncwarp();  // P tile and K/V stage reads done before the next tile reuses them
+    if (lane == 0) mbar_arrive(&hdr.empty[s]);
+  }
+  __syncthreads();
+  if (aborted || *reinterpret_cast<volatile int*>(&hdr.abort)) return;
+
+  // l partial sums over the 8 row-group lanes that share each query column
+#pragma unroll
+  for (int e = 0; e < 2; ++e)
+#pragma unroll
+    for (int off = 4; off < 32; off <<= 1) l[e] += __shfl_xor_sync(0xffffffffu, l[e], off);
+
+  const int S = p.num_splits;
+  if (n_splits <= 1) {
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      if (!col_on[e]) continue;
+      const int row = q0 + 2 * tq + e;
+      const float inv = l[e] > 0.f ? 1.f / l[e] : 0.f;
+      T* dst = static_cast<T*>(p.out) + (int64_t)row * p.out_stride + h * D;
+#pragma unroll
+      for (int mt = 0; mt < 4; ++mt) {
+        dst[16 * mt + g] = __float2bfloat16_rn(o[mt][e] * inv);
+        dst[16 * mt + g + 8] = __float2bfloat16_rn(o[mt][e + 2] * inv);
+      }
+    }
+    return;
+  }
+#pragma unroll
+  for (int e = 0; e < 2; ++e) {
+    if (!col_on[e]) continue;
+    const int64_t item = ((int64_t)(q0 + 2 * tq + e) * p.num_heads + h) * S + split;
+    float* dst = p.ws_acc + item * D;
+#pragma unroll
+    for (int mt = 0; mt < 4; ++mt) {
+      dst[16 * mt + g] = o[mt][e];
+      dst[16 * mt + g + 8] = o[mt][e + 2];
+    }
+    if (g == 0) *reinterpret_cast<float2*>(p.ws_ml + item * 2) = make_float2(m[e], l[e]);
+  }
+  if (p.ws_arrivals == nullptr) return;  // the combine launch merges
+  consumer_barrier(hpc);
+  if (threadIdx.x == 0) {
+    int* arrivals = p.ws_arrivals + ((int64_t)r * groups + h0 / hpc) * gridDim.z + blockIdx.z;
+    hdr.is_last = arrive_acq_rel(arrivals) == n_splits - 1;
+  }
+  consumer_barrier(hpc);
+  if (!hdr.is_last) return;
+  for (int j = 0; j < nq; ++j) merge_splits<T, D>(p, q0 + j, h, n_splits, lane);
+}
+
+}  // namespace vfl
