@@ -369,6 +369,24 @@ def run_sweep(args):
                               "cpu_oracle_gbs": cpu_gbs, "cpu_threads": threads, "cpu_sample_seqs": n}),
                   flush=True)
             del c, kc, vc
+    # beams sharing a request's encoder pages (configs 2-4): R requests x beams query rows
+    for R, beams, enc in ((64, 3, 587), (85, 3, 587), (256, 3, 587), (32, 4, 1024), (256, 4, 1024)):
+        c = _cross_workload(R, enc, 4, device)
+        q = torch.randn(R * beams, H, D, device=device, dtype=DTYPE)
+        qsl = torch.arange(0, R * beams + 1, beams, dtype=torch.int32)
+        meta_c = ops.get_scheduler_metadata(R, H, H, D, c["lens"], DTYPE, qsl, False, "sm100", BS)
+        lens_d, table_d, qsl_d = c["lens"].to(device), c["table"].to(device), qsl.to(device)
+        out_c = torch.empty_like(q)
+        fb = lambda: ops.attention_with_kv_cache(q, c["k"], c["v"], out_c, qsl_d, lens_d,  # noqa: E731
+                                                 D ** -0.5, False, table_d, meta_c)
+        for _ in range(3):
+            fb()
+        nbb = 2 * R * enc * row + 2 * R * beams * row + 4 * R * math.ceil(enc / BS) + 4 * R + 4 * (R + 1)
+        ms_b = _time_op(fb, 50, flush)
+        print(json.dumps({"point": "cross_beams", "requests": R, "beams": beams, "enc_len": enc, "us": ms_b * 1e3,
+                          "gbs": nbb / ms_b / 1e6, "frac_of_measured_hbm": nbb / ms_b / 1e6 / peak,
+                          "rows_per_cta": ops.plan_of(meta_c).queries_per_cta}), flush=True)
+        del c
 
 
 # ---------------------------------------------------------------------------- decode (engine)
@@ -698,7 +716,7 @@ def main():
             "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "ms_per_step": e2e_ms / e2e_steps, "steps": e2e_steps},
             "gpu_launches": launches,
-            "roofline": {"bound": "hbm", "kernel": "paged_attention_kernel<bf16,64,1> + combine (self decode)",
+            "roofline": {"bound": "hbm", "kernel": "self decode: paged_attention_tc_kernel (bf16, head_dim 64) + combine",
                          "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                          "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
                          else "fallback 6650 GB/s", "traffic": traffic,
