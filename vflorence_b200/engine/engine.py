@@ -22,7 +22,7 @@ from ..block_manager import BlockManager
 from ..context import set_context
 from ..kv_cache import PagedKVCache
 from .model import PagedSeq2Seq
-from .sampling import LogitsRules, SamplingParams, select_beam_candidates
+from .sampling import LogitsRules, SamplingParams
 
 
 @dataclass
@@ -222,14 +222,51 @@ class Engine:
                 done.append(s.request_id)
         return done
 
+    def _beam_candidates(self, seqs, scores, keep):
+        """Each request's best ``keep`` (row, token, cum_logprob) continuations, selected on the
+        GPU: every row's top-k plus its cumulative log-prob, scattered into a per-request grid in
+        row order, one stable descending sort per request - the order the reference's stable
+        Python sort of the concatenated rows gives (vflorence/engine/model_runner.py:383-410)."""
+        rows, vocab = scores.shape
+        k = min(keep, vocab)
+        req_of, slot_of, counts, order = [], [], [], {}
+        for s in seqs:
+            r = order.get(s.request_id)
+            if r is None:
+                r = order[s.request_id] = len(counts)
+                counts.append(0)
+            req_of.append(r)
+            slot_of.append(counts[r])
+            counts[r] += 1
+        R, width = len(counts), max(counts)
+        host = torch.tensor([req_of, slot_of], dtype=torch.long).pin_memory()
+        cum = torch.tensor([s.cum_logprob for s in seqs], dtype=torch.float32).pin_memory()
+        idx = host.to(self.device, non_blocking=True)
+        top_s, top_i = torch.topk(scores, k, dim=-1)
+        top_s += cum.to(self.device, non_blocking=True).unsqueeze(-1)
+        grid_s = torch.full((R, width, k), float("-inf"), device=self.device)
+        grid_t = torch.zeros((R, width, k), dtype=torch.long, device=self.device)
+        grid_r = torch.full((R, width, k), -1, dtype=torch.long, device=self.device)
+        grid_s[idx[0], idx[1]] = top_s
+        grid_t[idx[0], idx[1]] = top_i
+        grid_r[idx[0], idx[1]] = torch.arange(rows, device=self.device).unsqueeze(-1).expand(rows, k)
+        srt, pos = torch.sort(grid_s.view(R, width * k), dim=1, descending=True, stable=True)
+        n = min(keep, width * k)
+        pos = pos[:, :n]
+        picked = torch.stack([grid_r.view(R, -1).gather(1, pos).double(), grid_t.view(R, -1).gather(1, pos).double(),
+                              srt[:, :n].double()]).tolist()
+        rids = list(order)
+        cands = {}
+        for r in range(R):
+            cands[rids[r]] = [(int(row), int(tok), sc) for row, tok, sc in zip(*(picked[c][r] for c in range(3)))
+                              if row >= 0]
+        return cands
+
     def _finish_beam(self, seqs, logits) -> list[int]:
         params = seqs[0].params
         rules = self._rules_for(params)
         scores = rules(torch.log_softmax(logits.float(), dim=-1), [s.token_ids for s in seqs])
-        keep = params.beams_to_keep()
-        top_s, top_i = torch.topk(scores, min(keep, scores.shape[-1]), dim=-1)
-        top_s += torch.tensor([s.cum_logprob for s in seqs], dtype=torch.float32, device=self.device).unsqueeze(-1)
-        cands = select_beam_candidates(seqs, top_s.tolist(), top_i.tolist(), keep)
+        cands = self._beam_candidates(seqs, scores, params.beams_to_keep())
         eos = set(params.eos_ids())
         nb = params.num_beams
         done = []
