@@ -33,10 +33,15 @@ class Request:
 
 @dataclass(eq=False)
 class _Seq:
+    """One hypothesis. Its decoder tokens live in row ``slot`` of the engine's device token
+    buffer (start token first); the host keeps only the last token and the length."""
+
     request_id: int
-    token_ids: list[int]
     encoder_ids: list[int]
     params: SamplingParams
+    slot: int
+    last_token: int
+    length: int = 1
     pixel_values: torch.Tensor | None = None
     block_table: list[int] = field(default_factory=list)
     num_cached_tokens: int = 0
@@ -45,17 +50,13 @@ class _Seq:
 
     @property
     def num_generated(self) -> int:
-        return len(self.token_ids) - self.prompt_len
+        return self.length - self.prompt_len
 
     def finished(self, eos: set[int]) -> bool:
-        return self.token_ids[-1] in eos or self.num_generated >= self.params.max_tokens
+        return self.last_token in eos or self.num_generated >= self.params.max_tokens
 
     def score(self) -> float:
         return self.cum_logprob / (max(self.num_generated, 1) ** self.params.length_penalty)
-
-    def child(self, token: int, cum_logprob: float) -> "_Seq":
-        return _Seq(self.request_id, [*self.token_ids, token], self.encoder_ids, self.params,
-                    self.pixel_values, [], self.num_cached_tokens, cum_logprob, self.prompt_len)
 
 
 class Engine:
@@ -78,6 +79,11 @@ class Engine:
         self.blocks = BlockManager(self.num_blocks, block_size)
         cfg = hf_model.config.get_text_config()
         self.start_token = cfg.decoder_start_token_id if decoder_start_token_id is None else decoder_start_token_id
+        # decoder tokens of every live hypothesis, one row each. Beam children take fresh rows,
+        # so a step can hold parents, their children (up to 2 per kept beam) and the finished
+        # hypotheses kept per request: at most 4 rows per sequence slot
+        self.tokens = torch.zeros(4 * max_num_seqs + 4, max_decoder_len + 2, dtype=torch.int32, device=self.device)
+        self.free_slots = list(range(self.tokens.shape[0]))
         self.waiting: deque[_Seq] = deque()
         self.running: list[_Seq] = []
         self.finished_beams: dict[int, list[_Seq]] = {}
@@ -108,7 +114,8 @@ class Engine:
                 raise ValueError("all active requests must share the same SamplingParams")
         rid = self._next_id
         self._next_id += 1
-        self.waiting.append(_Seq(rid, [self.start_token], list(request.input_ids), params, request.pixel_values))
+        self.waiting.append(_Seq(rid, list(request.input_ids), params, -1, self.start_token,
+                                 pixel_values=request.pixel_values))
         return rid
 
     def is_finished(self) -> bool:
@@ -131,6 +138,7 @@ class Engine:
         self.finished_beams.clear()
         self.blocks.reset()
         self.kv.reset()
+        self.free_slots = list(range(self.tokens.shape[0]))
         set_context()
 
     # ------------------------------------------------------------------------------------ step
@@ -156,7 +164,7 @@ class Engine:
                         query_start_loc=st.query_start_loc, self_metadata=st.self_metadata, isa=self.kv.isa,
                         cross_staged=staged)
             try:
-                ids = torch.tensor([s.token_ids[-1] for s in seqs], dtype=torch.long).pin_memory()
+                ids = torch.tensor([s.last_token for s in seqs], dtype=torch.long).pin_memory()
                 logits = self.model.decode(ids.to(self.device, non_blocking=True), st.positions.long())
             finally:
                 set_context()
@@ -168,10 +176,15 @@ class Engine:
 
     def _schedule(self):
         used = sum({s.request_id: s.params.num_beams for s in self.running}.values())
+        admitted = []
         while self.waiting and used + self.waiting[0].params.num_beams <= self.max_num_seqs:
             s = self.waiting.popleft()
+            s.slot = self.free_slots.pop()
             self.running.append(s)
+            admitted.append(s.slot)
             used += s.params.num_beams
+        if admitted:
+            self.tokens[torch.tensor(admitted, device=self.device), 0] = self.start_token
         seqs = list(self.running)
         if self.blocks.required_new_blocks(seqs) > self.blocks.num_free_blocks:
             raise RuntimeError("KV cache is full; increase num_blocks")
@@ -179,17 +192,41 @@ class Engine:
         return seqs, copies
 
     def _encode(self, fresh) -> None:
+        """Page the encoder K/V of this step's new requests.
+
+        Encoder pages are assigned as the reference does (groups of equal prompt length and
+        image shape, in order of first appearance, vflorence/engine/model_runner.py:215-242).
+        The encoder itself runs once per image shape: shorter prompts are right-padded with an
+        attention mask, and padded positions get slot -1, so one append per layer writes only
+        real tokens.
+        """
+        bs = self.block_size
         groups: dict = {}
         for s in fresh:
             key = (len(s.encoder_ids), None if s.pixel_values is None else tuple(s.pixel_values.shape))
             groups.setdefault(key, []).append(s)
-        for (enc_len, px), group in groups.items():
-            ids = torch.tensor([s.encoder_ids for s in group], dtype=torch.long).to(self.device)
-            pix = None
-            if px is not None:
-                pix = torch.stack([s.pixel_values for s in group]).to(self.device)
-            hidden = self.model.encode(ids, pix)
-            slots = self.kv.page_requests([s.request_id for s in group], enc_len)
+        for (enc_len, _), group in groups.items():
+            self.kv.cross.assign([s.request_id for s in group], enc_len, bs)
+        batches: dict = {}
+        for s in fresh:
+            batches.setdefault(None if s.pixel_values is None else tuple(s.pixel_values.shape), []).append(s)
+        pad_id = self.model.lm.config.pad_token_id or 0
+        for px, batch in batches.items():
+            width = max(len(s.encoder_ids) for s in batch)
+            ids = torch.full((len(batch), width), pad_id, dtype=torch.long)
+            mask = torch.zeros((len(batch), width), dtype=torch.long)
+            slots = torch.full((len(batch), width), -1, dtype=torch.long)
+            for i, s in enumerate(batch):
+                n = len(s.encoder_ids)
+                ids[i, :n] = torch.tensor(s.encoder_ids)
+                mask[i, :n] = 1
+                pages = self.kv.cross.pages[s.request_id][0].long()
+                t = torch.arange(n)
+                slots[i, :n] = pages[t // bs] * bs + t % bs
+            ragged = bool((mask == 0).any())
+            ids, slots = ids.to(self.device), slots.view(-1).to(self.device)
+            pix = None if px is None else torch.stack([s.pixel_values for s in batch]).to(self.device)
+            hidden = self.model.encode(ids, pix, mask.to(self.device) if ragged else None)
             for layer in range(len(self.model.layers)):
                 k, v = self.model.cross_kv(layer, hidden)
                 self.kv.write_encoder_kv(layer, k, v, slots)
@@ -199,28 +236,44 @@ class Engine:
             self._rules = (params, LogitsRules(params, self.model.vocab_size, self.device))
         return self._rules[1]
 
-    def _finish(self, seq: _Seq, tokens: list[int]) -> None:
-        self.outputs[seq.request_id] = tokens
-        self.kv.clear_request(seq.request_id)
+    def _rows_state(self, seqs):
+        """Device views for the rules: token rows and lengths of ``seqs``."""
+        meta = torch.tensor([[s.slot for s in seqs], [s.length for s in seqs]], dtype=torch.long).pin_memory()
+        meta = meta.to(self.device, non_blocking=True)
+        rules = self._rules_for(seqs[0].params)
+        hist = self.tokens[meta[0]] if rules.needs_history else None
+        return rules, meta[0], meta[1], hist
+
+    def _emit(self, done: list[_Seq]) -> None:
+        """Record finished hypotheses' generated tokens (one copy for the step) and release them."""
+        if not done:
+            return
+        width = max(s.length for s in done)
+        rows = self.tokens[torch.tensor([s.slot for s in done], device=self.device), :width].tolist()
+        for s, row in zip(done, rows):
+            self.outputs[s.request_id] = row[s.prompt_len: s.length]
+            self.kv.clear_request(s.request_id)
 
     def _remove(self, seq: _Seq) -> None:
         self.running.remove(seq)
         self.blocks.deallocate(seq)
+        self.free_slots.append(seq.slot)
 
     def _finish_greedy(self, seqs, logits) -> list[int]:
         params = seqs[0].params
-        rules = self._rules_for(params)
-        scores = rules(logits.float(), [s.token_ids for s in seqs])
-        picks = scores.argmax(dim=-1).tolist()
+        rules, slots, lengths, hist = self._rows_state(seqs)
+        picks = rules(logits.float(), hist, lengths).argmax(dim=-1)
+        self.tokens[slots, lengths] = picks.to(torch.int32)
         eos = set(params.eos_ids())
         done = []
-        for s, t in zip(seqs, picks):
-            s.token_ids.append(t)
+        for s, t in zip(seqs, picks.tolist()):
+            s.last_token, s.length = t, s.length + 1
             if s.finished(eos):
-                self._remove(s)
-                self._finish(s, s.token_ids[s.prompt_len:])
-                done.append(s.request_id)
-        return done
+                done.append(s)
+        self._emit(done)
+        for s in done:
+            self._remove(s)
+        return [s.request_id for s in done]
 
     def _beam_candidates(self, seqs, scores, keep):
         """Each request's best ``keep`` (row, token, cum_logprob) continuations, selected on the
@@ -262,38 +315,60 @@ class Engine:
                               if row >= 0]
         return cands
 
+    def _child(self, parent: _Seq, token: int, cum_logprob: float) -> _Seq:
+        return _Seq(parent.request_id, parent.encoder_ids, parent.params, self.free_slots.pop(), token,
+                    parent.length + 1, parent.pixel_values, [], parent.num_cached_tokens, cum_logprob,
+                    parent.prompt_len)
+
     def _finish_beam(self, seqs, logits) -> list[int]:
         params = seqs[0].params
-        rules = self._rules_for(params)
-        scores = rules(torch.log_softmax(logits.float(), dim=-1), [s.token_ids for s in seqs])
+        rules, slots, lengths, hist = self._rows_state(seqs)
+        scores = rules(torch.log_softmax(logits.float(), dim=-1), hist, lengths)
         cands = self._beam_candidates(seqs, scores, params.beams_to_keep())
         eos = set(params.eos_ids())
         nb = params.num_beams
-        done = []
+        born = []   # (parent, child): every child whose tokens must be written this step
+        done_rids, emitted, released = [], [], []
         for rid, cand in cands.items():
             finished = self.finished_beams.setdefault(rid, [])
             running = []
             for rank, (row, token, cum) in enumerate(cand):
                 if rank >= nb and len(running) >= nb:
                     break
-                child = seqs[row].child(token, cum)
-                if child.finished(eos):
-                    if rank < nb:
-                        finished.append(child)
-                elif len(running) < nb:
-                    running.append((seqs[row], child))
+                parent = seqs[row]
+                is_done = token in eos or parent.num_generated + 1 >= params.max_tokens
+                if is_done and rank >= nb:
+                    continue
+                if not is_done and len(running) >= nb:
+                    continue
+                child = self._child(parent, token, cum)
+                born.append((parent, child))
+                (finished if is_done else running).append(child if is_done else (parent, child))
             finished.sort(key=lambda c: c.score(), reverse=True)
+            for dropped in finished[nb:]:
+                released.append(dropped)
             del finished[nb:]
             best_running = max((c.score() for _, c in running), default=float("-inf"))
             stop = len(finished) >= nb and (params.early_stopping or finished[-1].score() >= best_running)
             if not running or stop:
                 self.finished_beams.pop(rid, None)
-                self._finish(finished[0], finished[0].token_ids[finished[0].prompt_len:])
-                done.append(rid)
+                emitted.append(finished[0])
+                released.extend(finished)
+                released.extend(c for _, c in running)
+                done_rids.append(rid)
             else:
                 for parent, child in running:
                     self.blocks.fork(parent, child)
                     self.running.append(child)
+        if born:  # children's token rows: the parent's row plus the new token
+            meta = torch.tensor([[p.slot for p, _ in born], [c.slot for _, c in born],
+                                 [p.length for p, _ in born], [c.last_token for _, c in born]],
+                                dtype=torch.long).pin_memory().to(self.device, non_blocking=True)
+            self.tokens[meta[1]] = self.tokens[meta[0]]
+            self.tokens[meta[1], meta[2]] = meta[3].to(torch.int32)
+        self._emit(emitted)
         for s in seqs:
             self._remove(s)
-        return done
+        for c in released:  # finished hypotheses hold a token row but no blocks
+            self.free_slots.append(c.slot)
+        return done_rids

@@ -105,7 +105,7 @@ class _StepGraph:
         pos = hv[B * M: B * M + B]
         pos[:b] = [s.num_cached_tokens for s in seqs]
         pos[b:] = -1
-        hv[B * M + B: B * M + B + b] = [s.token_ids[-1] for s in seqs]
+        hv[B * M + B: B * M + B + b] = [s.last_token for s in seqs]
         self.dev_in.copy_(self.host_in, non_blocking=True)
         key = tuple(s.request_id for s in seqs)
         if key != self.cross_key:

@@ -72,15 +72,17 @@ class PagedSeq2Seq:
 
     # ------------------------------------------------------------------------------- encoder
     @torch.inference_mode()
-    def encode(self, input_ids: torch.Tensor, pixel_values: torch.Tensor | None = None) -> torch.Tensor:
-        """Encoder hidden states [G, S, d_model] for a group of equal-length prompts."""
+    def encode(self, input_ids: torch.Tensor, pixel_values: torch.Tensor | None = None,
+               attention_mask: torch.Tensor | None = None) -> torch.Tensor:
+        """Encoder hidden states [G, S, d_model] for a batch of prompts (right-padded and masked
+        when their lengths differ; padded positions are never paged)."""
         if pixel_values is None:
-            return self.lm.encoder(input_ids=input_ids).last_hidden_state
+            return self.lm.encoder(input_ids=input_ids, attention_mask=attention_mask).last_hidden_state
         feats = self.hf.model.get_image_features(pixel_values.to(self.dtype)).pooler_output
         embeds = self.lm.get_input_embeddings()(input_ids)
         mask = (input_ids == self.image_token_id).unsqueeze(-1).expand_as(embeds)
         embeds = embeds.masked_scatter(mask, feats.to(embeds.dtype))
-        return self.lm.encoder(inputs_embeds=embeds).last_hidden_state
+        return self.lm.encoder(inputs_embeds=embeds, attention_mask=attention_mask).last_hidden_state
 
     def cross_kv(self, layer: int, hidden: torch.Tensor):
         """Encoder K/V of one decoder layer as [G*S, H, head_dim] views of one fused GEMM."""

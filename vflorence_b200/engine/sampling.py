@@ -91,70 +91,60 @@ class LogitsRules:
         self.forced_eos = keep(_as_list(params.forced_eos_token_id))
         self.needs_history = params.repetition_penalty != 1.0 or params.no_repeat_ngram_size > 0
 
-    def __call__(self, scores: torch.Tensor, histories: list[list[int]]) -> torch.Tensor:
+    def __call__(self, scores: torch.Tensor, hist: torch.Tensor | None, lengths: torch.Tensor) -> torch.Tensor:
+        """``scores`` [rows, vocab] float (modified in place). ``hist`` [rows, W] int32: row i's
+        decoder tokens (start token first) in columns [0, lengths[i]), anything after; only read
+        when a rule needs the history. ``lengths`` int64 [rows] on the same device."""
         p = self.p
-        lengths = [len(h) for h in histories]
-        hist = None
+        dev = scores.device
         if self.needs_history:
-            width = max(lengths)
-            hist = torch.tensor([[-1] * (width - len(h)) + h for h in histories], dtype=torch.long,
-                                device=scores.device)
-        if p.repetition_penalty != 1.0:  # every token already in the row's history (not padding)
-            rows, cols = torch.where(hist >= 0)
-            tokens = hist[rows, cols]
+            cols = torch.arange(hist.shape[1], device=dev)
+            real = cols.unsqueeze(0) < lengths.unsqueeze(1)          # [rows, W]
+        if p.repetition_penalty != 1.0:  # every token already in the row's history
+            rows, pos = torch.where(real)
+            tokens = hist[rows, pos].long()
             seen = scores[rows, tokens]
-            scores[rows, tokens] = torch.where(seen < 0, seen * p.repetition_penalty,
-                                               seen / p.repetition_penalty)
+            scores[rows, tokens] = torch.where(seen < 0, seen * p.repetition_penalty, seen / p.repetition_penalty)
         if p.no_repeat_ngram_size > 0:
             self._ban_repeated_ngrams(scores, hist, lengths)
         if p.min_length > 0 and self.eos.numel():
-            rows = [i for i, n in enumerate(lengths) if n < p.min_length]
-            if rows:
-                r = torch.tensor(rows, device=scores.device)
-                scores[r.unsqueeze(1), self.eos.unsqueeze(0)] = NEG_INF
+            short = (lengths < p.min_length).unsqueeze(1)
+            scores[:, self.eos] = scores[:, self.eos].masked_fill(short, NEG_INF)
         if self.forced_bos:
-            self._force(scores, [i for i, n in enumerate(lengths) if n == 1], self.forced_bos)
+            self._force(scores, lengths == 1, self.forced_bos)
         if self.forced_eos:
-            self._force(scores, [i for i, n in enumerate(lengths) if n == self.max_length - 1], self.forced_eos)
+            self._force(scores, lengths == self.max_length - 1, self.forced_eos)
         if self.suppress.numel():
             scores[:, self.suppress] = NEG_INF
         if self.begin_suppress.numel():
-            rows = [i for i, n in enumerate(lengths) if n == self.begin_index]
-            if rows:
-                r = torch.tensor(rows, device=scores.device)
-                scores[r.unsqueeze(1), self.begin_suppress.unsqueeze(0)] = NEG_INF
+            first = (lengths == self.begin_index).unsqueeze(1)
+            scores[:, self.begin_suppress] = scores[:, self.begin_suppress].masked_fill(first, NEG_INF)
         return scores
 
     @staticmethod
-    def _force(scores, rows, ids):
-        """Make ``ids`` the only choice of each row in ``rows``: score 0 for them, -inf else."""
-        if not rows:
-            return
-        r = torch.tensor(rows, device=scores.device)
-        scores[r] = NEG_INF
-        scores[r.unsqueeze(1), torch.tensor(ids, device=scores.device).unsqueeze(0)] = 0.0
+    def _force(scores, rows_mask, ids):
+        """Make ``ids`` the only choice of each masked row: score 0 for them, -inf else."""
+        ids_t = torch.tensor(ids, device=scores.device)
+        keep = rows_mask.unsqueeze(1)
+        forced = torch.full_like(scores, NEG_INF)
+        forced[:, ids_t] = 0.0
+        scores.copy_(torch.where(keep, forced, scores))
 
     def _ban_repeated_ngrams(self, scores, hist, lengths):
+        """Ban every token that would complete an n-gram already in the row's history (rows
+        shorter than n - 1 tokens ban nothing)."""
         n = self.p.no_repeat_ngram_size
-        width = hist.shape[1]
-        if width < n:
+        W = hist.shape[1]
+        if W < n:
             return
-        windows = hist.unfold(1, n, 1)                 # [rows, width - n + 1, n]
-        tail = hist[:, width - (n - 1):] if n > 1 else hist[:, :0]
-        match = (windows[:, :, : n - 1] == tail.unsqueeze(1)).all(-1) & (windows >= 0).all(-1)
-        ok = torch.tensor([ln + 1 >= n for ln in lengths], device=scores.device)
-        match &= ok.unsqueeze(1)
+        dev = scores.device
+        windows = hist.unfold(1, n, 1)                                   # [rows, W - n + 1, n]
+        starts = torch.arange(W - n + 1, device=dev)
+        inside = starts.unsqueeze(0) + n <= lengths.unsqueeze(1)         # window within the row
+        tail_pos = (lengths.unsqueeze(1) - (n - 1) + torch.arange(n - 1, device=dev)).clamp(min=0)
+        tail = hist.gather(1, tail_pos)                                  # last n - 1 tokens
+        match = (windows[:, :, : n - 1] == tail.unsqueeze(1)).all(-1) & inside
+        match &= (lengths + 1 >= n).unsqueeze(1)
         rows, cols = match.nonzero(as_tuple=True)
         if rows.numel():
-            scores[rows, windows[rows, cols, n - 1]] = NEG_INF
-
-
-def select_beam_candidates(seqs, top_scores, top_ids, keep: int):
-    """Per request: its rows' (row, token, score) candidates, best ``keep`` first (stable)."""
-    by_req: dict[int, list] = {}
-    for row, (seq, scores, ids) in enumerate(zip(seqs, top_scores, top_ids)):
-        by_req.setdefault(seq.request_id, []).extend((row, t, s) for t, s in zip(ids, scores))
-    for cands in by_req.values():
-        cands.sort(key=lambda c: c[2], reverse=True)
-        del cands[keep:]
-    return by_req
+            scores[rows, windows[rows, cols, n - 1].long()] = NEG_INF
