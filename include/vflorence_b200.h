@@ -33,14 +33,15 @@
 extern "C" {
 #endif
 
-#define VFL_ABI_VERSION 1
+#define VFL_ABI_VERSION 2
 
 typedef enum vfl_status {
   VFL_OK = 0,
   VFL_ERR_INVALID_ARGUMENT = 1, /* shape, stride, alignment, dtype or range error */
   VFL_ERR_UNSUPPORTED = 2,      /* valid for the reference, not built here (e.g. head_dim) */
   VFL_ERR_WORKSPACE = 3,        /* workspace missing or smaller than the plan needs */
-  VFL_ERR_CUDA = 4              /* a CUDA runtime call failed (launch, attribute, copy) */
+  VFL_ERR_CUDA = 4,             /* a CUDA runtime call failed (launch, attribute, copy) */
+  VFL_ERR_CAPACITY = 5          /* a host pool is exhausted (KV blocks, hypothesis slots) */
 } vfl_status;
 
 typedef enum vfl_dtype {

@@ -1,5 +1,6 @@
-"""The C-ABI library without a GPU: it loads, exports exactly what include/vflorence_b200.h
-declares, and its host-only entry points (get_isa, the planner, argument validation) behave."""
+"""The C-ABI library without a GPU: it loads, exports exactly what include/vflorence_b200.h and
+include/vflorence_b200_runtime.h declare, and its host-only entry points (get_isa, the planner,
+argument validation) behave."""
 
 from __future__ import annotations
 
@@ -14,8 +15,11 @@ from conftest import REPO
 
 
 def _declared():
-    text = open(os.path.join(REPO, "include", "vflorence_b200.h")).read()
-    return re.findall(r"^(?:int|const char\*)\s+(vfl_\w+)\(", text, flags=re.M)
+    names = []
+    for header in ("vflorence_b200.h", "vflorence_b200_runtime.h"):
+        text = open(os.path.join(REPO, "include", header)).read()
+        names += re.findall(r"^(?:int|void|const char\*)\s+(vfl_\w+)\(", text, flags=re.M)
+    return names
 
 
 def test_library_exports_every_declared_symbol(native):
@@ -25,12 +29,13 @@ def test_library_exports_every_declared_symbol(native):
     assert sorted(declared) == sorted(_native.EXPORTS)
     for name in declared:
         assert hasattr(native, name), name
-    assert native.vfl_abi_version() == 1
+    assert native.vfl_abi_version() == _native.ABI_VERSION == 2
 
 
 def test_status_strings(native):
     assert native.vfl_status_string(0) == b"ok"
     assert b"workspace" in native.vfl_status_string(3)
+    assert b"capacity" in native.vfl_status_string(5)
 
 
 def test_get_isa(native):

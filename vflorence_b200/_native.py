@@ -1,4 +1,5 @@
-"""ctypes binding of ``libvflorence_b200.so`` (the C ABI declared in ``include/vflorence_b200.h``).
+"""ctypes binding of ``libvflorence_b200.so`` (the C ABI declared in ``include/vflorence_b200.h``
+and ``include/vflorence_b200_runtime.h``).
 
 This is the whole Python<->native boundary: plain pointers, sizes and a stream handle go in, a
 status code comes out. A missing or unloadable library raises at first use - there is no
@@ -18,6 +19,8 @@ VFL_ERR_INVALID_ARGUMENT = 1
 VFL_ERR_UNSUPPORTED = 2
 VFL_ERR_WORKSPACE = 3
 VFL_ERR_CUDA = 4
+VFL_ERR_CAPACITY = 5
+ABI_VERSION = 2
 
 DTYPE_F32 = 0
 DTYPE_BF16 = 1
@@ -46,6 +49,26 @@ EXPORTS = (
     "vfl_copy_blocks",
     "vfl_prepare_decode",
     "vfl_paged_slots",
+    # host decode runtime (vflorence_b200_runtime.h)
+    "vfl_rt_create",
+    "vfl_rt_destroy",
+    "vfl_rt_reset",
+    "vfl_rt_slot_acquire",
+    "vfl_rt_slot_release",
+    "vfl_rt_num_free_blocks",
+    "vfl_rt_free_block_ids",
+    "vfl_rt_ref_count",
+    "vfl_rt_block_table",
+    "vfl_rt_required_new_blocks",
+    "vfl_rt_ensure_capacity",
+    "vfl_rt_fork",
+    "vfl_rt_deallocate",
+    "vfl_rt_admit",
+    "vfl_rt_num_running",
+    "vfl_rt_prepare_step",
+    "vfl_rt_pack_step",
+    "vfl_rt_advance_greedy",
+    "vfl_rt_advance_beam",
 )
 
 
@@ -74,6 +97,37 @@ class AttentionPlan(ctypes.Structure):
 
 
 PLAN_BYTES = ctypes.sizeof(AttentionPlan)
+
+
+class DecodeRules(ctypes.Structure):
+    """Mirror of ``vfl_decode_rules``."""
+
+    _fields_ = [
+        ("num_beams", ctypes.c_int32),
+        ("max_tokens", ctypes.c_int32),
+        ("length_penalty", ctypes.c_double),
+        ("early_stopping", ctypes.c_int32),
+        ("num_eos", ctypes.c_int32),
+        ("eos_ids", ctypes.c_void_p),
+    ]
+
+
+class StepResult(ctypes.Structure):
+    """Mirror of ``vfl_step_result``."""
+
+    _fields_ = [
+        ("born_parent", ctypes.c_void_p),
+        ("born_child", ctypes.c_void_p),
+        ("born_pos", ctypes.c_void_p),
+        ("born_token", ctypes.c_void_p),
+        ("born_cap", ctypes.c_int32),
+        ("num_born", ctypes.c_int32),
+        ("done_request", ctypes.c_void_p),
+        ("done_slot", ctypes.c_void_p),
+        ("done_length", ctypes.c_void_p),
+        ("done_cap", ctypes.c_int32),
+        ("num_done", ctypes.c_int32),
+    ]
 
 
 class VflError(RuntimeError):
@@ -106,6 +160,26 @@ def _declare(L):
         "vfl_copy_blocks": (i32, [vp, vp, i32, vp, i32, i64, i64, vp]),
         "vfl_prepare_decode": (i32, [vp, i64, i32, vp, i32, i32, vp, vp, vp, vp]),
         "vfl_paged_slots": (i32, [vp, i64, i32, i32, i32, i32, vp, vp]),
+        "vfl_rt_create": (i32, [i32, i32, i32, i32, ctypes.POINTER(vp)]),
+        "vfl_rt_destroy": (None, [vp]),
+        "vfl_rt_reset": (i32, [vp]),
+        "vfl_rt_slot_acquire": (i32, [vp, vp]),
+        "vfl_rt_slot_release": (i32, [vp, i32]),
+        "vfl_rt_num_free_blocks": (i32, [vp, vp]),
+        "vfl_rt_free_block_ids": (i32, [vp, vp, i32, vp]),
+        "vfl_rt_ref_count": (i32, [vp, i32, vp]),
+        "vfl_rt_block_table": (i32, [vp, i32, vp, i32, vp]),
+        "vfl_rt_required_new_blocks": (i32, [vp, vp, vp, i32, vp]),
+        "vfl_rt_ensure_capacity": (i32, [vp, i32, i32, vp, vp]),
+        "vfl_rt_fork": (i32, [vp, i32, i32]),
+        "vfl_rt_deallocate": (i32, [vp, i32]),
+        "vfl_rt_admit": (i32, [vp, i64, i32, vp]),
+        "vfl_rt_num_running": (i32, [vp, vp]),
+        "vfl_rt_prepare_step": (i32, [vp, vp, i32, vp]),
+        "vfl_rt_pack_step": (i32, [vp, i32, vp, i64, i32, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp]),
+        "vfl_rt_advance_greedy": (i32, [vp, ctypes.POINTER(DecodeRules), vp, i32, ctypes.POINTER(StepResult)]),
+        "vfl_rt_advance_beam": (i32, [vp, ctypes.POINTER(DecodeRules), vp, vp, vp, i32, i32,
+                                      ctypes.POINTER(StepResult)]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -125,7 +199,7 @@ def lib():
                         "(run `python -m vflorence_b200.build`)")
                 L = ctypes.CDLL(LIB_PATH)
                 _declare(L)
-                if L.vfl_abi_version() != 1:
+                if L.vfl_abi_version() != ABI_VERSION:
                     raise ImportError("vflorence_b200: library ABI version mismatch")
                 _lib = L
     return _lib

@@ -9,56 +9,61 @@ allocator's (vflorence/engine/block_manager.py:1-73) bit for bit, so the policy 
   * a sequence's blocks are released last block first (block_manager.py:69-72);
   * a token written into a block held by several sequences goes to a private copy, except for
     the last holder, which writes in place (block_manager.py:28-59).
+
+The bookkeeping itself is native (``vfl_rt_*`` of the host decode runtime); this class keeps
+the reference's interface on sequence objects (anything with ``block_table`` and
+``num_cached_tokens``), mirroring each sequence's table after every call.
 """
 
 from __future__ import annotations
 
-from collections import deque
+from .runtime import DecodeRuntime
 
 
 class BlockManager:
-    def __init__(self, num_blocks: int, block_size: int):
+    def __init__(self, num_blocks: int, block_size: int, *, num_slots: int = 1024,
+                 max_blocks_per_seq: int | None = None, runtime: DecodeRuntime | None = None):
         if num_blocks <= 0 or block_size <= 0:
             raise ValueError("num_blocks and block_size must be positive")
         self.num_blocks = num_blocks
         self.block_size = block_size
-        self.reset()
+        self.rt = runtime or DecodeRuntime(num_blocks, block_size, num_slots, max_blocks_per_seq or num_blocks)
+        self._generation = 0
+
+    @classmethod
+    def over(cls, runtime: DecodeRuntime) -> "BlockManager":
+        """A view of an engine's runtime (the engine drives it through the batched calls)."""
+        return cls(runtime.num_blocks, runtime.block_size, runtime=runtime)
 
     def reset(self) -> None:
         """Forget every allocation (after an aborted batch)."""
-        self.ref_counts = [0] * self.num_blocks
-        self.free_block_ids = deque(range(self.num_blocks))
+        self.rt.reset()
+        self._generation += 1
 
     @property
     def num_free_blocks(self) -> int:
-        return len(self.free_block_ids)
+        return self.rt.num_free_blocks
 
-    def _take(self) -> int:
-        if not self.free_block_ids:
-            raise RuntimeError("KV cache is full; increase num_blocks")
-        block = self.free_block_ids.popleft()
-        self.ref_counts[block] = 1
-        return block
+    @property
+    def free_block_ids(self) -> list[int]:
+        """Free block ids in hand-out order."""
+        return self.rt.free_block_ids()
 
-    def _next_index(self, seq) -> int:
-        return seq.num_cached_tokens // self.block_size
+    @property
+    def ref_counts(self) -> list[int]:
+        return self.rt.ref_counts()
+
+    def _slot(self, seq) -> int:
+        if getattr(seq, "_bm_owner", None) != (id(self), self._generation):
+            seq._bm_slot = self.rt.slot_acquire()
+            seq._bm_owner = (id(self), self._generation)
+        return seq._bm_slot
 
     def required_new_blocks(self, seqs) -> int:
         """Blocks that appending one token to every sequence in ``seqs`` will take: fresh
         blocks plus private copies of shared blocks (all holders but the last copy)."""
-        needed = 0
-        left = {}  # shared block -> holders that have not claimed a copy yet
-        for seq in seqs:
-            idx = self._next_index(seq)
-            if idx >= len(seq.block_table):
-                needed += 1
-                continue
-            block = seq.block_table[idx]
-            holders = left.get(block, self.ref_counts[block])
-            if holders > 1:
-                needed += 1
-                left[block] = holders - 1
-        return needed
+        seqs = list(seqs)
+        return self.rt.required_new_blocks([self._slot(s) for s in seqs], [s.num_cached_tokens for s in seqs])
 
     def ensure_capacity(self, seq) -> tuple[int, int] | None:
         """Make the block that ``seq``'s next token lands in writable.
@@ -66,28 +71,21 @@ class BlockManager:
         Appends a fresh block when the table is full, or swaps a shared block for a private one
         and returns the ``(src, dst)`` pair whose contents must be copied before the write.
         """
-        idx = self._next_index(seq)
-        if idx >= len(seq.block_table):
-            seq.block_table.append(self._take())
-            return None
-        src = seq.block_table[idx]
-        if self.ref_counts[src] == 1:
-            return None
-        dst = self._take()
-        self.ref_counts[src] -= 1
-        seq.block_table[idx] = dst
-        return src, dst
+        slot = self._slot(seq)
+        pair = self.rt.ensure_capacity(slot, seq.num_cached_tokens)
+        seq.block_table[:] = self.rt.block_table(slot)
+        return pair
 
     def fork(self, parent, child) -> None:
         """``child`` shares every block of ``parent`` (one more reference each)."""
-        child.block_table = list(parent.block_table)
-        for block in child.block_table:
-            self.ref_counts[block] += 1
+        slot = self._slot(child)
+        self.rt.fork(self._slot(parent), slot)
+        child.block_table = self.rt.block_table(slot)
 
     def deallocate(self, seq) -> None:
         """Drop ``seq``'s references, last block first; blocks nobody holds become free."""
-        for block in reversed(seq.block_table):
-            self.ref_counts[block] -= 1
-            if self.ref_counts[block] == 0:
-                self.free_block_ids.append(block)
+        slot = self._slot(seq)
+        self.rt.deallocate(slot)
         seq.block_table.clear()
+        self.rt.slot_release(slot)
+        seq._bm_owner = None

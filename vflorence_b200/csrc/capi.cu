@@ -82,6 +82,7 @@ const char* vfl_status_string(int status) {
     case VFL_ERR_UNSUPPORTED: return "unsupported configuration";
     case VFL_ERR_WORKSPACE: return "workspace missing or too small";
     case VFL_ERR_CUDA: return "CUDA runtime error";
+    case VFL_ERR_CAPACITY: return "capacity exhausted";
     default: return "unknown status";
   }
 }

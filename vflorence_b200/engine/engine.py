@@ -2,25 +2,31 @@
 
 One step (the same order as the reference engine, vflorence/engine/llm_engine.py:57-63):
   1. admit waiting requests while their beams fit in ``max_num_seqs``;
-  2. make room for every running sequence's next token (BlockManager; copy-on-write pairs);
-  3. encode the step's new requests (grouped by prompt length and image shape) and page their
+  2. make room for every running row's next token (native runtime; copy-on-write pairs);
+  3. encode the step's new requests (one padded batch per image shape) and page their
      encoder K/V into the cross pool, once per request;
   4. copy-on-write copies (one launch), device-side step metadata (one upload, one kernel),
      cross staging (memoised on the batch's request ids), then one decoder forward;
-  5. greedy argmax or beam candidates on the GPU; forks, finishes and frees on the host.
+  5. greedy argmax or beam candidates on the GPU, one small copy back, and the step's
+     decisions (forks, finishes, frees) in the native runtime.
+
+The per-row bookkeeping - block tables, reference counts, hypotheses, finished beams - lives in
+the host decode runtime (``vflorence_b200.runtime``, C++); Python handles whole requests.
 """
 
 from __future__ import annotations
 
 import math
 from collections import deque
-from dataclasses import dataclass, field
+from dataclasses import dataclass
 
+import numpy as np
 import torch
 
 from ..block_manager import BlockManager
 from ..context import set_context
 from ..kv_cache import PagedKVCache
+from ..runtime import DecodeRules, DecodeRuntime, StepResult, StepRows
 from .model import PagedSeq2Seq
 from .sampling import LogitsRules, SamplingParams
 
@@ -32,31 +38,14 @@ class Request:
 
 
 @dataclass(eq=False)
-class _Seq:
-    """One hypothesis. Its decoder tokens live in row ``slot`` of the engine's device token
-    buffer (start token first); the host keeps only the last token and the length."""
+class _Req:
+    """A request's host-side state; its hypotheses live in the native runtime, their decoder
+    tokens in rows of the engine's device token buffer."""
 
     request_id: int
     encoder_ids: list[int]
     params: SamplingParams
-    slot: int
-    last_token: int
-    length: int = 1
     pixel_values: torch.Tensor | None = None
-    block_table: list[int] = field(default_factory=list)
-    num_cached_tokens: int = 0
-    cum_logprob: float = 0.0
-    prompt_len: int = 1
-
-    @property
-    def num_generated(self) -> int:
-        return self.length - self.prompt_len
-
-    def finished(self, eos: set[int]) -> bool:
-        return self.last_token in eos or self.num_generated >= self.params.max_tokens
-
-    def score(self) -> float:
-        return self.cum_logprob / (max(self.num_generated, 1) ** self.params.length_penalty)
 
 
 class Engine:
@@ -71,31 +60,41 @@ class Engine:
         self.max_decoder_len = max_decoder_len
         self.max_encoder_len = max_encoder_len
         self.num_blocks = num_blocks or max_num_seqs * math.ceil(max_decoder_len / block_size)
+        # a row caches at most max_decoder_len tokens: its table never exceeds this
+        self.max_blocks = math.ceil((max_decoder_len + 1) / block_size)
         num_cross = max_num_seqs * math.ceil(max_encoder_len / block_size)
         self.kv = PagedKVCache(num_layers=len(m.layers), num_heads=m.num_heads, head_dim=m.head_dim,
                                block_size=block_size, num_blocks=self.num_blocks, num_cross_blocks=num_cross,
                                dtype=self.dtype, device=self.device)
         self.kv.bind(m.layers)
-        self.blocks = BlockManager(self.num_blocks, block_size)
         cfg = hf_model.config.get_text_config()
         self.start_token = cfg.decoder_start_token_id if decoder_start_token_id is None else decoder_start_token_id
-        # decoder tokens of every live hypothesis, one row each. Beam children take fresh rows,
-        # so a step can hold parents, their children (up to 2 per kept beam) and the finished
-        # hypotheses kept per request: at most 4 rows per sequence slot
-        self.tokens = torch.zeros(4 * max_num_seqs + 4, max_decoder_len + 2, dtype=torch.int32, device=self.device)
-        self.free_slots = list(range(self.tokens.shape[0]))
-        self.waiting: deque[_Seq] = deque()
-        self.running: list[_Seq] = []
-        self.finished_beams: dict[int, list[_Seq]] = {}
+        self._make_runtime(4)
+        M, W = max_num_seqs, self.max_blocks
+        self._eager_host = torch.zeros(M * (W + 1), dtype=torch.int32).pin_memory()
+        self._meta_host = torch.zeros(5 * M, dtype=torch.int32).pin_memory()
+        self._meta_dev = torch.zeros(5 * M, dtype=torch.int32, device=self.device)
+        self._born_host = self._born_dev = None
+        self.waiting: deque[_Req] = deque()
+        self.requests: dict[int, _Req] = {}  # admitted and not finished
         self.outputs: dict[int, list[int]] = {}
         self._next_id = 0
-        self._rules: tuple[SamplingParams, LogitsRules] | None = None
+        self._rules: tuple[SamplingParams, LogitsRules, DecodeRules] | None = None
         self.record = [] if record_steps else None
         self.graphs = None
         if cuda_graphs:
             from .graphs import GraphedDecoder
 
             self.graphs = GraphedDecoder(self)
+
+    def _make_runtime(self, slots_per_row: int) -> None:
+        """Hypothesis slots (token rows) for ``slots_per_row`` per running row: a beam step holds
+        the parents, up to beams_to_keep children per request and the kept finished beams."""
+        self.slots_per_row = slots_per_row
+        self.num_slots = slots_per_row * self.max_num_seqs + 4
+        self.rt = DecodeRuntime(self.num_blocks, self.block_size, self.num_slots, self.max_blocks)
+        self.blocks = BlockManager.over(self.rt)
+        self.tokens = torch.zeros(self.num_slots, self.max_decoder_len + 2, dtype=torch.int32, device=self.device)
 
     # -------------------------------------------------------------------------------- requests
     def add_request(self, request: Request, params: SamplingParams) -> int:
@@ -108,18 +107,21 @@ class Engine:
             raise ValueError(f"max_tokens {params.max_tokens} exceeds max_decoder_len {self.max_decoder_len}")
         if params.num_beams > self.max_num_seqs:
             raise ValueError("num_beams exceeds max_num_seqs")
-        if self.waiting or self.running:
-            other = (self.waiting or self.running)[0].params
+        if self.waiting or self.requests:
+            other = (self.waiting[0] if self.waiting else next(iter(self.requests.values()))).params
             if other != params:
                 raise ValueError("all active requests must share the same SamplingParams")
+        else:
+            need = 2 + params.beams_to_keep() // params.num_beams if params.num_beams > 1 else 1
+            if need > self.slots_per_row:
+                self._make_runtime(need)
         rid = self._next_id
         self._next_id += 1
-        self.waiting.append(_Seq(rid, list(request.input_ids), params, -1, self.start_token,
-                                 pixel_values=request.pixel_values))
+        self.waiting.append(_Req(rid, list(request.input_ids), params, request.pixel_values))
         return rid
 
     def is_finished(self) -> bool:
-        return not self.waiting and not self.running
+        return not self.waiting and not self.requests
 
     @torch.inference_mode()
     def generate(self, requests, params: SamplingParams) -> list[list[int]]:
@@ -134,62 +136,65 @@ class Engine:
 
     def abort(self) -> None:
         self.waiting.clear()
-        self.running.clear()
-        self.finished_beams.clear()
-        self.blocks.reset()
+        self.requests.clear()
+        self.rt.reset()
         self.kv.reset()
-        self.free_slots = list(range(self.tokens.shape[0]))
         set_context()
 
     # ------------------------------------------------------------------------------------ step
     @torch.inference_mode()
     def step(self) -> list[int]:
-        seqs, copies = self._schedule()
-        if not seqs:
+        params = self._admit()
+        n = self.rt.num_running
+        if n == 0:
             return []
-        fresh = [s for s in seqs if s.num_cached_tokens == 0]
-        if fresh:
-            self._encode(fresh)
+        copies = self.rt.prepare_step()
+        g = self.graphs.graph_for(n, params.num_beams) if self.graphs is not None else None
+        if g is not None:
+            rows = self.rt.pack_step(*g.host_views())
+        else:
+            W = self.max_blocks
+            host = self._eager_host.numpy()[: n * W + n]
+            rows = self.rt.pack_step(host[: n * W].reshape(n, W), host[n * W:])
+        fresh = np.flatnonzero(rows.positions == 0)
+        if len(fresh):
+            self._encode([self.requests[int(r)] for r in rows.request_ids[fresh]])
         self.kv.copy_blocks(copies)
-        tables = [s.block_table for s in seqs]
-        positions = [s.num_cached_tokens for s in seqs]
         if self.record is not None:
-            self.record.append({"request_ids": [s.request_id for s in seqs], "positions": list(positions),
-                                "block_tables": [list(t) for t in tables], "copies": list(copies)})
-        logits = self.graphs.run(seqs) if self.graphs is not None else None
-        if logits is None:  # eager step
-            st = self.kv.prepare_decode(tables, positions)
-            staged = self.kv.stage_cross(self.model.layers, [s.request_id for s in seqs])
+            tables = g.host_views()[0] if g is not None else host[: n * W].reshape(n, W)
+            self.record.append({"request_ids": rows.request_ids.tolist(), "positions": rows.positions.tolist(),
+                                "block_tables": [tables[i, :k].tolist() for i, k in enumerate(rows.table_lens)],
+                                "copies": [tuple(c) for c in copies.tolist()]})
+        if g is not None:
+            logits = g.launch(rows)
+        else:
+            st = self.kv.prepare_decode_host(self._eager_host[: n * W + n], n, W)
+            staged = self.kv.stage_cross(self.model.layers, rows.request_ids.tolist())
             set_context(context_lens=st.context_lens, block_tables=st.block_tables, slot_mapping=st.slot_mapping,
                         query_start_loc=st.query_start_loc, self_metadata=st.self_metadata, isa=self.kv.isa,
                         cross_staged=staged)
             try:
-                ids = torch.tensor([s.last_token for s in seqs], dtype=torch.long).pin_memory()
-                logits = self.model.decode(ids.to(self.device, non_blocking=True), st.positions.long())
+                ids = torch.from_numpy(rows.tokens).to(self.device, non_blocking=True)
+                logits = self.model.decode(ids.long(), st.positions.long())
             finally:
                 set_context()
-        for s in seqs:
-            s.num_cached_tokens += 1
-        if seqs[0].params.num_beams == 1:
-            return self._finish_greedy(seqs, logits)
-        return self._finish_beam(seqs, logits)
+        meta = self._upload_rows(rows)
+        if params.num_beams == 1:
+            return self._finish_greedy(params, rows, meta, logits)
+        return self._finish_beam(params, rows, meta, logits)
 
-    def _schedule(self):
-        used = sum({s.request_id: s.params.num_beams for s in self.running}.values())
+    def _admit(self) -> SamplingParams | None:
+        """Admit waiting requests while their beams fit (scheduler.py:37-48)."""
+        used = sum(r.params.num_beams for r in self.requests.values())
         admitted = []
         while self.waiting and used + self.waiting[0].params.num_beams <= self.max_num_seqs:
-            s = self.waiting.popleft()
-            s.slot = self.free_slots.pop()
-            self.running.append(s)
-            admitted.append(s.slot)
-            used += s.params.num_beams
+            r = self.waiting.popleft()
+            admitted.append(self.rt.admit(r.request_id, self.start_token))
+            self.requests[r.request_id] = r
+            used += r.params.num_beams
         if admitted:
             self.tokens[torch.tensor(admitted, device=self.device), 0] = self.start_token
-        seqs = list(self.running)
-        if self.blocks.required_new_blocks(seqs) > self.blocks.num_free_blocks:
-            raise RuntimeError("KV cache is full; increase num_blocks")
-        copies = [c for s in seqs if (c := self.blocks.ensure_capacity(s)) is not None]
-        return seqs, copies
+        return next(iter(self.requests.values())).params if self.requests else None
 
     def _encode(self, fresh) -> None:
         """Page the encoder K/V of this step's new requests.
@@ -231,144 +236,88 @@ class Engine:
                 k, v = self.model.cross_kv(layer, hidden)
                 self.kv.write_encoder_kv(layer, k, v, slots)
 
-    def _rules_for(self, params: SamplingParams) -> LogitsRules:
+    def _rules_for(self, params: SamplingParams) -> tuple[LogitsRules, DecodeRules]:
         if self._rules is None or self._rules[0] is not params:
-            self._rules = (params, LogitsRules(params, self.model.vocab_size, self.device))
-        return self._rules[1]
+            self._rules = (params, LogitsRules(params, self.model.vocab_size, self.device),
+                           DecodeRules.from_params(params))
+        return self._rules[1], self._rules[2]
 
-    def _rows_state(self, seqs):
-        """Device views for the rules: token rows and lengths of ``seqs``."""
-        meta = torch.tensor([[s.slot for s in seqs], [s.length for s in seqs]], dtype=torch.long).pin_memory()
-        meta = meta.to(self.device, non_blocking=True)
-        rules = self._rules_for(seqs[0].params)
-        hist = self.tokens[meta[0]] if rules.needs_history else None
-        return rules, meta[0], meta[1], hist
+    def _upload_rows(self, rows: StepRows) -> torch.Tensor:
+        """Rows' slots, lengths, request groups, ranks and cumulative log-probs on the device:
+        int32 [5, n] (the last row holds float32 bits), one pinned copy."""
+        n = rows.n
+        host = self._meta_host.numpy()[: 5 * n].reshape(5, n)
+        host[0], host[1], host[2], host[3] = rows.slots, rows.lengths, rows.groups, rows.ranks
+        host[4] = rows.cum_logprobs.view(np.int32)
+        dev = self._meta_dev[: 5 * n]
+        dev.copy_(self._meta_host[: 5 * n], non_blocking=True)
+        return dev.view(5, n)
 
-    def _emit(self, done: list[_Seq]) -> None:
-        """Record finished hypotheses' generated tokens (one copy for the step) and release them."""
+    def _emit(self, res: StepResult) -> list[int]:
+        """Record finished requests' generated tokens (one copy for the step) and release them."""
+        done = res.done_request.tolist()
         if not done:
-            return
-        width = max(s.length for s in done)
-        rows = self.tokens[torch.tensor([s.slot for s in done], device=self.device), :width].tolist()
-        for s, row in zip(done, rows):
-            self.outputs[s.request_id] = row[s.prompt_len: s.length]
-            self.kv.clear_request(s.request_id)
+            return done
+        width = int(res.done_length.max())
+        slots = torch.from_numpy(res.done_slot.astype(np.int64)).to(self.device)
+        rows = self.tokens[slots, :width].cpu().numpy()
+        for rid, row, length in zip(done, rows, res.done_length.tolist()):
+            self.outputs[rid] = row[1:length].tolist()
+            self.kv.clear_request(rid)
+            del self.requests[rid]
+        return done
 
-    def _remove(self, seq: _Seq) -> None:
-        self.running.remove(seq)
-        self.blocks.deallocate(seq)
-        self.free_slots.append(seq.slot)
-
-    def _finish_greedy(self, seqs, logits) -> list[int]:
-        params = seqs[0].params
-        rules, slots, lengths, hist = self._rows_state(seqs)
+    def _finish_greedy(self, params, rows: StepRows, meta: torch.Tensor, logits) -> list[int]:
+        rules, drules = self._rules_for(params)
+        slots, lengths = meta[0].long(), meta[1].long()
+        hist = self.tokens[slots] if rules.needs_history else None
         picks = rules(logits.float(), hist, lengths).argmax(dim=-1)
         self.tokens[slots, lengths] = picks.to(torch.int32)
-        eos = set(params.eos_ids())
-        done = []
-        for s, t in zip(seqs, picks.tolist()):
-            s.last_token, s.length = t, s.length + 1
-            if s.finished(eos):
-                done.append(s)
-        self._emit(done)
-        for s in done:
-            self._remove(s)
-        return [s.request_id for s in done]
+        res = self.rt.advance_greedy(drules, picks.cpu().numpy())
+        return self._emit(res)
 
-    def _beam_candidates(self, seqs, scores, keep):
+    def _beam_candidates(self, rows: StepRows, meta: torch.Tensor, scores: torch.Tensor, keep: int) -> np.ndarray:
         """Each request's best ``keep`` (row, token, cum_logprob) continuations, selected on the
         GPU: every row's top-k plus its cumulative log-prob, scattered into a per-request grid in
         row order, one stable descending sort per request - the order the reference's stable
-        Python sort of the concatenated rows gives (vflorence/engine/model_runner.py:383-410)."""
-        rows, vocab = scores.shape
+        Python sort of the concatenated rows gives (vflorence/engine/model_runner.py:383-410).
+        Returns int32 [3, requests, n] (row, token, float32 bits of the score); row -1 = none."""
+        n, vocab = scores.shape
         k = min(keep, vocab)
-        req_of, slot_of, counts, order = [], [], [], {}
-        for s in seqs:
-            r = order.get(s.request_id)
-            if r is None:
-                r = order[s.request_id] = len(counts)
-                counts.append(0)
-            req_of.append(r)
-            slot_of.append(counts[r])
-            counts[r] += 1
-        R, width = len(counts), max(counts)
-        host = torch.tensor([req_of, slot_of], dtype=torch.long).pin_memory()
-        cum = torch.tensor([s.cum_logprob for s in seqs], dtype=torch.float32).pin_memory()
-        idx = host.to(self.device, non_blocking=True)
+        R, width = rows.num_groups, rows.max_rank
+        grp, rank = meta[2].long(), meta[3].long()
         top_s, top_i = torch.topk(scores, k, dim=-1)
-        top_s += cum.to(self.device, non_blocking=True).unsqueeze(-1)
+        top_s += meta[4].view(torch.float32).unsqueeze(-1)
         grid_s = torch.full((R, width, k), float("-inf"), device=self.device)
-        grid_t = torch.zeros((R, width, k), dtype=torch.long, device=self.device)
-        grid_r = torch.full((R, width, k), -1, dtype=torch.long, device=self.device)
-        grid_s[idx[0], idx[1]] = top_s
-        grid_t[idx[0], idx[1]] = top_i
-        grid_r[idx[0], idx[1]] = torch.arange(rows, device=self.device).unsqueeze(-1).expand(rows, k)
+        grid_t = torch.zeros((R, width, k), dtype=torch.int32, device=self.device)
+        grid_r = torch.full((R, width, k), -1, dtype=torch.int32, device=self.device)
+        grid_s[grp, rank] = top_s
+        grid_t[grp, rank] = top_i.to(torch.int32)
+        grid_r[grp, rank] = torch.arange(n, device=self.device, dtype=torch.int32).unsqueeze(-1).expand(n, k)
         srt, pos = torch.sort(grid_s.view(R, width * k), dim=1, descending=True, stable=True)
-        n = min(keep, width * k)
-        pos = pos[:, :n]
-        picked = torch.stack([grid_r.view(R, -1).gather(1, pos).double(), grid_t.view(R, -1).gather(1, pos).double(),
-                              srt[:, :n].double()]).tolist()
-        rids = list(order)
-        cands = {}
-        for r in range(R):
-            cands[rids[r]] = [(int(row), int(tok), sc) for row, tok, sc in zip(*(picked[c][r] for c in range(3)))
-                              if row >= 0]
-        return cands
+        m = min(keep, width * k)
+        pos = pos[:, :m]
+        picked = torch.stack([grid_r.view(R, -1).gather(1, pos), grid_t.view(R, -1).gather(1, pos),
+                              srt[:, :m].contiguous().view(torch.int32)])
+        return picked.cpu().numpy()
 
-    def _child(self, parent: _Seq, token: int, cum_logprob: float) -> _Seq:
-        return _Seq(parent.request_id, parent.encoder_ids, parent.params, self.free_slots.pop(), token,
-                    parent.length + 1, parent.pixel_values, [], parent.num_cached_tokens, cum_logprob,
-                    parent.prompt_len)
-
-    def _finish_beam(self, seqs, logits) -> list[int]:
-        params = seqs[0].params
-        rules, slots, lengths, hist = self._rows_state(seqs)
+    def _finish_beam(self, params, rows: StepRows, meta: torch.Tensor, logits) -> list[int]:
+        rules, drules = self._rules_for(params)
+        lengths = meta[1].long()
+        hist = self.tokens[meta[0].long()] if rules.needs_history else None
         scores = rules(torch.log_softmax(logits.float(), dim=-1), hist, lengths)
-        cands = self._beam_candidates(seqs, scores, params.beams_to_keep())
-        eos = set(params.eos_ids())
-        nb = params.num_beams
-        born = []   # (parent, child): every child whose tokens must be written this step
-        done_rids, emitted, released = [], [], []
-        for rid, cand in cands.items():
-            finished = self.finished_beams.setdefault(rid, [])
-            running = []
-            for rank, (row, token, cum) in enumerate(cand):
-                if rank >= nb and len(running) >= nb:
-                    break
-                parent = seqs[row]
-                is_done = token in eos or parent.num_generated + 1 >= params.max_tokens
-                if is_done and rank >= nb:
-                    continue
-                if not is_done and len(running) >= nb:
-                    continue
-                child = self._child(parent, token, cum)
-                born.append((parent, child))
-                (finished if is_done else running).append(child if is_done else (parent, child))
-            finished.sort(key=lambda c: c.score(), reverse=True)
-            for dropped in finished[nb:]:
-                released.append(dropped)
-            del finished[nb:]
-            best_running = max((c.score() for _, c in running), default=float("-inf"))
-            stop = len(finished) >= nb and (params.early_stopping or finished[-1].score() >= best_running)
-            if not running or stop:
-                self.finished_beams.pop(rid, None)
-                emitted.append(finished[0])
-                released.extend(finished)
-                released.extend(c for _, c in running)
-                done_rids.append(rid)
-            else:
-                for parent, child in running:
-                    self.blocks.fork(parent, child)
-                    self.running.append(child)
-        if born:  # children's token rows: the parent's row plus the new token
-            meta = torch.tensor([[p.slot for p, _ in born], [c.slot for _, c in born],
-                                 [p.length for p, _ in born], [c.last_token for _, c in born]],
-                                dtype=torch.long).pin_memory().to(self.device, non_blocking=True)
-            self.tokens[meta[1]] = self.tokens[meta[0]]
-            self.tokens[meta[1], meta[2]] = meta[3].to(torch.int32)
-        self._emit(emitted)
-        for s in seqs:
-            self._remove(s)
-        for c in released:  # finished hypotheses hold a token row but no blocks
-            self.free_slots.append(c.slot)
-        return done_rids
+        cand = self._beam_candidates(rows, meta, scores, params.beams_to_keep())
+        res = self.rt.advance_beam(drules, cand[0], cand[1], cand[2].view(np.float32))
+        nb = len(res.born_child)
+        if nb:  # children's token rows: the parent's row plus the new token
+            if self._born_host is None or self._born_host.numel() < 4 * nb:
+                self._born_host = torch.zeros(max(4 * nb, 4096), dtype=torch.int32).pin_memory()
+                self._born_dev = torch.zeros_like(self._born_host, device=self.device)
+            host = self._born_host.numpy()[: 4 * nb].reshape(4, nb)
+            host[0], host[1], host[2], host[3] = res.born_parent, res.born_child, res.born_pos, res.born_token
+            dev = self._born_dev[: 4 * nb]
+            dev.copy_(self._born_host[: 4 * nb], non_blocking=True)
+            b = dev.view(4, nb).long()
+            self.tokens[b[1]] = self.tokens[b[0]]
+            self.tokens[b[1], b[2]] = b[3].to(torch.int32)
+        return self._emit(res)

@@ -94,30 +94,29 @@ class _StepGraph:
         paged_ops.prepare_decode(self.tables, self.pos, self.e.block_size, self.slots, self.ctx_lens, self.qsl)
         return self.e.model.decode(self.ids.long(), self.pos.long())
 
-    def run(self, seqs) -> torch.Tensor:
-        b, B, M, Mc = len(seqs), self.rows, self.width, self.cwidth
-        self.copy_done.synchronize()  # the previous upload has left the pinned buffers
+    def host_views(self):
+        """Pinned upload views (tables [B, M], positions [B], token ids [B]) for the runtime to
+        pack the step's rows into; waits until the previous upload has left them."""
+        self.copy_done.synchronize()
+        B, M = self.rows, self.width
         hv = self.host_in.numpy()
-        tables = hv[: B * M].reshape(B, M)
-        tables[:b] = 0
-        for i, s in enumerate(seqs):
-            tables[i, : len(s.block_table)] = s.block_table
-        pos = hv[B * M: B * M + B]
-        pos[:b] = [s.num_cached_tokens for s in seqs]
-        pos[b:] = -1
-        hv[B * M + B: B * M + B + b] = [s.last_token for s in seqs]
+        return hv[: B * M].reshape(B, M), hv[B * M: B * M + B], hv[B * M + B:]
+
+    def launch(self, rows) -> torch.Tensor:
+        """Replay for the packed rows; rows past ``rows.n`` are padding. Logits [n, vocab]."""
+        b, B, M = rows.n, self.rows, self.width
+        self.host_in.numpy()[B * M + b: B * M + B] = -1
         self.dev_in.copy_(self.host_in, non_blocking=True)
-        key = tuple(s.request_id for s in seqs)
-        if key != self.cross_key:
-            self._stage_cross(seqs)
-            self.cross_key = key
+        if self.cross_key is None or not np.array_equal(self.cross_key, rows.request_ids):
+            self._stage_cross(rows.request_ids.tolist())
+            self.cross_key = rows.request_ids.copy()
         self.copy_done.record()
         self.graph.replay()
         return self.logits[:b]
 
-    def _stage_cross(self, seqs):
+    def _stage_cross(self, request_ids):
         B, Mc = self.rows, self.cwidth
-        pages, lens = zip(*(self.e.kv.cross.pages[s.request_id] for s in seqs))
+        pages, lens = zip(*(self.e.kv.cross.pages[r] for r in request_ids))
         firsts, offsets = group_rows(list(pages), list(lens))
         hc = self.host_cross.numpy()
         ctab = hc[: B * Mc].reshape(B, Mc)
@@ -125,7 +124,7 @@ class _StepGraph:
         clens = hc[B * Mc: B * Mc + B]
         clens[:] = 0
         cqsl = hc[B * Mc + B:]
-        cqsl[:] = len(seqs)
+        cqsl[:] = len(request_ids)
         for g, i in enumerate(firsts):
             ctab[g, : pages[i].numel()] = pages[i].numpy()
             clens[g] = lens[i]
@@ -155,13 +154,14 @@ class GraphedDecoder:
             if (rows, beams) not in self.graphs:
                 self.graphs[(rows, beams)] = _StepGraph(self.e, rows, beams, None)
 
-    def run(self, seqs) -> torch.Tensor | None:
-        """Logits [len(seqs), vocab], or None when the batch is larger than every bucket."""
-        rows = self.bucket(len(seqs))
-        if rows is None:
+    def graph_for(self, rows: int, beams: int) -> _StepGraph | None:
+        """The captured step for ``rows`` running rows, or None when the batch is larger than
+        every bucket (the step then runs eagerly)."""
+        b = self.bucket(rows)
+        if b is None:
             return None
-        key = (rows, seqs[0].params.num_beams)
+        key = (b, beams)
         g = self.graphs.get(key)
         if g is None:
-            g = self.graphs[key] = _StepGraph(self.e, rows, key[1], None)  # own memory pool
-        return g.run(seqs)
+            g = self.graphs[key] = _StepGraph(self.e, b, beams, None)  # own memory pool
+        return g

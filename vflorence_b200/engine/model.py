@@ -66,6 +66,14 @@ class PagedSeq2Seq:
         self.lm_head = hf_model.lm_head
         self.final_logits_bias = getattr(hf_model, "final_logits_bias", None)
         self.vocab_size = self.lm_head.out_features
+        # the vocabulary projection padded to a multiple of 64 rows: logit rows of an odd vocab
+        # size (51289, 50265) are not 16-byte aligned, which keeps the GEMM off its fast kernels
+        w, b = self.lm_head.weight, self.lm_head.bias
+        pad = -self.vocab_size % 64
+        if pad:
+            w = torch.cat([w, w.new_zeros(pad, w.shape[1])])
+            b = None if b is None else torch.cat([b, b.new_zeros(pad)])
+        self.w_head, self.b_head = w, b
         self.dtype = self.pos_weight.dtype
         self.device = self.pos_weight.device
         self.image_token_id = getattr(cfg, "image_token_id", None)
@@ -108,7 +116,7 @@ class PagedSeq2Seq:
             c = decoder_cross_attention(L.cross_q(h).reshape(shape), i, self.scale)
             h = L.ln_cross(h + L.cross_out(c.reshape(B, self.d_model)))
             h = L.ln_final(h + L.fc2(self.act(L.fc1(h))))
-        logits = self.lm_head(h)
+        logits = F.linear(h, self.w_head, self.b_head)[:, : self.vocab_size]
         if self.final_logits_bias is not None:
             logits = logits + self.final_logits_bias
         return logits

@@ -101,6 +101,7 @@ class PagedKVCache:
         self.cross = CrossPageAllocator(num_cross_blocks)
         self._cross_key = None
         self._cross_staged = None
+        self._pairs_host = self._pairs_dev = None
 
     # ----------------------------------------------------------------------------- binding
     def bind(self, decoder_layers) -> None:
@@ -116,8 +117,23 @@ class PagedKVCache:
 
     # ------------------------------------------------------------------------ copy-on-write
     def copy_blocks(self, copies) -> None:
-        """Copy whole self-attention blocks src -> dst in every layer (before the step's append)."""
-        if copies:
+        """Copy whole self-attention blocks src -> dst in every layer (before the step's append).
+        ``copies``: (src, dst) pairs, a list or an integer [P, 2] array (uploaded through one
+        reused pinned buffer)."""
+        if isinstance(copies, np.ndarray):
+            pairs = np.asarray(copies, dtype=np.int64).reshape(-1, 2)
+            P = len(pairs)
+            if P == 0:
+                return
+            paged_ops.check_copy_pairs_array(pairs, self.num_blocks)
+            if self._pairs_host is None or self._pairs_host.numel() < 2 * P:
+                self._pairs_host = torch.zeros(max(2 * P, 1024), dtype=torch.int64).pin_memory()
+                self._pairs_dev = torch.zeros_like(self._pairs_host, device=self.device)
+            self._pairs_host.numpy()[: 2 * P] = pairs.reshape(-1)
+            dev = self._pairs_dev[: 2 * P]
+            dev.copy_(self._pairs_host[: 2 * P], non_blocking=True)
+            paged_ops.copy_blocks(self.k_caches, self.v_caches, dev.view(P, 2))
+        elif copies:
             paged_ops.copy_blocks(self.k_caches, self.v_caches, copies)
 
     # ------------------------------------------------------------------------ encoder pages
@@ -147,9 +163,14 @@ class PagedKVCache:
         mapping, context lengths and query_start_loc on the device."""
         b = len(positions)
         width = max(len(t) for t in block_tables)
-        host = pack_decode_step(block_tables, positions)
-        pos = host[b * width:]
-        dev = torch.from_numpy(host).pin_memory().to(self.device, non_blocking=True)
+        host = torch.from_numpy(pack_decode_step(block_tables, positions)).pin_memory()
+        return self.prepare_decode_host(host, b, width)
+
+    def prepare_decode_host(self, host: torch.Tensor, b: int, width: int) -> DecodeStep:
+        """``prepare_decode`` from a pinned int32 host buffer that already holds the block
+        tables [b, width] followed by the positions [b]."""
+        pos = host.numpy()[b * width: b * width + b]
+        dev = host[: b * width + b].to(self.device, non_blocking=True)
         tables_dev = dev[: b * width].view(b, width)
         pos_dev = dev[b * width:]
         slot_mapping = torch.empty(b, dtype=torch.int64, device=self.device)

@@ -27,6 +27,7 @@ from __future__ import annotations
 
 import ctypes
 
+import numpy as np
 import torch
 
 from . import _native as N
@@ -206,6 +207,21 @@ def check_copy_pairs(pairs, num_blocks: int) -> list[tuple[int, int]]:
     if srcs.intersection(dsts):
         raise ValueError("vflorence_b200: copy_blocks sources and destinations must be disjoint")
     return pairs
+
+
+def check_copy_pairs_array(pairs, num_blocks: int) -> None:
+    """``check_copy_pairs`` for an integer [P, 2] numpy array (vectorised)."""
+    if pairs.ndim != 2 or pairs.shape[1] != 2:
+        raise ValueError("vflorence_b200: copy pairs must be a [P, 2] array")
+    if len(pairs) == 0:
+        return
+    if pairs.min() < 0 or pairs.max() >= num_blocks:
+        raise ValueError(f"vflorence_b200: a copy pair lies outside [0, {num_blocks})")
+    src, dst = pairs[:, 0], pairs[:, 1]
+    if np.unique(dst).size != dst.size:
+        raise ValueError("vflorence_b200: copy_blocks destinations must be unique")
+    if np.intersect1d(src, dst).size:
+        raise ValueError("vflorence_b200: copy_blocks sources and destinations must be disjoint")
 
 
 def copy_blocks(k_caches, v_caches, block_pairs) -> None:
