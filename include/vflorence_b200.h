@@ -187,6 +187,31 @@ int vfl_paged_slots(const int32_t* pages, int64_t pages_stride, int32_t pages_co
                     int num_reqs, int seq_len, int block_size, int64_t* slot_mapping,
                     void* stream);
 
+/* ---- candidate selection of a decode step ----------------------------------------------------
+ * replaces, on the device, the float copy, log_softmax, top-k and cumulative-log-prob add of
+ *   ModelRunner._sample / _beam_search (vflorence/engine/model_runner.py:370-371, :394-399)
+ *   and the greedy argmax (:379-380). Row r of `scores` (float32 or bfloat16, `vocab` entries at
+ *   `row_stride` elements apart) gives its best k entries:
+ *     value = log_softmax ? (x - max_r) - log(sum_v exp(x_v - max_r)) : x, plus row_offset[r]
+ *             when row_offset is not NULL (float32, device)
+ *   ordered by value descending, equal values by lower index (the argmax rule; the reference's
+ *   CPU top-k leaves that order unspecified). values: float32 [rows, k]; indices: int32
+ *   [rows, k]. k in [1, 64] and <= vocab. With log_softmax the entries are chosen on x, which
+ *   log_softmax maps monotonically. */
+int vfl_row_topk(const void* scores, int32_t dtype, int64_t rows, int64_t vocab, int64_t row_stride,
+                 int32_t log_softmax, const float* row_offset, int32_t k, float* values,
+                 int32_t* indices, void* stream);
+
+/* replaces the per-request merge of ModelRunner._beam_search (model_runner.py:401-410): the
+ *   rows of request group g (groups[r] == g, at most 64 rows, placed by ranks[r]) pool their
+ *   k candidates from vfl_row_topk, ordered by value descending, equal values in row-rank then
+ *   list order (a stable sort of the rows' lists in row order); the best `keep` are written to
+ *   out, int32 [3, num_groups, keep]: row, token index, float32 bits of the value; row -1 pads
+ *   a group with fewer than `keep` candidates. All pointers are device pointers. */
+int vfl_beam_merge(const float* values, const int32_t* indices, int64_t rows, int32_t k,
+                   const int32_t* groups, const int32_t* ranks, int32_t num_groups, int32_t keep,
+                   int32_t* out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -49,6 +49,8 @@ EXPORTS = (
     "vfl_copy_blocks",
     "vfl_prepare_decode",
     "vfl_paged_slots",
+    "vfl_row_topk",
+    "vfl_beam_merge",
     # host decode runtime (vflorence_b200_runtime.h)
     "vfl_rt_create",
     "vfl_rt_destroy",
@@ -160,6 +162,8 @@ def _declare(L):
         "vfl_copy_blocks": (i32, [vp, vp, i32, vp, i32, i64, i64, vp]),
         "vfl_prepare_decode": (i32, [vp, i64, i32, vp, i32, i32, vp, vp, vp, vp]),
         "vfl_paged_slots": (i32, [vp, i64, i32, i32, i32, i32, vp, vp]),
+        "vfl_row_topk": (i32, [vp, i32, i64, i64, i64, i32, vp, i32, vp, vp, vp]),
+        "vfl_beam_merge": (i32, [vp, vp, i64, i32, vp, vp, i32, i32, vp, vp]),
         "vfl_rt_create": (i32, [i32, i32, i32, i32, ctypes.POINTER(vp)]),
         "vfl_rt_destroy": (None, [vp]),
         "vfl_rt_reset": (i32, [vp]),

@@ -23,6 +23,7 @@ from dataclasses import dataclass
 import numpy as np
 import torch
 
+from .. import paged_ops
 from ..block_manager import BlockManager
 from ..context import set_context
 from ..kv_cache import PagedKVCache
@@ -107,6 +108,9 @@ class Engine:
             raise ValueError(f"max_tokens {params.max_tokens} exceeds max_decoder_len {self.max_decoder_len}")
         if params.num_beams > self.max_num_seqs:
             raise ValueError("num_beams exceeds max_num_seqs")
+        if params.beams_to_keep() > paged_ops.MAX_TOPK:
+            raise ValueError(f"beam search keeps {params.beams_to_keep()} candidates per row; the device "
+                             f"selection is built for at most {paged_ops.MAX_TOPK}")
         if self.waiting or self.requests:
             other = (self.waiting[0] if self.waiting else next(iter(self.requests.values()))).params
             if other != params:
@@ -270,43 +274,39 @@ class Engine:
     def _finish_greedy(self, params, rows: StepRows, meta: torch.Tensor, logits) -> list[int]:
         rules, drules = self._rules_for(params)
         slots, lengths = meta[0].long(), meta[1].long()
-        hist = self.tokens[slots] if rules.needs_history else None
-        picks = rules(logits.float(), hist, lengths).argmax(dim=-1)
-        self.tokens[slots, lengths] = picks.to(torch.int32)
+        scores = logits
+        if rules.active:
+            hist = self.tokens[slots] if rules.needs_history else None
+            scores = rules(logits.float(), hist, lengths)
+        _, picks = paged_ops.row_topk(scores, 1)  # the argmax, first index on ties
+        picks = picks.view(-1)
+        self.tokens[slots, lengths] = picks
         res = self.rt.advance_greedy(drules, picks.cpu().numpy())
         return self._emit(res)
 
-    def _beam_candidates(self, rows: StepRows, meta: torch.Tensor, scores: torch.Tensor, keep: int) -> np.ndarray:
+    def _beam_candidates(self, rows: StepRows, meta: torch.Tensor, logits: torch.Tensor, scores, keep: int) -> np.ndarray:
         """Each request's best ``keep`` (row, token, cum_logprob) continuations, selected on the
-        GPU: every row's top-k plus its cumulative log-prob, scattered into a per-request grid in
-        row order, one stable descending sort per request - the order the reference's stable
-        Python sort of the concatenated rows gives (vflorence/engine/model_runner.py:383-410).
-        Returns int32 [3, requests, n] (row, token, float32 bits of the score); row -1 = none."""
-        n, vocab = scores.shape
+        GPU: every row's top-k log-probs plus its cumulative log-prob (one fused kernel over the
+        logits, or over the rule-processed scores), then one merge per request in the order of
+        a stable descending sort of its rows' lists - the reference's stable Python sort of the
+        concatenated rows (vflorence/engine/model_runner.py:383-410).
+        Returns int32 [3, requests, keep] (row, token, float32 bits of the score); row -1 = none."""
+        vocab = logits.shape[1]
         k = min(keep, vocab)
-        R, width = rows.num_groups, rows.max_rank
-        grp, rank = meta[2].long(), meta[3].long()
-        top_s, top_i = torch.topk(scores, k, dim=-1)
-        top_s += meta[4].view(torch.float32).unsqueeze(-1)
-        grid_s = torch.full((R, width, k), float("-inf"), device=self.device)
-        grid_t = torch.zeros((R, width, k), dtype=torch.int32, device=self.device)
-        grid_r = torch.full((R, width, k), -1, dtype=torch.int32, device=self.device)
-        grid_s[grp, rank] = top_s
-        grid_t[grp, rank] = top_i.to(torch.int32)
-        grid_r[grp, rank] = torch.arange(n, device=self.device, dtype=torch.int32).unsqueeze(-1).expand(n, k)
-        srt, pos = torch.sort(grid_s.view(R, width * k), dim=1, descending=True, stable=True)
-        m = min(keep, width * k)
-        pos = pos[:, :m]
-        picked = torch.stack([grid_r.view(R, -1).gather(1, pos), grid_t.view(R, -1).gather(1, pos),
-                              srt[:, :m].contiguous().view(torch.int32)])
-        return picked.cpu().numpy()
+        cum = meta[4].view(torch.float32)
+        if scores is None:
+            values, ids = paged_ops.row_topk(logits, k, log_softmax=True, row_offset=cum)
+        else:
+            values, ids = paged_ops.row_topk(scores, k, row_offset=cum)
+        return paged_ops.beam_merge(values, ids, meta[2], meta[3], rows.num_groups, keep).cpu().numpy()
 
     def _finish_beam(self, params, rows: StepRows, meta: torch.Tensor, logits) -> list[int]:
         rules, drules = self._rules_for(params)
-        lengths = meta[1].long()
-        hist = self.tokens[meta[0].long()] if rules.needs_history else None
-        scores = rules(torch.log_softmax(logits.float(), dim=-1), hist, lengths)
-        cand = self._beam_candidates(rows, meta, scores, params.beams_to_keep())
+        scores = None
+        if rules.active:
+            hist = self.tokens[meta[0].long()] if rules.needs_history else None
+            scores = rules(torch.log_softmax(logits.float(), dim=-1), hist, meta[1].long())
+        cand = self._beam_candidates(rows, meta, logits, scores, params.beams_to_keep())
         res = self.rt.advance_beam(drules, cand[0], cand[1], cand[2].view(np.float32))
         nb = len(res.born_child)
         if nb:  # children's token rows: the parent's row plus the new token

@@ -90,6 +90,9 @@ class LogitsRules:
         self.forced_bos = keep(_as_list(params.forced_bos_token_id))
         self.forced_eos = keep(_as_list(params.forced_eos_token_id))
         self.needs_history = params.repetition_penalty != 1.0 or params.no_repeat_ngram_size > 0
+        # whether any rule can change a score (else the selection reads the raw logits)
+        self.active = bool(self.needs_history or (params.min_length > 0 and self.eos.numel()) or self.forced_bos
+                           or self.forced_eos or self.suppress.numel() or self.begin_suppress.numel())
 
     def __call__(self, scores: torch.Tensor, hist: torch.Tensor | None, lengths: torch.Tensor) -> torch.Tensor:
         """``scores`` [rows, vocab] float (modified in place). ``hist`` [rows, W] int32: row i's
@@ -97,14 +100,14 @@ class LogitsRules:
         when a rule needs the history. ``lengths`` int64 [rows] on the same device."""
         p = self.p
         dev = scores.device
-        if self.needs_history:
+        if p.repetition_penalty != 1.0:  # every token already in the row's history, once
             cols = torch.arange(hist.shape[1], device=dev)
             real = cols.unsqueeze(0) < lengths.unsqueeze(1)          # [rows, W]
-        if p.repetition_penalty != 1.0:  # every token already in the row's history
-            rows, pos = torch.where(real)
-            tokens = hist[rows, pos].long()
-            seen = scores[rows, tokens]
-            scores[rows, tokens] = torch.where(seen < 0, seen * p.repetition_penalty, seen / p.repetition_penalty)
+            # columns past a row's length repeat its first token, so they rewrite that token's
+            # (identical) penalised score and nothing else; no host synchronisation
+            tokens = torch.where(real, hist, hist[:, :1]).long()
+            seen = scores.gather(1, tokens)
+            scores.scatter_(1, tokens, torch.where(seen < 0, seen * p.repetition_penalty, seen / p.repetition_penalty))
         if p.no_repeat_ngram_size > 0:
             self._ban_repeated_ngrams(scores, hist, lengths)
         if p.min_length > 0 and self.eos.numel():
@@ -145,6 +148,6 @@ class LogitsRules:
         tail = hist.gather(1, tail_pos)                                  # last n - 1 tokens
         match = (windows[:, :, : n - 1] == tail.unsqueeze(1)).all(-1) & inside
         match &= (lengths + 1 >= n).unsqueeze(1)
-        rows, cols = match.nonzero(as_tuple=True)
-        if rows.numel():
-            scores[rows, windows[rows, cols, n - 1].long()] = NEG_INF
+        # -inf where a window matches, +inf (no change under min) elsewhere: no host sync
+        ban = torch.full(match.shape, float("inf"), device=dev).masked_fill_(match, NEG_INF)
+        scores.scatter_reduce_(1, windows[:, :, n - 1].long(), ban, reduce="amin")

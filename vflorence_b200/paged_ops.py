@@ -300,6 +300,55 @@ def paged_slots(pages: torch.Tensor, seq_len: int, block_size: int) -> torch.Ten
     return out
 
 
+# ---------------------------------------------------------------------- candidate selection
+MAX_TOPK = 64
+
+
+def row_topk(scores: torch.Tensor, k: int, log_softmax: bool = False, row_offset: torch.Tensor | None = None,
+             out: tuple[torch.Tensor, torch.Tensor] | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """Each row's best ``k`` entries of a [rows, vocab] float32/bfloat16 matrix (unit column
+    stride), as log-probs when ``log_softmax``, plus ``row_offset`` (float32 [rows]) when given:
+    (values float32 [rows, k], indices int32 [rows, k]), value descending, ties by lower index."""
+    _require_cuda("scores", scores)
+    dev = scores.device
+    if scores.dim() != 2 or scores.stride(1) != 1:
+        raise ValueError("vflorence_b200: row_topk wants a [rows, vocab] matrix with unit column stride")
+    rows, vocab = scores.shape
+    if row_offset is not None:
+        _require_cuda("row_offset", row_offset, dev)
+        if row_offset.dtype != torch.float32 or row_offset.numel() < rows or not row_offset.is_contiguous():
+            raise ValueError("vflorence_b200: row_offset must be contiguous float32 [rows]")
+    if out is None:
+        out = (torch.empty(rows, k, dtype=torch.float32, device=dev), torch.empty(rows, k, dtype=torch.int32, device=dev))
+    values, indices = out
+    st = N.lib().vfl_row_topk(scores.data_ptr(), _dtype_code(scores.dtype), rows, vocab,
+                              scores.stride(0) if rows > 1 else vocab, int(bool(log_softmax)),
+                              None if row_offset is None else row_offset.data_ptr(), int(k), values.data_ptr(),
+                              indices.data_ptr(), _stream(dev))
+    N.check(st, "row_topk")
+    return values, indices
+
+
+def beam_merge(values: torch.Tensor, indices: torch.Tensor, groups: torch.Tensor, ranks: torch.Tensor,
+               num_groups: int, keep: int) -> torch.Tensor:
+    """Per-request merge of ``row_topk`` candidates: int32 [3, num_groups, keep] (row, token,
+    float32 bits of the value; row -1 pads). ``groups``/``ranks``: int32 [rows] on the device."""
+    dev = values.device
+    for name, t in (("values", values), ("indices", indices), ("groups", groups), ("ranks", ranks)):
+        _require_cuda(name, t, dev)
+        if not t.is_contiguous():
+            raise ValueError(f"vflorence_b200: beam_merge {name} must be contiguous")
+    if (values.dtype != torch.float32 or indices.dtype != torch.int32 or groups.dtype != torch.int32
+            or ranks.dtype != torch.int32 or values.shape != indices.shape or values.dim() != 2):
+        raise ValueError("vflorence_b200: beam_merge dtypes or shapes are wrong")
+    rows, k = values.shape
+    out = torch.empty(3, num_groups, keep, dtype=torch.int32, device=dev)
+    st = N.lib().vfl_beam_merge(values.data_ptr(), indices.data_ptr(), rows, k, groups.data_ptr(), ranks.data_ptr(),
+                                int(num_groups), int(keep), out.data_ptr(), _stream(dev))
+    N.check(st, "beam_merge")
+    return out
+
+
 def read_device_errors(device: torch.device | int | None = None, clear: bool = True) -> int:
     """VFL_DEVERR_* bits the kernels raised on ``device`` since the last clear (synchronises)."""
     dev = torch.device("cuda", torch.cuda.current_device() if device is None else
