@@ -137,6 +137,27 @@ def test_attention_rejects_foreign_metadata_without_touching_the_gpu(native):
     assert b"plan" in native.vfl_last_error_message()
 
 
+@pytest.mark.parametrize("field,value", [("blocks_per_split", 65), ("blocks_per_split", 0), ("stages", 5),
+                                         ("stages", 1), ("heads_per_cta", 3), ("num_splits", 1),
+                                         ("workspace_bytes", 16), ("queries_per_cta", 2), ("merge_in_kernel", 2)])
+def test_attention_refuses_a_corrupted_plan_before_the_device(native, field, value):
+    """A plan is caller memory; every field the kernels rely on is re-checked on the host (a
+    larger split than the shared-memory table slice would overrun it)."""
+    from vflorence_b200 import _native
+
+    plan = _plan([2048, 1000, 37])
+    assert plan.num_splits > 1 and plan.blocks_per_split <= 64
+    setattr(plan, field, value)
+    fake = 1 << 20  # never dereferenced: the call must fail before touching memory
+    st = native.vfl_attention_with_kv_cache(ctypes.byref(plan), fake, 16 * 64, fake, fake, 1000, fake, 16 * 64,
+                                            fake, fake, fake, 128, 128, 1.0, fake, 1 << 30, None)
+    assert st == _native.VFL_ERR_INVALID_ARGUMENT, native.vfl_last_error_message()
+    assert b"plan" in native.vfl_last_error_message()
+    st = native.vfl_attention_with_kv_cache_no_alloc(ctypes.byref(plan), fake, 16 * 64, fake, fake, 1000, fake,
+                                                     16 * 64, fake, fake, fake, 128, 128, 1.0, None)
+    assert st == _native.VFL_ERR_INVALID_ARGUMENT, native.vfl_last_error_message()
+
+
 def test_copy_blocks_host_checks(native):
     from vflorence_b200 import paged_ops as ops
 

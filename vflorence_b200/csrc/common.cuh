@@ -20,6 +20,8 @@ int fail(int status, const char* fmt, ...);
 int cuda_status(cudaError_t e, const char* what);
 // Device address of the current device's error word (set up once per device).
 int device_error_word(unsigned int** out);
+// Re-checks every field of a caller-provided attention plan that the kernels rely on.
+int check_attention_plan(const vfl_attention_plan* plan);
 // Raises the dynamic shared-memory limit of `func` once per device.
 int ensure_smem_attribute(const void* func, int bytes, int* done_flags /* [kMaxDevices] */);
 

@@ -85,6 +85,50 @@ int pool_tensor_map(const void* base, uint64_t rows, uint32_t box_rows, CUtensor
 }
 
 }  // namespace
+
+// A plan is caller memory: every constraint the kernels rely on (shared-memory table slice,
+// stage ring, CTA shape, workspace size) is re-derived here before anything touches the device.
+int check_attention_plan(const vfl_attention_plan* plan) {
+  const int H = plan->num_heads, D = plan->head_dim, bs = plan->block_size;
+  if (plan->num_reqs < 0 || plan->total_q < 0 || plan->total_q > INT32_MAX / 2 || plan->max_q_len < 0 ||
+      plan->max_seq_len < 0 || H <= 0 || (plan->causal != 0 && plan->causal != 1))
+    return fail(VFL_ERR_INVALID_ARGUMENT, "attention: plan counts out of range");
+  if (!dtype_ok(plan->dtype) || !head_dim_supported(D) || bs < 16 || bs > 1024 || bs % 16 != 0)
+    return fail(VFL_ERR_INVALID_ARGUMENT, "attention: plan dtype / head_dim / block_size not built");
+  const int hpc = plan->heads_per_cta, qpc = plan->queries_per_cta;
+  if (!(hpc == 1 || hpc == 2 || hpc == 4) || H % hpc != 0)
+    return fail(VFL_ERR_INVALID_ARGUMENT, "attention: plan heads_per_cta %d for %d heads", hpc, H);
+  const bool tc = qpc == kTcRows;
+  if (tc ? !use_tensor_cores(plan->dtype, D) : !(qpc == 1 || qpc == 4))
+    return fail(VFL_ERR_INVALID_ARGUMENT, "attention: plan queries_per_cta %d not built for this shape", qpc);
+  if (plan->stages < 2 || plan->stages > 4)
+    return fail(VFL_ERR_INVALID_ARGUMENT, "attention: plan stages %d outside [2, 4]", plan->stages);
+  const int64_t stage_bytes = (int64_t)2 * hpc * 16 * D * (int64_t)dtype_size(plan->dtype);
+  if ((tc ? kTcHeaderBytes : kHeaderBytes) + plan->stages * stage_bytes > 227 * 1024)
+    return fail(VFL_ERR_INVALID_ARGUMENT, "attention: plan stages do not fit in shared memory");
+  if (plan->blocks_per_split < 1 || plan->blocks_per_split > kMaxBlocksPerSplit || plan->num_splits < 1 ||
+      plan->num_splits > 65535)
+    return fail(VFL_ERR_INVALID_ARGUMENT, "attention: plan split %d x %d blocks outside [1, 65535] x [1, %d]",
+                plan->num_splits, plan->blocks_per_split, kMaxBlocksPerSplit);
+  const int64_t max_blocks = ceil_div((int64_t)plan->max_seq_len, (int64_t)bs);
+  if ((int64_t)plan->num_splits * plan->blocks_per_split < max_blocks)
+    return fail(VFL_ERR_INVALID_ARGUMENT, "attention: plan splits do not cover max_seq_len %d", plan->max_seq_len);
+  if (plan->merge_in_kernel != 0 && plan->merge_in_kernel != 1)
+    return fail(VFL_ERR_INVALID_ARGUMENT, "attention: plan merge mode %d", plan->merge_in_kernel);
+  const int64_t q_chunks = ceil_div((int64_t)(plan->max_q_len < 1 ? 1 : plan->max_q_len), (int64_t)qpc);
+  if (q_chunks > 65535 || (int64_t)plan->num_reqs * (H / hpc) > INT32_MAX)
+    return fail(VFL_ERR_INVALID_ARGUMENT, "attention: plan launch grid too large");
+  if (plan->num_splits > 1) {
+    const int64_t items = (int64_t)plan->total_q * H * plan->num_splits;
+    const int64_t need = ceil_div(items * D * 4, (int64_t)256) * 256 + ceil_div(items * 2 * 4, (int64_t)256) * 256 +
+                         (plan->merge_in_kernel ? (int64_t)plan->num_reqs * (H / hpc) * q_chunks * 4 : 0);
+    if (plan->workspace_bytes < need)
+      return fail(VFL_ERR_INVALID_ARGUMENT, "attention: plan workspace_bytes %lld < the %lld its splits need",
+                  (long long)plan->workspace_bytes, (long long)need);
+  }
+  return VFL_OK;
+}
+
 }  // namespace vfl
 
 using namespace vfl;
@@ -213,6 +257,8 @@ int vfl_attention_with_kv_cache(const vfl_attention_plan* plan, const void* quer
                                 void* workspace, size_t workspace_bytes, void* stream) {
   if (plan == nullptr || plan->magic != VFL_PLAN_MAGIC)
     return fail(VFL_ERR_INVALID_ARGUMENT, "attention: plan missing or not built by vfl_plan_attention");
+  int st0 = check_attention_plan(plan);
+  if (st0) return st0;
   const int H = plan->num_heads, D = plan->head_dim;
   if (plan->num_reqs == 0 || plan->total_q == 0) return VFL_OK;
   const int es = static_cast<int>(dtype_size(plan->dtype));

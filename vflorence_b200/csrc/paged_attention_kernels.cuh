@@ -173,7 +173,11 @@ __global__ void __launch_bounds__(160, QPC == 1 ? 3 : 2) paged_attention_kernel(
   const int bs = p.block_size;
   const int bps = p.blocks_per_split;
 
-  if (load_volatile(p.err) & VFL_DEVERR_TIMEOUT) return;  // an earlier CTA gave up waiting
+  if (load_volatile(p.err) & VFL_DEVERR_TIMEOUT) return;
+  if (bps < 1 || bps > kMaxBlocksPerSplit || p.stages < 2 || p.stages > kMaxStages) {  // the host checks the plan too
+    if (threadIdx.x == 0) report(p.err, VFL_DEVERR_CONTEXT);
+    return;
+  }  // an earlier CTA gave up waiting
 
   // ---- this CTA's query rows and visible lengths (uniform across the CTA)
   const int q_begin = __ldg(p.qsl + r);

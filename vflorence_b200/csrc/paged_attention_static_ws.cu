@@ -69,6 +69,8 @@ extern "C" int vfl_attention_with_kv_cache_no_alloc(
   if (plan == nullptr || plan->magic != VFL_PLAN_MAGIC)
     return vfl::fail(VFL_ERR_INVALID_ARGUMENT,
                      "attention (no alloc): plan missing or not built by vfl_plan_attention");
+  int st0 = vfl::check_attention_plan(plan);
+  if (st0) return st0;
   if (plan->workspace_bytes > (int64_t)VFL_STATIC_WORKSPACE_BYTES)
     return vfl::fail(VFL_ERR_WORKSPACE,
                      "attention (no alloc): this plan needs %lld bytes of split-K scratch but the "

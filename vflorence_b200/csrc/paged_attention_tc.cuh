@@ -87,6 +87,10 @@ __global__ void __launch_bounds__(160, 3) paged_attention_tc_kernel(const AttnPa
   const int bps = p.blocks_per_split;
 
   if (load_volatile(p.err) & VFL_DEVERR_TIMEOUT) return;
+  if (bps < 1 || bps > kMaxBlocksPerSplit || p.stages < 2 || p.stages > kMaxStages) {  // the host checks the plan too
+    if (threadIdx.x == 0) report(p.err, VFL_DEVERR_CONTEXT);
+    return;
+  }
 
   const int q_begin = __ldg(p.qsl + r);
   const int q_end = __ldg(p.qsl + r + 1);
