@@ -66,8 +66,8 @@ def test_plan_large_batch_splits_long_requests(native):
     lens = torch.randint(1, 4097, (1024,), generator=g).tolist()
     p = _plan(lens)
     assert (p.heads_per_cta, p.queries_per_cta, p.stages) == (4, 8, 4)   # bf16 x 64: tensor cores
-    assert p.blocks_per_split * 16 == 256          # items capped at 256 tokens
-    assert p.num_splits == -(-max(lens) // 256)
+    assert p.blocks_per_split == 64                # only the table slice (64 blocks) splits them
+    assert p.num_splits == -(-max(lens) // 1024)
     assert p.workspace_bytes >= 1024 * 16 * p.num_splits * (64 + 2) * 4
     assert p.total_q == 1024 and p.max_seq_len == max(lens)
     assert p.merge_in_kernel == 0          # bandwidth-bound: separate combine launch
@@ -81,6 +81,22 @@ def test_plan_merge_mode_follows_the_work(native):
     assert big.num_splits > 1 and big.merge_in_kernel == 0
     # the in-kernel merge needs arrival counters, one per (request, head group, query chunk)
     assert small.workspace_bytes >= 8 * (16 // small.heads_per_cta) * 4
+
+
+def test_plan_uniform_batches_are_not_split(native):
+    # decode-step shapes (half a wave or more of near-uniform items): no split, and short items
+    # run two-stage rings when they fill a wave
+    p = _plan([592] * 85, qsl=[min(3 * r, 255) for r in range(86)])
+    assert p.num_splits == 1 and p.workspace_bytes == 0
+    q = _plan([100 + i % 60 for i in range(255)])
+    assert q.num_splits == 1 and q.stages == 2
+    # few near-uniform items: balanced over about half a wave, items of at least 128 tokens
+    few = _plan([2048] * 8)
+    assert 4 <= few.num_splits <= 16 and few.blocks_per_split >= 8
+    # skewed lengths: finer items than a uniform batch of the same size
+    g = torch.Generator().manual_seed(2)
+    skew = _plan(torch.randint(1, 4097, (64,), generator=g).tolist())
+    assert skew.num_splits >= 6
 
 
 def test_plan_single_long_request_fills_the_gpu(native):

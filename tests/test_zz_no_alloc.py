@@ -77,8 +77,8 @@ def test_no_alloc_rejects_plans_beyond_its_scratch(native):
     from vflorence_b200 import _native
     from vflorence_b200 import paged_ops as ops
 
-    lens = torch.full((1024,), 4096, dtype=torch.int32)
-    meta = ops.get_scheduler_metadata(1024, H, H, D, lens, torch.bfloat16, None, False, "sm100", BS)
+    lens = torch.full((4096,), 4096, dtype=torch.int32)
+    meta = ops.get_scheduler_metadata(4096, H, H, D, lens, torch.bfloat16, None, False, "sm100", BS)
     plan = ops.plan_of(meta)
     assert plan.workspace_bytes > _native.STATIC_WORKSPACE_BYTES
     st = native.vfl_attention_with_kv_cache_no_alloc(ctypes.byref(plan), None, 0, None, None, 0, None, 0,
