@@ -200,7 +200,12 @@ int vfl_paged_slots(const int32_t* pages, int64_t pages_stride, int32_t pages_co
  *   log_softmax maps monotonically. */
 int vfl_row_topk(const void* scores, int32_t dtype, int64_t rows, int64_t vocab, int64_t row_stride,
                  int32_t log_softmax, const float* row_offset, int32_t k, float* values,
-                 int32_t* indices, void* stream);
+                 int32_t* indices, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Scratch vfl_row_topk needs for `rows` x `vocab` at this k: 0, or the bytes of the per-chunk
+ * partial results when rows are split across several CTAs (16-byte aligned, no initial
+ * contents needed). VFL_ERR_WORKSPACE when a call gets less. */
+size_t vfl_row_topk_workspace_size(int64_t rows, int64_t vocab, int32_t k);
 
 /* replaces the per-request merge of ModelRunner._beam_search (model_runner.py:401-410): the
  *   rows of request group g (groups[r] == g, at most 64 rows, placed by ranks[r]) pool their

@@ -18,7 +18,7 @@ def _declared():
     names = []
     for header in ("vflorence_b200.h", "vflorence_b200_runtime.h"):
         text = open(os.path.join(REPO, "include", header)).read()
-        names += re.findall(r"^(?:int|void|const char\*)\s+(vfl_\w+)\(", text, flags=re.M)
+        names += re.findall(r"^(?:int|void|size_t|const char\*)\s+(vfl_\w+)\(", text, flags=re.M)
     return names
 
 

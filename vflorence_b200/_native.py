@@ -50,6 +50,7 @@ EXPORTS = (
     "vfl_prepare_decode",
     "vfl_paged_slots",
     "vfl_row_topk",
+    "vfl_row_topk_workspace_size",
     "vfl_beam_merge",
     # host decode runtime (vflorence_b200_runtime.h)
     "vfl_rt_create",
@@ -162,7 +163,8 @@ def _declare(L):
         "vfl_copy_blocks": (i32, [vp, vp, i32, vp, i32, i64, i64, vp]),
         "vfl_prepare_decode": (i32, [vp, i64, i32, vp, i32, i32, vp, vp, vp, vp]),
         "vfl_paged_slots": (i32, [vp, i64, i32, i32, i32, i32, vp, vp]),
-        "vfl_row_topk": (i32, [vp, i32, i64, i64, i64, i32, vp, i32, vp, vp, vp]),
+        "vfl_row_topk": (i32, [vp, i32, i64, i64, i64, i32, vp, i32, vp, vp, vp, sz, vp]),
+        "vfl_row_topk_workspace_size": (sz, [i64, i64, i32]),
         "vfl_beam_merge": (i32, [vp, vp, i64, i32, vp, vp, i32, i32, vp, vp]),
         "vfl_rt_create": (i32, [i32, i32, i32, i32, ctypes.POINTER(vp)]),
         "vfl_rt_destroy": (None, [vp]),

@@ -16,7 +16,7 @@ namespace {
 constexpr int kMergeWaves = 4;       // split items up to this many waves merge in the kernel
 constexpr int kMinSplitTokens = 128;  // below this a split costs more (prologue, merge) than it saves
 constexpr int kMinSplitTokensTiny = 64;  // ... except for a handful of items (a few long requests)
-constexpr int kShortItemTokens = 640;    // items this short run 2-stage rings when they fill a wave
+constexpr int kShortItemTokens = 256;    // items this short run 2-stage rings when they fill a wave
 constexpr int kSmemPerSM = 227 * 1024;
 
 int plan_fail(vfl_attention_plan* plan, int status) {
@@ -208,6 +208,11 @@ int vfl_plan_attention(int num_reqs, int num_heads, int num_kv_heads, int head_d
   int64_t bps;
   if (!skewed && 2 * base_items >= slots) {
     bps = max_blocks;  // no split beyond what the table slice forces
+    // ... unless long items leave a second wave less than half full: its few CTAs cannot pull
+    // the full bandwidth (128 x 1024-token items, 1.15 waves: 119 us unsplit, 100 us in halves;
+    // at 1.8 waves halving was 8 % slower)
+    if (base_items > slots && 2 * base_items < 3 * slots && max_blocks * block_size >= 512)
+      bps = ceil_div(max_blocks, (int64_t)2);
   } else {
     const int64_t target = skewed ? 2 * slots : slots / 2;
     bps = ceil_div(ceil_div(work_tiles, target), (int64_t)tpb);
@@ -223,7 +228,8 @@ int vfl_plan_attention(int num_reqs, int num_heads, int num_kv_heads, int head_d
     splits = ceil_div(max_blocks, bps);
   }
   // a full wave of short items: two stages per CTA, so twice as many CTAs hide each other's
-  // item prologues (measured 5-11 % faster than four stages for items of 128-592 tokens)
+  // item prologues (measured 3-11 % faster than four stages for items of up to 256 tokens;
+  // mixed, within 10 % either way, at 577-592 tokens)
   if (base_items >= slots && bps * block_size <= kShortItemTokens && stages > 2) stages = 2;
   splits = splits < 1 ? 1 : splits;
   const int64_t q_chunks = ceil_div(max_q < 1 ? 1 : max_q, (int64_t)qpc);

@@ -1,12 +1,15 @@
 // Device-side candidate selection of a decode step (sm_100a).
 //
-//   row_topk_kernel    one CTA per row of a [rows, vocab] score matrix: a single pass over the
-//                      row keeps every thread's best K keys in registers (and, for beam search,
-//                      the row's running max and sum of exponentials), then warp and block
-//                      merges give the row's top-k, turned into log-probs and shifted by the
-//                      row's cumulative log-prob. Replaces logits.float(), log_softmax, topk and
-//                      the cum add of the reference's _sample / _beam_search
-//                      (vflorence/engine/model_runner.py:370-399) and the greedy argmax (:379).
+//   row_topk_warp_kernel  (k <= 32) rows x chunks CTAs: one pass over a chunk of a row of a
+//                      [rows, vocab] score matrix keeps each warp's best k keys in one list
+//                      shared by its lanes (and, for beam search, running maxima and sums of
+//                      exponentials); the block's warps merge, and with several chunks per row
+//                      row_topk_merge_kernel merges the chunks. The top-k become log-probs
+//                      shifted by the row's cumulative log-prob. Replaces logits.float(),
+//                      log_softmax, topk and the cum add of the reference's _sample /
+//                      _beam_search (vflorence/engine/model_runner.py:370-399) and the greedy
+//                      argmax (:379).
+//   row_topk_kernel    (33 <= k <= 64) one CTA per row, per-thread register lists.
 //   beam_merge_kernel  one warp per request: the request's rows' candidates ordered as a
 //                      stable descending sort of the rows' lists in row order
 //                      (model_runner.py:401-410), the best `keep` written out.
@@ -159,12 +162,26 @@ __global__ void __launch_bounds__(kTopkThreads) row_topk_kernel(const T* __restr
   for (int64_t i = tid; i < head; i += kTopkThreads) visit<T, K, kLogSoftmax>(list, st, to_float(x[i]), (uint32_t)i);
   const int64_t nvec = (vocab - head) / V::N;
   const T* xv = x + head;
-  for (int64_t v = tid; v < nvec; v += kTopkThreads) {
-    float e[V::N];
-    V::load(xv + v * V::N, e);
+  // U independent 16-byte loads in flight per thread before any of them is consumed (one CTA
+  // per row leaves few warps per SM, so the row streams only if each thread keeps several
+  // loads outstanding); fewer for the wide-K lists, whose registers are already committed
+  constexpr int U = K <= 16 ? 32 / V::N : (K <= 32 ? (V::N >= 8 ? 1 : 8 / V::N) : 1);
+  for (int64_t v0 = tid; v0 < nvec; v0 += (int64_t)kTopkThreads * U) {
+    float e[U][V::N];
 #pragma unroll
-    for (int q = 0; q < V::N; ++q)
-      visit<T, K, kLogSoftmax>(list, st, e[q], (uint32_t)(head + v * V::N + q));
+    for (int u = 0; u < U; ++u) {
+      const int64_t v = v0 + (int64_t)u * kTopkThreads;
+      if (v < nvec) V::load(xv + v * V::N, e[u]);
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t v = v0 + (int64_t)u * kTopkThreads;
+      if (v < nvec) {
+#pragma unroll
+        for (int q = 0; q < V::N; ++q)
+          visit<T, K, kLogSoftmax>(list, st, e[u][q], (uint32_t)(head + v * V::N + q));
+      }
+    }
   }
   for (int64_t i = head + nvec * V::N + tid; i < vocab; i += kTopkThreads)
     visit<T, K, kLogSoftmax>(list, st, to_float(x[i]), (uint32_t)i);
@@ -203,6 +220,280 @@ __global__ void __launch_bounds__(kTopkThreads) row_topk_kernel(const T* __restr
       indices[r * k + j] = (int32_t)key_index(row_best[j]);
     }
   }
+}
+
+// k <= 32: each warp keeps ONE shared list, lane j holding the warp's j-th best key, so an
+// element costs a float compare with the warp's k-th value and a ballot; the rare winners are
+// inserted one at a time by the whole warp. Every lane walks its range in the same order
+// (warp-uniform loops, out-of-range lanes offer nothing). For beam search each lane also keeps
+// a running max and sum of exp(x - max), updated once per batch of its elements.
+struct WarpList {
+  uint64_t mine = 0;  // lane j < k: the warp's j-th best key (0 = empty)
+  uint64_t thr = 0;   // the warp's k-th best key (0 while the list is not full)
+  float thr_val = 0.0f;
+
+  __device__ __forceinline__ static uint64_t shfl_u64(uint64_t v, int src) {
+    return __shfl_sync(0xffffffffu, v, src);
+  }
+
+  // `pass`: this lane's element may beat the k-th key (a cheap superset test); `key` is only
+  // read for such lanes
+  __device__ __forceinline__ void offer_if(bool pass, uint64_t key, int lane, int k) {
+    unsigned ball = __ballot_sync(0xffffffffu, pass && key > thr);
+    while (ball) {
+      const int src = __ffs(ball) - 1;
+      ball &= ball - 1;
+      const uint64_t cand = shfl_u64(key, src);
+      if (cand > thr) {  // uniform: cand and thr are the same in every lane
+        const int pos = __popc(__ballot_sync(0xffffffffu, lane < k && mine > cand));
+        const uint64_t up = __shfl_up_sync(0xffffffffu, mine, 1);
+        if (lane < k) mine = lane > pos ? up : (lane == pos ? cand : mine);
+        thr = shfl_u64(mine, k - 1);
+        thr_val = key_value(thr);
+      }
+    }
+  }
+
+  __device__ __forceinline__ bool may_win(float x) const { return thr == 0 || !(x < thr_val); }
+
+  __device__ __forceinline__ void offer_value(bool ok, float x, uint32_t idx, int lane, int k) {
+    const bool pass = ok && may_win(x);
+    offer_if(pass, pass ? make_key(x, idx) : 0ull, lane, k);
+  }
+};
+
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr int kMaxChunks = 16;
+constexpr int64_t kMinChunkElems = 4096;
+
+// What one CTA of a split row leaves for the merge: its best keys and its (max, sum of exp).
+struct TopkPartial {
+  uint64_t keys[32];
+  float m, s;
+};
+
+// Chunks per row: as many as one wave of CTAs holds (3 per SM), chunks of at least
+// kMinChunkElems elements; a second partial wave costs more than the extra parallelism gives.
+int topk_chunks(int64_t rows, int64_t vocab, int k) {
+  if (k > 32 || rows <= 0) return 1;
+  int64_t c = (int64_t)kNumSMs * 3 / rows;
+  const int64_t by_len = vocab / kMinChunkElems;
+  c = c < by_len ? c : by_len;
+  return (int)(c < 1 ? 1 : (c > kMaxChunks ? kMaxChunks : c));
+}
+
+// adds a lane's batch (its valid values, batch maximum `bm`) to its (max, sum of exp) with one
+// rescale per batch
+__device__ __forceinline__ void stats_rescale(RowStats& st, float bm) {
+  if (bm > st.m) {
+    st.s *= exp2_approx((st.m - bm) * kLog2e);
+    st.m = bm;
+  }
+}
+
+__device__ __forceinline__ void write_row(float* values, int32_t* indices, const float* offset, int64_t r, int k,
+                                          int lane, uint64_t key, bool log_softmax, float shift, float lse) {
+  if (lane < k) {
+    float v = key_value(key);
+    if (log_softmax) v = (v - shift) - lse;  // log_softmax as (x - max) - log(sum)
+    values[r * k + lane] = v + (offset != nullptr ? offset[r] : 0.0f);
+    indices[r * k + lane] = (int32_t)key_index(key);
+  }
+}
+
+// The chunk a CTA walks: a contiguous range of the row's 16-byte vectors; chunk 0 also takes the
+// ragged head, the last chunk the ragged tail (fewer than 8 elements each, warp 0).
+template <typename T>
+struct ChunkWalk {
+  using V = Vec16<T>;
+  static constexpr int U = 32 / V::N;  // a lane's batch: 32 elements, U 16-byte loads in flight
+  const T* x;
+  const T* xv;
+  int64_t vocab, head, tail0, vbegin, vend;
+  bool first, last;
+
+  __device__ ChunkWalk(const T* row, int64_t vocab_, int chunk, int chunks) : x(row), vocab(vocab_) {
+    const int64_t mis = (reinterpret_cast<uintptr_t>(row) & 15u) / sizeof(T);
+    head = mis == 0 ? 0 : (16 / (int64_t)sizeof(T)) - mis;
+    head = head < vocab ? head : vocab;
+    const int64_t nvec = (vocab - head) / V::N;
+    tail0 = head + nvec * V::N;
+    xv = x + head;
+    const int64_t per = ceil_div(nvec, (int64_t)chunks);
+    vbegin = chunk * per;
+    vend = vbegin + per < nvec ? vbegin + per : nvec;
+    first = chunk == 0;
+    last = chunk == chunks - 1;
+  }
+
+  // f(ok, values[U][N], first element index of each of the U vectors) once per batch, the same
+  // number of times in every lane of a warp; then the ragged ends for warp 0 (one value a lane)
+  template <typename F, typename G>
+  __device__ __forceinline__ void walk(int warp, int lane, F&& batch, G&& single) const {
+    for (int64_t base = vbegin + (int64_t)warp * 32; base < vend; base += (int64_t)kTopkThreads * U) {
+      float e[U][V::N];
+      bool ok[U];
+      int64_t idx[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int64_t v = base + lane + (int64_t)u * kTopkThreads;
+        ok[u] = v < vend;
+        idx[u] = head + v * V::N;
+        if (ok[u]) V::load(xv + v * V::N, e[u]);
+      }
+      batch(ok, e, idx);
+    }
+    if (warp == 0) {
+      for (int part = 0; part < 2; ++part) {
+        if ((part == 0 && !first) || (part == 1 && !last)) continue;
+        const int64_t begin = part == 0 ? 0 : tail0, end = part == 0 ? head : vocab;
+        const bool ok1 = begin + lane < end;
+        single(ok1, ok1 ? to_float(x[begin + lane]) : -INFINITY, begin + lane);
+      }
+    }
+  }
+};
+
+// grid: rows x chunks, two passes over the CTA's chunk.
+//  pass 1: each lane folds its batches into (max, sum of exp) and offers only the batch maximum
+//          to its warp's list; the k-th largest batch maximum of the CTA, T, is a lower bound of
+//          the chunk's k-th largest value (batch maxima are distinct elements of the chunk).
+//  pass 2: the chunk again (now from L2): one compare per element, one ballot per batch; only
+//          batches holding a value >= T insert into the candidate lists.
+// With one chunk the CTA writes the row's result, otherwise its TopkPartial.
+template <typename T, bool kLogSoftmax>
+__global__ void __launch_bounds__(kTopkThreads, 3) row_topk_warp_kernel(const T* __restrict__ scores, int64_t vocab,
+                                                                     int64_t row_stride,
+                                                                     const float* __restrict__ offset, int k,
+                                                                     int chunks, float* __restrict__ values,
+                                                                     int32_t* __restrict__ indices,
+                                                                     TopkPartial* __restrict__ partials) {
+  constexpr int kWarps = kTopkThreads / 32;
+  using W = ChunkWalk<T>;
+  __shared__ uint64_t warp_best[kWarps][32];
+  __shared__ RowStats warp_stats[kWarps];
+  __shared__ float s_threshold;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t r = blockIdx.x / chunks;
+  const int chunk = blockIdx.x - (int)(r * chunks);
+  const W walk(scores + r * row_stride, vocab, chunk, chunks);
+
+  // ---- pass 1: statistics and batch maxima
+  WarpList maxima;
+  RowStats st{-INFINITY, 0.0f};
+  walk.walk(
+      warp, lane,
+      [&](const bool (&ok)[W::U], const float (&e)[W::U][W::V::N], const int64_t (&idx)[W::U]) {
+        float bm = -INFINITY;
+        bool any = false;
+#pragma unroll
+        for (int u = 0; u < W::U; ++u)
+          if (ok[u]) {
+            any = true;
+#pragma unroll
+            for (int q = 0; q < W::V::N; ++q) bm = fmaxf(bm, e[u][q]);
+          }
+        if (kLogSoftmax && any) {
+          stats_rescale(st, bm);
+          if (st.m != -INFINITY) {
+            float add = 0.0f;
+#pragma unroll
+            for (int u = 0; u < W::U; ++u)
+              if (ok[u]) {
+#pragma unroll
+                for (int q = 0; q < W::V::N; ++q) add += exp2_approx((e[u][q] - st.m) * kLog2e);
+              }
+            st.s += add;
+          }
+        }
+        maxima.offer_value(any, bm, (uint32_t)idx[0], lane, k);
+      },
+      [&](bool ok1, float v, int64_t i) {
+        if (kLogSoftmax && ok1) {
+          stats_rescale(st, v);
+          if (st.m != -INFINITY) st.s += exp2_approx((v - st.m) * kLog2e);
+        }
+        maxima.offer_value(ok1, v, (uint32_t)i, lane, k);
+      });
+  if (lane < k) warp_best[warp][lane] = maxima.mine;
+  if (kLogSoftmax) {
+#pragma unroll
+    for (int m = 16; m >= 1; m >>= 1) {
+      RowStats o{__shfl_xor_sync(0xffffffffu, st.m, m), __shfl_xor_sync(0xffffffffu, st.s, m)};
+      st = stats_merge(st, o);
+    }
+    if (lane == 0) warp_stats[warp] = st;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    for (int w = 1; w < kWarps; ++w) {
+      const uint64_t key = lane < k ? warp_best[w][lane] : 0ull;
+      maxima.offer_if(key != 0, key, lane, k);
+    }
+    if (lane == 0) s_threshold = maxima.thr == 0 ? -INFINITY : key_value(maxima.thr);
+  }
+  __syncthreads();
+  const float thr = s_threshold;
+
+  // ---- pass 2: every value >= T competes
+  WarpList cand;
+  walk.walk(
+      warp, lane,
+      [&](const bool (&ok)[W::U], const float (&e)[W::U][W::V::N], const int64_t (&idx)[W::U]) {
+        bool any = false;
+#pragma unroll
+        for (int u = 0; u < W::U; ++u)
+#pragma unroll
+          for (int q = 0; q < W::V::N; ++q) any |= ok[u] && e[u][q] >= thr;
+        if (__ballot_sync(0xffffffffu, any) == 0u) return;
+#pragma unroll
+        for (int u = 0; u < W::U; ++u)
+#pragma unroll
+          for (int q = 0; q < W::V::N; ++q)
+            cand.offer_value(ok[u] && e[u][q] >= thr, e[u][q], (uint32_t)(idx[u] + q), lane, k);
+      },
+      [&](bool ok1, float v, int64_t i) { cand.offer_value(ok1 && v >= thr, v, (uint32_t)i, lane, k); });
+
+  __syncthreads();  // warp_best is reused
+  if (lane < k) warp_best[warp][lane] = cand.mine;
+  __syncthreads();
+  if (warp != 0) return;
+  for (int w = 1; w < kWarps; ++w) {
+    const uint64_t key = lane < k ? warp_best[w][lane] : 0ull;
+    cand.offer_if(key != 0, key, lane, k);
+  }
+  RowStats all{-INFINITY, 0.0f};
+  if (kLogSoftmax) {
+    all = warp_stats[0];
+    for (int w = 1; w < kWarps; ++w) all = stats_merge(all, warp_stats[w]);
+  }
+  if (chunks == 1) {
+    write_row(values, indices, offset, r, k, lane, cand.mine, kLogSoftmax, all.m, kLogSoftmax ? logf(all.s) : 0.0f);
+  } else {
+    TopkPartial& part = partials[r * chunks + chunk];
+    part.keys[lane] = lane < k ? cand.mine : 0ull;
+    if (lane == 0) {
+      part.m = all.m;
+      part.s = all.s;
+    }
+  }
+}
+
+// One warp per row: the row's chunk partials merged into its final top-k.
+template <bool kLogSoftmax>
+__global__ void row_topk_merge_kernel(const TopkPartial* __restrict__ partials, int chunks, const float* offset,
+                                      int k, float* __restrict__ values, int32_t* __restrict__ indices) {
+  const int lane = threadIdx.x;
+  const int64_t r = blockIdx.x;
+  WarpList wl;
+  RowStats all{-INFINITY, 0.0f};
+  for (int c = 0; c < chunks; ++c) {
+    const TopkPartial& part = partials[r * chunks + c];
+    const uint64_t key = lane < k ? part.keys[lane] : 0ull;
+    wl.offer_if(key != 0, key, lane, k);
+    if (kLogSoftmax) all = stats_merge(all, RowStats{part.m, part.s});
+  }
+  write_row(values, indices, offset, r, k, lane, wl.mine, kLogSoftmax, all.m, kLogSoftmax ? logf(all.s) : 0.0f);
 }
 
 // One warp per request group: its rows (found by group id, placed by rank), then `keep` rounds
@@ -282,14 +573,31 @@ int launch_topk_k(const T* scores, int64_t rows, int64_t vocab, int64_t stride, 
 
 template <typename T>
 int launch_topk(const T* scores, int64_t rows, int64_t vocab, int64_t stride, int log_softmax, const float* offset,
-                int k, float* values, int32_t* indices, cudaStream_t s) {
-  if (k <= 1) return launch_topk_k<T, 1>(scores, rows, vocab, stride, log_softmax, offset, k, values, indices, s);
-  if (k <= 2) return launch_topk_k<T, 2>(scores, rows, vocab, stride, log_softmax, offset, k, values, indices, s);
-  if (k <= 4) return launch_topk_k<T, 4>(scores, rows, vocab, stride, log_softmax, offset, k, values, indices, s);
-  if (k <= 8) return launch_topk_k<T, 8>(scores, rows, vocab, stride, log_softmax, offset, k, values, indices, s);
-  if (k <= 16) return launch_topk_k<T, 16>(scores, rows, vocab, stride, log_softmax, offset, k, values, indices, s);
-  if (k <= 32) return launch_topk_k<T, 32>(scores, rows, vocab, stride, log_softmax, offset, k, values, indices, s);
-  return launch_topk_k<T, 64>(scores, rows, vocab, stride, log_softmax, offset, k, values, indices, s);
+                int k, float* values, int32_t* indices, void* workspace, size_t workspace_bytes, cudaStream_t s) {
+  if (k > 32) return launch_topk_k<T, 64>(scores, rows, vocab, stride, log_softmax, offset, k, values, indices, s);
+  const int chunks = topk_chunks(rows, vocab, k);
+  TopkPartial* partials = nullptr;
+  if (chunks > 1) {
+    const size_t need = (size_t)rows * chunks * sizeof(TopkPartial);
+    if (workspace == nullptr || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 15u) != 0)
+      return fail(VFL_ERR_WORKSPACE, "row_topk: needs %zu workspace bytes (16-byte aligned), got %zu", need,
+                  workspace_bytes);
+    partials = static_cast<TopkPartial*>(workspace);
+  }
+  const unsigned grid = (unsigned)(rows * chunks);
+  if (log_softmax)
+    row_topk_warp_kernel<T, true><<<grid, kTopkThreads, 0, s>>>(scores, vocab, stride, offset, k, chunks, values,
+                                                                indices, partials);
+  else
+    row_topk_warp_kernel<T, false><<<grid, kTopkThreads, 0, s>>>(scores, vocab, stride, offset, k, chunks, values,
+                                                                 indices, partials);
+  int st = cuda_status(cudaGetLastError(), "row_topk launch");
+  if (st || chunks == 1) return st;
+  if (log_softmax)
+    row_topk_merge_kernel<true><<<(unsigned)rows, 32, 0, s>>>(partials, chunks, offset, k, values, indices);
+  else
+    row_topk_merge_kernel<false><<<(unsigned)rows, 32, 0, s>>>(partials, chunks, offset, k, values, indices);
+  return cuda_status(cudaGetLastError(), "row_topk merge launch");
 }
 
 }  // namespace
@@ -297,11 +605,16 @@ int launch_topk(const T* scores, int64_t rows, int64_t vocab, int64_t stride, in
 
 using namespace vfl;
 
+extern "C" size_t vfl_row_topk_workspace_size(int64_t rows, int64_t vocab, int32_t k) {
+  const int chunks = topk_chunks(rows, vocab, k);
+  return chunks > 1 ? (size_t)rows * chunks * sizeof(TopkPartial) : 0;
+}
+
 extern "C" int vfl_row_topk(const void* scores, int32_t dtype, int64_t rows, int64_t vocab, int64_t row_stride,
                             int32_t log_softmax, const float* row_offset, int32_t k, float* values,
-                            int32_t* indices, void* stream) {
+                            int32_t* indices, void* workspace, size_t workspace_bytes, void* stream) {
   if (!dtype_ok(dtype)) return fail(VFL_ERR_UNSUPPORTED, "row_topk: dtype %d is not float32 or bfloat16", dtype);
-  if (rows < 0 || rows > INT32_MAX || vocab < 1 || vocab > INT32_MAX || row_stride < vocab)
+  if (rows < 0 || rows > INT32_MAX / kMaxChunks || vocab < 1 || vocab > INT32_MAX || row_stride < vocab)
     return fail(VFL_ERR_INVALID_ARGUMENT, "row_topk: rows %lld, vocab %lld, row stride %lld", (long long)rows,
                 (long long)vocab, (long long)row_stride);
   if (k < 1 || k > kMaxK || k > vocab)
@@ -315,9 +628,9 @@ extern "C" int vfl_row_topk(const void* scores, int32_t dtype, int64_t rows, int
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (dtype == VFL_DTYPE_F32)
     return launch_topk(static_cast<const float*>(scores), rows, vocab, row_stride, log_softmax, row_offset, k,
-                       values, indices, s);
+                       values, indices, workspace, workspace_bytes, s);
   return launch_topk(static_cast<const __nv_bfloat16*>(scores), rows, vocab, row_stride, log_softmax, row_offset, k,
-                     values, indices, s);
+                     values, indices, workspace, workspace_bytes, s);
 }
 
 extern "C" int vfl_beam_merge(const float* values, const int32_t* indices, int64_t rows, int32_t k,

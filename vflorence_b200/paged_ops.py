@@ -321,10 +321,13 @@ def row_topk(scores: torch.Tensor, k: int, log_softmax: bool = False, row_offset
     if out is None:
         out = (torch.empty(rows, k, dtype=torch.float32, device=dev), torch.empty(rows, k, dtype=torch.int32, device=dev))
     values, indices = out
-    st = N.lib().vfl_row_topk(scores.data_ptr(), _dtype_code(scores.dtype), rows, vocab,
-                              scores.stride(0) if rows > 1 else vocab, int(bool(log_softmax)),
-                              None if row_offset is None else row_offset.data_ptr(), int(k), values.data_ptr(),
-                              indices.data_ptr(), _stream(dev))
+    lib = N.lib()
+    ws_bytes = lib.vfl_row_topk_workspace_size(rows, vocab, int(k)) if 1 <= k <= vocab else 0
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev) if ws_bytes else None
+    st = lib.vfl_row_topk(scores.data_ptr(), _dtype_code(scores.dtype), rows, vocab,
+                          scores.stride(0) if rows > 1 else vocab, int(bool(log_softmax)),
+                          None if row_offset is None else row_offset.data_ptr(), int(k), values.data_ptr(),
+                          indices.data_ptr(), None if ws is None else ws.data_ptr(), ws_bytes, _stream(dev))
     N.check(st, "row_topk")
     return values, indices
 
