@@ -33,7 +33,7 @@
 extern "C" {
 #endif
 
-#define VFL_ABI_VERSION 2
+#define VFL_ABI_VERSION 3
 
 typedef enum vfl_status {
   VFL_OK = 0,
@@ -79,6 +79,8 @@ typedef struct vfl_attention_plan {
   int32_t merge_in_kernel;  /* split partials merged by the last split CTA (1) or by a
                                separate combine launch (0)                              */
   int64_t workspace_bytes;  /* scratch the caller must pass (0 = none)                   */
+  int32_t row_tables;       /* 1: block_table rows are query rows (vfl_plan_attention_row_tables) */
+  int32_t reserved;
 } vfl_attention_plan;
 
 #define VFL_PLAN_MAGIC 0x31504c4656LL /* "VFLP1" */
@@ -110,6 +112,19 @@ int vfl_get_isa(int dtype, int block_size, int head_dim, char* buf, int buf_len)
 int vfl_plan_attention(int num_reqs, int num_heads, int num_kv_heads, int head_dim,
                        int block_size, int dtype, int causal, const int32_t* seq_lens_host,
                        const int32_t* query_start_loc_host, vfl_attention_plan* plan);
+
+/* A plan for requests whose query rows each have their own block table - the beams of one
+ * request in beam search, which share most of their blocks (copy-on-write forks) but not all.
+ * With this plan, vfl_attention_with_kv_cache reads row i's table at block_table + i *
+ * table_stride (query rows, not requests); query_start_loc groups the rows of a request and
+ * seq_lens holds one length per request (its rows must all see that many tokens). A CTA serves
+ * up to 8 rows of a request and loads each distinct block of a tile position once, for all the
+ * rows that hold it. Extends vllm_cpu_attn.get_scheduler_metadata (attention.py:18-29), where
+ * every beam is its own request. bf16 with head_dim 64 only (VFL_ERR_UNSUPPORTED otherwise);
+ * never causal. */
+int vfl_plan_attention_row_tables(int num_reqs, int num_heads, int num_kv_heads, int head_dim,
+                                  int block_size, int dtype, const int32_t* seq_lens_host,
+                                  const int32_t* query_start_loc_host, vfl_attention_plan* plan);
 
 /* replaces vllm_cpu_attn.reshape_and_cache(key, value, k_cache, v_cache, slot_mapping, isa=)
  *   (vflorence/layers/attention.py:55-57, vflorence/engine/model_runner.py:252-259).

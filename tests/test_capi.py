@@ -29,7 +29,7 @@ def test_library_exports_every_declared_symbol(native):
     assert sorted(declared) == sorted(_native.EXPORTS)
     for name in declared:
         assert hasattr(native, name), name
-    assert native.vfl_abi_version() == _native.ABI_VERSION == 2
+    assert native.vfl_abi_version() == _native.ABI_VERSION == 3
 
 
 def test_status_strings(native):

@@ -267,3 +267,77 @@ def test_device_lengths_beyond_the_plan_are_clamped_and_flagged(oracle_lib):
     assert o.read_device_errors(DEV) & 0x4  # VFL_DEVERR_CONTEXT
     ref = oracle_attn(oracle_lib, q, kc, vc, qsl, planned, table, 0.125)
     assert_attention_close(got, ref, torch.float32, "clamped")
+
+
+def beam_case(*, requests, beams, block_size, max_len, seed, heads=16, head_dim=64):
+    """Beam-search self-attention: each request's rows (its beams) share a prefix of blocks and
+    then diverge (copy-on-write forks); a request's rows see the same number of tokens."""
+    g = torch.Generator().manual_seed(seed)
+    gd = torch.Generator(device=DEV).manual_seed(seed)
+    counts = [int(torch.randint(1, beams + 1, (1,), generator=g)) for _ in range(requests)]
+    lens = torch.randint(1, max_len + 1, (requests,), generator=g, dtype=torch.int32)
+    nbs = [max(1, math.ceil(int(n) / block_size)) for n in lens]
+    rows = sum(counts)
+    width = max(nbs)
+    table = torch.zeros(rows, width, dtype=torch.int32)
+    next_block = 0
+    row = 0
+    for r, (c, nb) in enumerate(zip(counts, nbs)):
+        base = torch.arange(next_block, next_block + nb, dtype=torch.int32)
+        next_block += nb
+        for b in range(c):
+            t = base.clone()
+            shared = int(torch.randint(0, nb + 1, (1,), generator=g)) if b else nb  # row 0 keeps all
+            for j in range(shared, nb):
+                t[j] = next_block
+                next_block += 1
+            if b and int(torch.randint(0, 3, (1,), generator=g)) == 0 and nb > 1:
+                t[0] = table[row - 1, 0]  # also share with a sibling rather than row 0
+            table[row, :nb] = t
+            row += 1
+    perm = torch.randperm(next_block + 3, generator=g).to(torch.int32)
+    table = perm[table.long()] * (table >= 0)
+    qsl = torch.tensor([0] + torch.tensor(counts).cumsum(0).tolist(), dtype=torch.int32)
+    kc = torch.randn(next_block + 3, heads, block_size, head_dim, generator=gd, device=DEV, dtype=torch.bfloat16)
+    vc = torch.randn_like(kc)
+    q = torch.randn(rows, heads, head_dim, generator=gd, device=DEV, dtype=torch.bfloat16)
+    row_lens = torch.repeat_interleave(lens, torch.tensor(counts))
+    return q, kc, vc, qsl, lens, row_lens, table
+
+
+@pytest.mark.parametrize("requests,beams,block_size,max_len,seed", [
+    (40, 3, 16, 150, 1), (12, 4, 16, 2500, 2), (7, 8, 32, 900, 3), (64, 5, 16, 60, 4), (3, 2, 16, 4096, 5),
+    (6, 12, 16, 300, 6)])
+def test_row_tables_match_per_row_requests(oracle_lib, requests, beams, block_size, max_len, seed):
+    """One CTA serves the beams of a request with their own block tables (shared prefix, forked
+    tails); the result equals attention with every beam as its own request."""
+    o = ops()
+    q, kc, vc, qsl, lens, row_lens, table = beam_case(requests=requests, beams=beams, block_size=block_size,
+                                                      max_len=max_len, seed=seed)
+    n, h, bs, d = kc.shape
+    meta = o.get_scheduler_metadata(requests, h, h, d, lens, torch.bfloat16, qsl, False, "sm100", bs, row_tables=True)
+    plan = o.plan_of(meta)
+    assert plan.row_tables == 1 and plan.queries_per_cta == 8
+    out = torch.full(q.shape, float("nan"), dtype=q.dtype, device=DEV)
+    o.attention_with_kv_cache(q, kc, vc, out, qsl.to(DEV), lens.to(DEV), d ** -0.5, False, table.to(DEV), meta)
+    rows_qsl = torch.arange(q.shape[0] + 1, dtype=torch.int32)
+    want = oracle_attn(oracle_lib, q.cpu(), kc.cpu(), vc.cpu(), rows_qsl, row_lens, table, d ** -0.5)
+    assert_attention_close(out.cpu(), want, torch.bfloat16, f"row tables {requests}x{beams} bs{bs} len<={max_len}")
+    # and the per-row kernel agrees
+    per_row, _ = kernel(q, kc, vc, rows_qsl, row_lens, table, d ** -0.5)
+    assert_attention_close(out.cpu(), per_row, torch.bfloat16, "row tables vs per-row kernel")
+    assert o.read_device_errors(DEV) == 0
+    if max_len >= 2500:
+        assert plan.num_splits > 1  # the split path and its merge are exercised
+
+
+def test_row_tables_refused_where_not_built():
+    o = ops()
+    from vflorence_b200._native import VflError
+
+    lens = torch.tensor([10, 20], dtype=torch.int32)
+    qsl = torch.tensor([0, 2, 4], dtype=torch.int32)
+    with pytest.raises(VflError, match="row tables"):
+        o.get_scheduler_metadata(2, 16, 16, 64, lens, torch.float32, qsl, False, "sm100", 16, row_tables=True)
+    with pytest.raises(ValueError, match="causal"):
+        o.get_scheduler_metadata(2, 16, 16, 64, lens, torch.bfloat16, qsl, True, "sm100", 16, row_tables=True)

@@ -118,6 +118,13 @@ __device__ __forceinline__ uint64_t l2_evict_first_policy() {
   return pol;
 }
 
+// L2 policy for data other CTAs read soon after (blocks shared by the beams of a request).
+__device__ __forceinline__ uint64_t l2_evict_normal_policy() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+
 // bulk_copy_g2s with an L2 cache-policy hint.
 __device__ __forceinline__ void bulk_copy_g2s_hint(void* dst, const void* src, uint32_t bytes,
                                                    uint64_t* bar, uint64_t policy) {

@@ -116,6 +116,8 @@ int check_attention_plan(const vfl_attention_plan* plan) {
     return fail(VFL_ERR_INVALID_ARGUMENT, "attention: plan splits do not cover max_seq_len %d", plan->max_seq_len);
   if (plan->merge_in_kernel != 0 && plan->merge_in_kernel != 1)
     return fail(VFL_ERR_INVALID_ARGUMENT, "attention: plan merge mode %d", plan->merge_in_kernel);
+  if (plan->row_tables != 0 && (plan->row_tables != 1 || !tc || plan->causal))
+    return fail(VFL_ERR_INVALID_ARGUMENT, "attention: plan row_tables needs the tensor-core kernel, not causal");
   const int64_t q_chunks = ceil_div((int64_t)(plan->max_q_len < 1 ? 1 : plan->max_q_len), (int64_t)qpc);
   if (q_chunks > 65535 || (int64_t)plan->num_reqs * (H / hpc) > INT32_MAX)
     return fail(VFL_ERR_INVALID_ARGUMENT, "attention: plan launch grid too large");
@@ -272,6 +274,22 @@ int vfl_plan_attention(int num_reqs, int num_heads, int num_kv_heads, int head_d
   plan->stages = stages;
   plan->merge_in_kernel = merge_in_kernel;
   plan->workspace_bytes = ws;
+  plan->row_tables = 0;
+  plan->reserved = 0;
+  return VFL_OK;
+}
+
+int vfl_plan_attention_row_tables(int num_reqs, int num_heads, int num_kv_heads, int head_dim, int block_size,
+                                  int dtype, const int32_t* seq_lens_host, const int32_t* query_start_loc_host,
+                                  vfl_attention_plan* plan) {
+  if (!use_tensor_cores(dtype, head_dim))
+    return plan_fail(plan, fail(VFL_ERR_UNSUPPORTED, "row tables: built for bfloat16 with head_dim 64 only"));
+  if (query_start_loc_host == nullptr && num_reqs > 0)
+    return plan_fail(plan, fail(VFL_ERR_INVALID_ARGUMENT, "row tables: query_start_loc_host is NULL"));
+  const int st = vfl_plan_attention(num_reqs, num_heads, num_kv_heads, head_dim, block_size, dtype, 0, seq_lens_host,
+                                    query_start_loc_host, plan);
+  if (st) return st;
+  plan->row_tables = 1;
   return VFL_OK;
 }
 
@@ -330,6 +348,7 @@ int vfl_attention_with_kv_cache(const vfl_attention_plan* plan, const void* quer
   p.num_splits = plan->num_splits;
   p.stages = plan->stages;
   p.max_seq_len = plan->max_seq_len;
+  p.row_tables = plan->row_tables;
   p.scale_log2 = scale * 1.4426950408889634f;
   int st = device_error_word(&p.err);
   if (st) return st;

@@ -39,7 +39,7 @@ struct AttnParams {
   int64_t out_stride;
   const int32_t* qsl;       // [num_reqs + 1]
   const int32_t* seq_lens;  // [num_reqs]
-  const int32_t* table;     // [num_reqs, table_stride]
+  const int32_t* table;     // [num_reqs, table_stride], or [total_q, table_stride] with row_tables
   int64_t table_stride;
   int32_t table_cols;
   int32_t num_reqs;
@@ -52,6 +52,7 @@ struct AttnParams {
   int32_t num_splits;  // workspace stride (max splits of any request)
   int32_t stages;
   int32_t max_seq_len;  // planned maximum; longer device lengths are clamped and reported
+  int32_t row_tables;   // 1: one block table per query row (tensor-core kernel only)
   float scale_log2;  // softmax scale * log2(e)
   float* ws_acc;     // [total_q, H, num_splits, D]
   float* ws_ml;      // [total_q, H, num_splits, 2]
@@ -514,7 +515,7 @@ __global__ void __launch_bounds__(128) paged_attention_combine_kernel(const Attn
 }
 
 // Tensor-core variant (paged_attention_tc.cuh): bf16, head_dim 64, up to kTcRows rows per CTA.
-constexpr int kTcHeaderBytes = 2048;  // SmemHeader + one 8x16 bf16 P tile per consumer warp
+constexpr int kTcHeaderBytes = 4096;  // SmemHeader | one 8x16 bf16 P tile per consumer warp | row tables
 constexpr int kTcRows = 8;            // query rows per CTA (the mma N dimension)
 int launch_paged_attention_tc(const AttnParams& p, const CUtensorMap& kmap, const CUtensorMap& vmap, dim3 grid,
                               int threads, int smem_bytes, cudaStream_t stream);

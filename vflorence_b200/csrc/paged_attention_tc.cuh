@@ -20,9 +20,39 @@
 
 namespace vfl {
 
-constexpr int kTcPTileOffset = 1024;  // P tiles after the SmemHeader
-static_assert(sizeof(SmemHeader) <= kTcPTileOffset && kTcPTileOffset + 4 * kTcRows * 16 * 2 <= kTcHeaderBytes,
+constexpr int kTcPTileOffset = 1024;     // P tiles after the SmemHeader
+constexpr int kTcRowTableOffset = 2048;  // per-row block-table slices (row_tables plans)
+static_assert(sizeof(SmemHeader) <= kTcPTileOffset && kTcPTileOffset + 4 * kTcRows * 16 * 2 <= kTcRowTableOffset &&
+                  kTcRowTableOffset + kTcRows * kMaxBlocksPerSplit * 4 <= kTcHeaderBytes,
               "tc header");
+
+// The blocks of one tile position, in a fixed order that the producer and every consumer warp
+// derive alike: row j's block unless an earlier row already holds it, with the mask of the rows
+// that hold it. Plans without row tables have one block per position, for every row.
+struct TileBlocks {
+  const int32_t* rows;  // row tables [kTcRows][kMaxBlocksPerSplit], or null
+  const int32_t* table; // the request's slice
+  int nq;
+
+  __device__ __forceinline__ int count_and_get(int bi, int j, unsigned done, int64_t* phys, unsigned* mask) const {
+    // returns the next row >= j that starts a new block (or nq), with that block and its rows
+    if (rows == nullptr) {
+      if (j > 0) return nq;
+      *phys = table[bi];
+      *mask = (1u << nq) - 1u;
+      return 0;
+    }
+    while (j < nq && ((done >> j) & 1u)) ++j;
+    if (j >= nq) return nq;
+    const int32_t b = rows[j * kMaxBlocksPerSplit + bi];
+    unsigned m = 0;
+    for (int t = j; t < nq; ++t)
+      if (rows[t * kMaxBlocksPerSplit + bi] == b) m |= 1u << t;
+    *phys = b;
+    *mask = m;
+    return j;
+  }
+};
 
 __device__ __forceinline__ uint32_t swz(uint32_t tile_base, int row, int chunk) {
   const uint32_t row_addr = tile_base + row * 128;
@@ -123,17 +153,25 @@ __global__ void __launch_bounds__(160, 3) paged_attention_tc_kernel(const AttnPa
   const int stage_elems = 2 * hpc * TILE;
   const uint32_t head_tile_bytes = TILE * sizeof(T);
 
+  int32_t* row_tab = reinterpret_cast<int32_t*>(smem + kTcRowTableOffset);
   if (producer) {
     const int nb = min(bps, nblk - blk_begin);
-    for (int i = lane; i < nb; i += 32) {
-      int b = __ldg(p.table + r * p.table_stride + blk_begin + i);
+    const int nrows = p.row_tables ? nq : 1;
+    for (int e = lane; e < nrows * nb; e += 32) {
+      const int j = e / nb, i = e - j * nb;
+      const int64_t trow = p.row_tables ? (int64_t)(q0 + j) : (int64_t)r;
+      int b = __ldg(p.table + trow * p.table_stride + blk_begin + i);
       if (b < 0 || b >= p.num_blocks) {
         report(p.err, VFL_DEVERR_BLOCK_ID);
         b = 0;
       }
-      hdr.table[i] = b;
+      if (p.row_tables)
+        row_tab[j * kMaxBlocksPerSplit + i] = b;
+      else
+        hdr.table[i] = b;
     }
   }
+  const TileBlocks tiles{p.row_tables ? row_tab : nullptr, hdr.table, nq};
   if (threadIdx.x == 0) {
     for (int s = 0; s < stages; ++s) {
       mbar_init(&hdr.full[s], 1);
@@ -146,36 +184,49 @@ __global__ void __launch_bounds__(160, 3) paged_attention_tc_kernel(const AttnPa
   __syncthreads();
 
   if (producer) {
+    // units: (tile position, distinct block of the position); u counts them across the item
     int issued = 0;
     if (lane == 0) {
-      const uint64_t policy = l2_evict_first_policy();
-      for (int i = 0; i < ntiles; ++i) {
-        const int s = i % stages;
-        if (i >= stages && !mbar_wait_bounded(&hdr.empty[s], ((i / stages) - 1) & 1)) {
-          report(p.err, VFL_DEVERR_TIMEOUT);
-          hdr.abort = 1;
-          break;
-        }
-        if (*reinterpret_cast<volatile int*>(&hdr.abort)) break;
-        fence_proxy_async_smem();
+      const uint64_t policy = p.row_tables ? l2_evict_normal_policy() : l2_evict_first_policy();
+      int u = 0;
+      bool stop = false;
+      for (int i = 0; i < ntiles && !stop; ++i) {
         const int tile = tile_begin + i;
         const int blk = tile / tpb;
         const int sub_tile = tile - blk * tpb;
-        const int64_t phys = hdr.table[blk - blk_begin];
-        T* ks = s_kv + (size_t)s * stage_elems;
-        T* vs = ks + hpc * TILE;
-        mbar_arrive_expect_tx(&hdr.full[s], 2u * hpc * head_tile_bytes);
-        const int row0 = static_cast<int>((phys * p.num_heads + h0) * bs + sub_tile * 16);
-        if (tpb == 1) {  // the head group's tiles are adjacent rows: one box of 16 * hpc rows
-          tma_load_2d(ks, &kmap, 0, row0, &hdr.full[s], policy);
-          tma_load_2d(vs, &vmap, 0, row0, &hdr.full[s], policy);
-        } else {
-          for (int w = 0; w < hpc; ++w) {
-            tma_load_2d(ks + w * TILE, &kmap, 0, row0 + w * bs, &hdr.full[s], policy);
-            tma_load_2d(vs + w * TILE, &vmap, 0, row0 + w * bs, &hdr.full[s], policy);
+        unsigned done = 0;
+        int64_t phys;
+        unsigned mask;
+        for (int j = tiles.count_and_get(blk - blk_begin, 0, done, &phys, &mask); j < nq;
+             j = tiles.count_and_get(blk - blk_begin, j + 1, done, &phys, &mask)) {
+          done |= mask;
+          const int s = u % stages;
+          if (u >= stages && !mbar_wait_bounded(&hdr.empty[s], ((u / stages) - 1) & 1)) {
+            report(p.err, VFL_DEVERR_TIMEOUT);
+            hdr.abort = 1;
+            stop = true;
+            break;
           }
+          if (*reinterpret_cast<volatile int*>(&hdr.abort)) {
+            stop = true;
+            break;
+          }
+          fence_proxy_async_smem();
+          T* ks = s_kv + (size_t)s * stage_elems;
+          T* vs = ks + hpc * TILE;
+          mbar_arrive_expect_tx(&hdr.full[s], 2u * hpc * head_tile_bytes);
+          const int row0 = static_cast<int>((phys * p.num_heads + h0) * bs + sub_tile * 16);
+          if (tpb == 1) {  // the head group's tiles are adjacent rows: one box of 16 * hpc rows
+            tma_load_2d(ks, &kmap, 0, row0, &hdr.full[s], policy);
+            tma_load_2d(vs, &vmap, 0, row0, &hdr.full[s], policy);
+          } else {
+            for (int w = 0; w < hpc; ++w) {
+              tma_load_2d(ks + w * TILE, &kmap, 0, row0 + w * bs, &hdr.full[s], policy);
+              tma_load_2d(vs + w * TILE, &vmap, 0, row0 + w * bs, &hdr.full[s], policy);
+            }
+          }
+          issued = ++u;
         }
-        issued = i + 1;
       }
     }
     __syncwarp();
@@ -222,21 +273,32 @@ __global__ void __launch_bounds__(160, 3) paged_attention_tc_kernel(const AttnPa
   const int v_row = (lane & 7) + (mat >> 1) * 8, v_chunk_hi = mat & 1;
 
   bool aborted = false;
+  int u = 0;
 #pragma unroll 1
-  for (int i = 0; i < ntiles; ++i) {
-    const int s = i % stages;
-    if (!mbar_wait_bounded(&hdr.full[s], (i / stages) & 1)) {
+  for (int i = 0; i < ntiles && !aborted; ++i) {
+    const int tok0 = (tile_begin + i) * 16;
+    const int bi = (tile_begin + i) / tpb - blk_begin;
+    unsigned done = 0;
+    int64_t phys_unused;
+    unsigned mask;
+#pragma unroll 1
+    for (int j = tiles.count_and_get(bi, 0, done, &phys_unused, &mask); j < nq;
+         j = tiles.count_and_get(bi, j + 1, done, &phys_unused, &mask)) {
+    done |= mask;
+    const int s = u % stages;
+    if (!mbar_wait_bounded(&hdr.full[s], (u / stages) & 1)) {
       report(p.err, VFL_DEVERR_TIMEOUT);
       if (lane == 0) {
         hdr.abort = 1;
-        atomicMax(&hdr.consumed, i);
+        atomicMax(&hdr.consumed, u);
       }
       aborted = true;
       break;
     }
     const uint32_t kt = smem_u32(s_kv + (size_t)s * stage_elems + warp * TILE);
     const uint32_t vt = kt + hpc * TILE * sizeof(T);
-    const int tok0 = (tile_begin + i) * 16;
+    // the rows this unit's block belongs to (every row without row tables)
+    const bool row_on[2] = {col_on[0] && ((mask >> (2 * tq)) & 1u), col_on[1] && ((mask >> (2 * tq + 1)) & 1u)};
 
     // S[token g, g+8][query 2tq, 2tq+1]
     float sc[4] = {0.f, 0.f, 0.f, 0.f};
@@ -251,8 +313,8 @@ __global__ void __launch_bounds__(160, 3) paged_attention_tc_kernel(const AttnPa
     __nv_bfloat16 pb[4];
 #pragma unroll
     for (int e = 0; e < 2; ++e) {
-      const bool v0 = col_on[e] && tok0 + g < vis_c[e];
-      const bool v1 = col_on[e] && tok0 + g + 8 < vis_c[e];
+      const bool v0 = row_on[e] && tok0 + g < vis_c[e];
+      const bool v1 = row_on[e] && tok0 + g + 8 < vis_c[e];
       const float s0 = v0 ? sc[e] * p.scale_log2 : -INFINITY;
       const float s1 = v1 ? sc[e + 2] * p.scale_log2 : -INFINITY;
       float mx = fmaxf(s0, s1);
@@ -291,6 +353,8 @@ __global__ void __launch_bounds__(160, 3) paged_attention_tc_kernel(const AttnPa
     }
     __syncwarp();  // P tile and K/V stage reads done before the next tile reuses them
     if (lane == 0) mbar_arrive(&hdr.empty[s]);
+    ++u;
+    }
   }
   __syncthreads();
   if (aborted || *reinterpret_cast<volatile int*>(&hdr.abort)) return;

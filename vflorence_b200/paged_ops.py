@@ -89,8 +89,11 @@ def get_isa(dtype: torch.dtype, block_size: int, head_dim: int) -> str:
 def get_scheduler_metadata(num_reqs: int, num_heads: int, num_kv_heads: int, head_dim: int,
                            seq_lens: torch.Tensor, dtype: torch.dtype,
                            query_start_loc: torch.Tensor | None, causal: bool, isa: str,
-                           block_size: int) -> torch.Tensor:
-    """Launch plan for ``attention_with_kv_cache``: a host int64 tensor holding the plan struct."""
+                           block_size: int, row_tables: bool = False) -> torch.Tensor:
+    """Launch plan for ``attention_with_kv_cache``: a host int64 tensor holding the plan struct.
+
+    ``row_tables``: every query row has its own block table (the beams of a request, grouped
+    by ``query_start_loc``, one length per request); bf16 with head_dim 64, not causal."""
     lens = _host_int32(seq_lens)
     if lens.numel() != num_reqs:
         raise ValueError(f"vflorence_b200: seq_lens has {lens.numel()} entries for {num_reqs} requests")
@@ -99,10 +102,20 @@ def get_scheduler_metadata(num_reqs: int, num_heads: int, num_kv_heads: int, hea
         raise ValueError("vflorence_b200: query_start_loc must have num_reqs + 1 entries")
     meta = torch.zeros(N.PLAN_BYTES // 8, dtype=torch.int64)
     plan = N.AttentionPlan.from_address(meta.data_ptr())
-    st = N.lib().vfl_plan_attention(int(num_reqs), int(num_heads), int(num_kv_heads), int(head_dim),
-                                    int(block_size), _dtype_code(dtype), int(bool(causal)),
-                                    lens.data_ptr() if num_reqs else None,
-                                    qsl.data_ptr() if qsl is not None else None, ctypes.byref(plan))
+    if row_tables:
+        if causal:
+            raise ValueError("vflorence_b200: row_tables plans are not causal")
+        if qsl is None:
+            raise ValueError("vflorence_b200: row_tables plans need query_start_loc")
+        st = N.lib().vfl_plan_attention_row_tables(int(num_reqs), int(num_heads), int(num_kv_heads), int(head_dim),
+                                                   int(block_size), _dtype_code(dtype),
+                                                   lens.data_ptr() if num_reqs else None, qsl.data_ptr(),
+                                                   ctypes.byref(plan))
+    else:
+        st = N.lib().vfl_plan_attention(int(num_reqs), int(num_heads), int(num_kv_heads), int(head_dim),
+                                        int(block_size), _dtype_code(dtype), int(bool(causal)),
+                                        lens.data_ptr() if num_reqs else None,
+                                        qsl.data_ptr() if qsl is not None else None, ctypes.byref(plan))
     N.check(st, "get_scheduler_metadata")
     return meta
 
@@ -177,8 +190,9 @@ def attention_with_kv_cache(query: torch.Tensor, k_cache: torch.Tensor, v_cache:
         raise ValueError("vflorence_b200: query_start_loc, seq_lens and block_table must be int32 "
                          "(block_table [num_reqs, cols] with unit column stride)")
     if seq_lens.numel() != plan.num_reqs or query_start_loc.numel() != plan.num_reqs + 1 \
-            or block_table.shape[0] < plan.num_reqs:
-        raise ValueError("vflorence_b200: metadata planned for a different number of requests")
+            or block_table.shape[0] < (plan.total_q if plan.row_tables else plan.num_reqs):
+        raise ValueError("vflorence_b200: metadata planned for a different number of requests "
+                         "(with row tables, block_table holds one row per query row)")
     ws = None
     if plan.workspace_bytes > 0:
         ws = torch.empty(plan.workspace_bytes, dtype=torch.uint8, device=dev)
