@@ -71,3 +71,26 @@ def test_engine_bf16_tokens_same_length(engine_trace, hf_model):
     assert [len(t) for t in tokens] == [len(t) for t in run["tokens"]]
     same = sum(a == b for t, u in zip(tokens, run["tokens"]) for a, b in zip(t, u))
     assert same >= 0.5 * sum(len(t) for t in tokens)
+
+
+@pytest.mark.parametrize("graphs", [False, True], ids=["eager", "cuda_graphs"])
+def test_grouped_beams_match_row_by_row(engine_trace, graphs):
+    """bf16 beam search with the beams of a request attending as one group (per-row block
+    tables) decides exactly as row-by-row attention: each row's tiles are reduced in the same
+    order, and a tile a row does not hold adds exact zeros."""
+    from vflorence_b200.engine import Engine, Request, SamplingParams
+    from vflorence_b200 import paged_ops
+
+    run = next(r for r in engine_trace["runs"] if r["name"] == "beam4")
+    cfg = run["config"]
+    model = _hf_model(engine_trace).to(torch.bfloat16)
+    results = []
+    for group in ("always", False):
+        eng = Engine(model, max_num_seqs=cfg["max_num_seqs"], max_decoder_len=cfg["max_decoder_len"],
+                     max_encoder_len=model.config.max_position_embeddings, block_size=16,
+                     num_blocks=run["num_blocks"], record_steps=True, cuda_graphs=graphs, group_beams=group)
+        tokens = eng.generate([Request(r) for r in run["requests"]], SamplingParams.from_dict(run["sampling"]))
+        results.append((tokens, eng.record))
+    assert results[0][0] == results[1][0]
+    assert results[0][1] == results[1][1]
+    assert paged_ops.read_device_errors(DEV) == 0

@@ -74,9 +74,12 @@ def decoder_self_attention(query: torch.Tensor, key: torch.Tensor, value: torch.
     out = torch.empty_like(query)
     # causal=False is still causal: each sequence queries only its newest token, and the cache
     # holds nothing after it.
-    paged_ops.attention_with_kv_cache(query, k_cache, v_cache, out, ctx.query_start_loc, ctx.context_lens,
-                                      scale=scale, causal=False, block_table=ctx.block_tables,
-                                      scheduler_metadata=ctx.self_metadata)
+    if ctx.self_groups is not None:  # the beams of a request share one CTA, each row its own table
+        qsl, lens = ctx.self_groups, ctx.self_group_lens
+    else:
+        qsl, lens = ctx.query_start_loc, ctx.context_lens
+    paged_ops.attention_with_kv_cache(query, k_cache, v_cache, out, qsl, lens, scale=scale, causal=False,
+                                      block_table=ctx.block_tables, scheduler_metadata=ctx.self_metadata)
     return out
 
 

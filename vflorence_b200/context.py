@@ -21,6 +21,10 @@ class Context:
     self_metadata: torch.Tensor | None = None    # host plan (paged_ops.get_scheduler_metadata)
     isa: str | None = None
     cross_staged: list | None = None             # per layer: (k, v, table, lens, metadata, qsl)
+    # beam search: runs of consecutive rows at one position (the beams of a request) attend as
+    # one group with per-row block tables (self_metadata is then a row-tables plan)
+    self_groups: torch.Tensor | None = None      # int32 [G + 1], device: row offsets of the groups
+    self_group_lens: torch.Tensor | None = None  # int32 [G], device: each group's context length
 
 
 _CONTEXT: Context | None = None

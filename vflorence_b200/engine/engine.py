@@ -52,8 +52,12 @@ class _Req:
 class Engine:
     def __init__(self, hf_model, *, max_num_seqs: int, max_decoder_len: int, max_encoder_len: int,
                  block_size: int = 16, num_blocks: int | None = None, decoder_start_token_id: int | None = None,
-                 record_steps: bool = False, cuda_graphs: bool = False):
+                 record_steps: bool = False, cuda_graphs: bool = False, group_beams: bool | str = True):
         self.model = PagedSeq2Seq(hf_model)
+        # beam search: one attention group per request with per-row block tables (bf16, head_dim
+        # 64) where enough requests keep the GPU busy ("always": whatever the batch); False
+        # attends row by row (the same results, for comparisons)
+        self.group_beams = group_beams
         m = self.model
         self.device, self.dtype = m.device, m.dtype
         self.block_size = block_size
@@ -174,9 +178,14 @@ class Engine:
         else:
             st = self.kv.prepare_decode_host(self._eager_host[: n * W + n], n, W)
             staged = self.kv.stage_cross(self.model.layers, rows.request_ids.tolist())
+            self_kw = dict(self_metadata=st.self_metadata)
+            if (params.num_beams > 1 and self.group_beams and paged_ops.row_tables_supported(self.dtype,
+                                                                                           self.model.head_dim)
+                    and (self.group_beams == "always"
+                         or paged_ops.row_tables_pay_off(rows.num_groups, self.model.num_heads))):
+                self_kw = self._beam_groups(rows)
             set_context(context_lens=st.context_lens, block_tables=st.block_tables, slot_mapping=st.slot_mapping,
-                        query_start_loc=st.query_start_loc, self_metadata=st.self_metadata, isa=self.kv.isa,
-                        cross_staged=staged)
+                        query_start_loc=st.query_start_loc, isa=self.kv.isa, cross_staged=staged, **self_kw)
             try:
                 ids = torch.from_numpy(rows.tokens).to(self.device, non_blocking=True)
                 logits = self.model.decode(ids.long(), st.positions.long())
@@ -239,6 +248,20 @@ class Engine:
             for layer in range(len(self.model.layers)):
                 k, v = self.model.cross_kv(layer, hidden)
                 self.kv.write_encoder_kv(layer, k, v, slots)
+
+    def _beam_groups(self, rows: StepRows) -> dict:
+        """Self-attention groups of an eager beam step: runs of consecutive rows of one request
+        (the same position), a row-tables plan, one upload of the groups' offsets and lengths."""
+        rid = rows.request_ids
+        starts = np.flatnonzero(np.r_[True, rid[1:] != rid[:-1]])
+        qsl = np.r_[starts, rows.n].astype(np.int32)
+        lens = (rows.positions[starts] + 1).astype(np.int32)
+        m = self.model
+        meta = paged_ops.get_scheduler_metadata(len(starts), m.num_heads, m.num_heads, m.head_dim,
+                                                torch.from_numpy(lens), self.dtype, torch.from_numpy(qsl), False,
+                                                self.kv.isa, self.block_size, row_tables=True)
+        dev = torch.from_numpy(np.r_[qsl, lens]).to(self.device)
+        return dict(self_metadata=meta, self_groups=dev[: len(qsl)], self_group_lens=dev[len(qsl):])
 
     def _rules_for(self, params: SamplingParams) -> tuple[LogitsRules, DecodeRules]:
         if self._rules is None or self._rules[0] is not params:

@@ -25,7 +25,7 @@ import torch
 
 from .. import paged_ops
 from ..attention import group_rows
-from ..context import set_context
+from ..context import get_context, set_context
 
 BUCKETS = (1, 2, 4, 8, 16, 24, 32, 48, 64, 96, 128, 160, 192, 224, 256, 320, 384, 448, 512)
 
@@ -58,9 +58,14 @@ class _StepGraph:
         self.cross_key = None
         self.copy_done = torch.cuda.Event()
         H, D = m.num_heads, m.head_dim
-        self.meta_self = paged_ops.get_scheduler_metadata(
-            B, H, H, D, torch.full((B,), e.max_decoder_len, dtype=torch.int32), e.dtype, None, False, kv.isa, bs)
         plan_qsl = torch.tensor([min(r * beams, B) for r in range(B + 1)], dtype=torch.int32)
+        # beam search: the beams of a request (the cross-staging groups) attend as one group with
+        # per-row block tables; the groups' lengths are gathered from the rows' in the graph
+        self.grouped = (beams > 1 and e.group_beams and paged_ops.row_tables_supported(e.dtype, D)
+                        and (e.group_beams == "always" or paged_ops.row_tables_pay_off(math.ceil(B / beams), H)))
+        self.meta_self = paged_ops.get_scheduler_metadata(
+            B, H, H, D, torch.full((B,), e.max_decoder_len, dtype=torch.int32), e.dtype,
+            plan_qsl if self.grouped else None, False, kv.isa, bs, row_tables=self.grouped)
         self.meta_cross = paged_ops.get_scheduler_metadata(
             B, H, H, D, torch.full((B,), e.max_encoder_len, dtype=torch.int32), e.dtype, plan_qsl, False,
             kv.isa, bs)
@@ -92,6 +97,11 @@ class _StepGraph:
 
     def _forward(self):
         paged_ops.prepare_decode(self.tables, self.pos, self.e.block_size, self.slots, self.ctx_lens, self.qsl)
+        if self.grouped:
+            ctx = get_context()
+            ctx.self_groups = self.cqsl
+            # a group's length is its first row's; groups without rows read any row
+            ctx.self_group_lens = self.ctx_lens.index_select(0, self.cqsl[:-1].clamp(max=self.rows - 1))
         return self.e.model.decode(self.ids.long(), self.pos.long())
 
     def host_views(self):
