@@ -195,6 +195,21 @@ int vfl_prepare_decode(const int32_t* block_table, int64_t table_stride, int32_t
                        int64_t* slot_mapping, int32_t* context_lens, int32_t* query_start_loc,
                        void* stream);
 
+/* replaces the encoder K/V projection and page write of ModelRunner._encode
+ *   (vflorence/engine/model_runner.py:248-259: per layer kv_proj, then reshape_and_cache) with
+ *   one tensor-core launch per layer: kv = hidden . w_kv^T (+ bias) with fp32 accumulation,
+ *   token t's k half written to k_cache[slot // block_size, h, slot % block_size, :] and its v
+ *   half to v_cache likewise (slot = slot_mapping[t]; negative slots skipped, slots past the pool
+ *   flagged with VFL_DEVERR_SLOT). bf16 only. hidden: [num_tokens, hidden_dim] with rows
+ *   hidden_stride elements apart; w_kv: [2 * num_heads * head_dim, hidden_dim] row-major (a
+ *   torch.nn.Linear weight holding the k rows, then the v rows); bias: [2 * num_heads *
+ *   head_dim] or NULL. hidden_dim a multiple of 64, head_dim of 32, 2 * num_heads * head_dim
+ *   of 128 (VFL_ERR_UNSUPPORTED otherwise); 16-byte aligned pointers and row stride. */
+int vfl_kv_proj_paged(const void* hidden, int64_t hidden_stride, const void* w_kv, const void* bias,
+                      void* k_cache, void* v_cache, const int64_t* slot_mapping, int64_t num_tokens,
+                      int32_t hidden_dim, int32_t num_heads, int32_t head_dim, int32_t block_size,
+                      int64_t num_blocks, void* stream);
+
 /* replaces the encoder slot computation of ModelRunner._encode
  *   (vflorence/engine/model_runner.py:240-242): for request g and token t < seq_len,
  *   slot_mapping[g * seq_len + t] = pages[g, t // block_size] * block_size + t % block_size. */

@@ -49,6 +49,7 @@ EXPORTS = (
     "vfl_attention_with_kv_cache_no_alloc",
     "vfl_copy_blocks",
     "vfl_prepare_decode",
+    "vfl_kv_proj_paged",
     "vfl_paged_slots",
     "vfl_row_topk",
     "vfl_row_topk_workspace_size",
@@ -167,6 +168,7 @@ def _declare(L):
         "vfl_copy_blocks": (i32, [vp, vp, i32, vp, i32, i64, i64, vp]),
         "vfl_prepare_decode": (i32, [vp, i64, i32, vp, i32, i32, vp, vp, vp, vp]),
         "vfl_paged_slots": (i32, [vp, i64, i32, i32, i32, i32, vp, vp]),
+        "vfl_kv_proj_paged": (i32, [vp, i64, vp, vp, vp, vp, vp, i64, i32, i32, i32, i32, i64, vp]),
         "vfl_row_topk": (i32, [vp, i32, i64, i64, i64, i32, vp, i32, vp, vp, vp, sz, vp]),
         "vfl_row_topk_workspace_size": (sz, [i64, i64, i32]),
         "vfl_beam_merge": (i32, [vp, vp, i64, i32, vp, vp, i32, i32, vp, vp]),

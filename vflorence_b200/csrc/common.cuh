@@ -2,6 +2,7 @@
 // few PTX forms the kernels use (mbarrier, bulk global->shared copies, bounded waits).
 #pragma once
 
+#include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
@@ -20,6 +21,9 @@ int fail(int status, const char* fmt, ...);
 int cuda_status(cudaError_t e, const char* what);
 // Device address of the current device's error word (set up once per device).
 int device_error_word(unsigned int** out);
+// A row-major bf16 matrix as a 2-D TMA tensor map (128-byte swizzle, zero fill outside).
+int make_tensor_map_2d_bf16(const void* base, uint64_t inner, uint64_t outer, uint64_t row_bytes, uint32_t box_inner,
+                            uint32_t box_outer, CUtensorMap* out);
 // Re-checks every field of a caller-provided attention plan that the kernels rely on.
 int check_attention_plan(const vfl_attention_plan* plan);
 // Raises the dynamic shared-memory limit of `func` once per device.

@@ -87,6 +87,24 @@ int pool_tensor_map(const void* base, uint64_t rows, uint32_t box_rows, CUtensor
 
 }  // namespace
 
+// A row-major bf16 matrix [outer rows, inner columns] (rows `row_bytes` apart) as a 2-D tensor
+// map with the 128-byte swizzle, box inner x outer; reads outside the matrix fill zeros.
+int make_tensor_map_2d_bf16(const void* base, uint64_t inner, uint64_t outer, uint64_t row_bytes, uint32_t box_inner,
+                            uint32_t box_outer, CUtensorMap* out) {
+  EncodeTiledFn fn = nullptr;
+  int st = encode_fn(&fn);
+  if (st) return st;
+  const cuuint64_t dims[2] = {inner, outer};
+  const cuuint64_t strides[1] = {row_bytes};
+  const cuuint32_t box[2] = {box_inner, box_outer};
+  const cuuint32_t elem_strides[2] = {1, 1};
+  const CUresult r = fn(out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+                        elem_strides, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(VFL_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return VFL_OK;
+}
+
 // A plan is caller memory: every constraint the kernels rely on (shared-memory table slice,
 // stage ring, CTA shape, workspace size) is re-derived here before anything touches the device.
 int check_attention_plan(const vfl_attention_plan* plan) {

@@ -316,6 +316,43 @@ def prepare_decode(block_table: torch.Tensor, positions: torch.Tensor, block_siz
     N.check(st, "prepare_decode")
 
 
+def kv_proj_supported(dtype: torch.dtype, hidden_dim: int, num_heads: int, head_dim: int) -> bool:
+    """Whether the fused projection + page write is built for this shape (bf16 tensor cores)."""
+    return (dtype == torch.bfloat16 and hidden_dim % 64 == 0 and head_dim % 32 == 0
+            and (2 * num_heads * head_dim) % 128 == 0)
+
+
+def kv_proj_paged(hidden: torch.Tensor, w_kv: torch.Tensor, bias: torch.Tensor | None, k_cache: torch.Tensor,
+                  v_cache: torch.Tensor, slot_mapping: torch.Tensor) -> None:
+    """``kv = hidden @ w_kv.T (+ bias)`` written straight into the paged caches: row t's first
+    half (k) and second half (v), split into heads, go to ``slot_mapping[t]`` (negative: skip).
+    hidden [T, hidden_dim] bf16 (unit column stride), w_kv [2 * H * D, hidden_dim] contiguous,
+    caches [num_blocks, H, block_size, D] bf16, slot_mapping int64 [T]."""
+    dev = k_cache.device
+    for name, t in (("hidden", hidden), ("w_kv", w_kv), ("k_cache", k_cache), ("v_cache", v_cache),
+                    ("slot_mapping", slot_mapping)):
+        _require_cuda(name, t, dev)
+    n, h, bs, d = k_cache.shape
+    if (hidden.dtype != torch.bfloat16 or w_kv.dtype != torch.bfloat16 or k_cache.dtype != torch.bfloat16
+            or v_cache.shape != k_cache.shape or v_cache.dtype != k_cache.dtype):
+        raise ValueError("vflorence_b200: kv_proj_paged is built for bfloat16")
+    if hidden.dim() != 2 or hidden.stride(1) != 1 or not w_kv.is_contiguous() or w_kv.shape != (2 * h * d, hidden.shape[1]):
+        raise ValueError("vflorence_b200: kv_proj_paged wants hidden [T, K] (unit column stride) and w_kv [2*H*D, K]")
+    if not (k_cache.is_contiguous() and v_cache.is_contiguous()):
+        raise ValueError("vflorence_b200: caches must be contiguous")
+    if bias is not None:
+        _require_cuda("bias", bias, dev)
+        if bias.dtype != torch.bfloat16 or bias.numel() != 2 * h * d or not bias.is_contiguous():
+            raise ValueError("vflorence_b200: kv_proj_paged bias must be contiguous bf16 [2*H*D]")
+    if slot_mapping.dtype != torch.int64 or slot_mapping.numel() < hidden.shape[0] or not slot_mapping.is_contiguous():
+        raise ValueError("vflorence_b200: slot_mapping must be contiguous int64 [T]")
+    st = N.lib().vfl_kv_proj_paged(hidden.data_ptr(), hidden.stride(0), w_kv.data_ptr(),
+                                   None if bias is None else bias.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
+                                   slot_mapping.data_ptr(), hidden.shape[0], hidden.shape[1], h, d, bs, n,
+                                   _stream(dev))
+    N.check(st, "kv_proj_paged")
+
+
 def paged_slots(pages: torch.Tensor, seq_len: int, block_size: int) -> torch.Tensor:
     """Slots of ``seq_len`` tokens for each row of ``pages`` [G, M] (int64 [G * seq_len])."""
     _require_cuda("pages", pages)
