@@ -2,8 +2,9 @@
 PyTorch fp32 reference of the same op: kv = hidden @ w_kv.T + bias, rounded to bf16, scattered
 by slot into [num_blocks, H, block_size, D] pools (vflorence/engine/model_runner.py:248-259).
 
-Tolerance: bf16 (2e-2 absolute on values of unit scale); in practice all but a few entries at a
-rounding boundary are bit-equal."""
+Tolerance: bf16, 2e-2 absolute plus one bf16 step (2^-7 relative) - both sides round the same
+fp32 value after sums in different orders, so an entry at a rounding boundary may differ by one
+step; at least 99 % of entries must be bit-equal."""
 
 from __future__ import annotations
 
@@ -49,6 +50,8 @@ def _reference(hidden, w, bias, kc, vc, slots):
     (1000, 768, 12, 64, 16, True),     # Florence-2-base
     (128, 1024, 16, 64, 32, False),    # one full tile, block 32, no bias
     (77, 64, 2, 32, 16, True),         # one K step, head_dim 32
+    (5000, 1024, 16, 64, 16, True),    # enough tokens for 256-feature tiles
+    (4500, 768, 12, 64, 16, False),    # 256-feature tiles over 1536 features
 ])
 def test_kv_proj_paged_matches_fp32_reference(tokens, hidden_dim, heads, head_dim, block_size, with_bias):
     from vflorence_b200 import paged_ops as ops
@@ -61,7 +64,8 @@ def test_kv_proj_paged_matches_fp32_reference(tokens, hidden_dim, heads, head_di
     assert ops.read_device_errors(DEV) == 0
     for got, want, name in ((kc, ek, "k"), (vc, ev, "v")):
         diff = (got.float() - want.float()).abs()
-        assert float(diff.max()) <= 2e-2, f"{name}: max |diff| {float(diff.max())}"
+        bound = 2e-2 + want.float().abs() * 2.0 ** -7
+        assert bool((diff <= bound).all()), f"{name}: max |diff| {float(diff.max())}"
         assert float((diff == 0).float().mean()) >= 0.99, f"{name}: too few bit-equal entries"
 
 
@@ -76,8 +80,8 @@ def test_kv_proj_paged_equals_gemm_then_append():
     k, v = kv.chunk(2, dim=-1)
     ops.reshape_and_cache(k.reshape(-1, 16, 64), v.reshape(-1, 16, 64), kc2, vc2, slots)
     torch.cuda.synchronize()
-    assert float((kc.float() - kc2.float()).abs().max()) <= 2e-2
-    assert float((vc.float() - vc2.float()).abs().max()) <= 2e-2
+    for got, want in ((kc, kc2), (vc, vc2)):
+        assert bool(((got.float() - want.float()).abs() <= 2e-2 + want.float().abs() * 2.0 ** -7).all())
 
 
 def test_kv_proj_paged_flags_slots_past_the_pool():
@@ -90,8 +94,8 @@ def test_kv_proj_paged_flags_slots_past_the_pool():
     ek, ev = _reference(hidden, w, bias, before_k, before_v, torch.where(slots == slots[5], -1, slots))
     ops.kv_proj_paged(hidden, w, bias, kc, vc, slots)
     assert ops.read_device_errors(DEV) & _native.DEVERR_SLOT
-    assert float((kc.float() - ek.float()).abs().max()) <= 2e-2
-    assert float((vc.float() - ev.float()).abs().max()) <= 2e-2
+    for got, want in ((kc, ek), (vc, ev)):
+        assert bool(((got.float() - want.float()).abs() <= 2e-2 + want.float().abs() * 2.0 ** -7).all())
 
 
 def test_kv_proj_paged_rejects_unbuilt_shapes():

@@ -5,31 +5,44 @@
 //   slot_mapping[t] - the encoder half of ModelRunner._encode (vflorence/engine/model_runner.py:
 //   248-259), which runs a GEMM per layer and then reshape_and_cache.
 //
-// One CTA (4 warps) computes one 128 x 128 tile of kv:
-//   * warp 0, one thread: TMA loads of 128 x 64 tiles of hidden and w_kv (128-byte swizzle) into a
-//     3-stage shared-memory ring paced by full / empty mbarriers;
-//   * warp 1, one thread: per stage four tcgen05.mma (M 128, N 128, K 16, bf16 in, fp32 out)
-//     into a 128-column TMEM accumulator, then tcgen05.commit to the stage's empty barrier, and
-//     after the last stage to the accumulator barrier;
-//   * all 4 warps: the epilogue - warp w reads TMEM lanes 32w..32w+31 (its tile rows) with
-//     tcgen05.ld, adds the bias, rounds to bf16 and writes each token's 32-dim head slices
-//     straight into its page (64 contiguous bytes per store group).
-// Every wait is bounded (VFL_DEVERR_TIMEOUT); a CTA that gave up waits (bounded) for its copies
-// and its MMAs, frees its TMEM and returns. Bad slots set VFL_DEVERR_SLOT and are skipped.
+// A persistent, warp-specialised kernel: one CTA per SM walks 128 x BN output tiles (BN = 256
+// features where the feature count allows, else 128; features fastest, so consecutive tiles
+// reuse the same hidden rows from L2).
+//   * warp 4, one thread: TMA loads of 128 x 64 tiles of hidden and w_kv (128-byte swizzle) into
+//     a 4-stage shared-memory ring paced by full / empty mbarriers, running ahead across tiles;
+//   * warp 5: allocates 2 x BN TMEM columns (two fp32 accumulators); one thread issues, per
+//     stage, four tcgen05.mma (M 128, N BN, K 16, bf16 in, fp32 out) and tcgen05.commit to
+//     the stage's empty barrier, and after a tile's last stage to the accumulator's full barrier;
+//   * warps 0-3: the epilogue of tile i (tcgen05.ld of TMEM lanes 32w..32w+31 = the tile's
+//     rows, bias, bf16, each token's 32-dim head slices stored straight into its page) while the
+//     tensor cores already accumulate tile i+1 into the other accumulator.
+// Every wait is bounded (VFL_DEVERR_TIMEOUT): a CTA that gave up stops issuing, waits (bounded)
+// for its copies and its MMAs, frees its TMEM and returns. Bad slots set VFL_DEVERR_SLOT.
 #include "common.cuh"
 
 namespace vfl {
 namespace {
 
-constexpr int kBM = 128, kBN = 128, kBK = 64, kStages = 3;
-constexpr int kTileBytes = kBM * kBK * 2;  // 16 KiB (A and B tiles alike)
-constexpr int kTmemCols = 128;
-constexpr int kSmemBytes = 1024 /* alignment slack */ + kStages * 2 * kTileBytes + 256 /* barriers */;
+constexpr int kBM = 128, kBK = 64, kStages = 4;
+constexpr int kTileA = kBM * kBK * 2;                  // 16 KiB
+constexpr int kEpilogueWarps = 4;
+constexpr int kThreads = (kEpilogueWarps + 2) * 32;   // + producer warp + MMA warp
+constexpr int kProducerWarp = 4, kMmaWarp = 5;
 
-// tcgen05 instruction descriptor, kind::f16: f32 accumulator, bf16 A and B, both K-major,
-// N = 128 (bits 17-22: N >> 3), M = 128 (bits 24-28: M >> 4)
-constexpr uint32_t kInstrDesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kBN >> 3) << 17) |
-                                ((uint32_t)(kBM >> 4) << 24);
+// Tile width BN (output features): 256 where the feature count allows (a third less L2 traffic
+// per flop than 128), else 128.
+template <int BN>
+struct KvTile {
+  static constexpr int kTileB = BN * kBK * 2;
+  static constexpr int kStageBytes = kTileA + kTileB;
+  static constexpr int kAccCols = BN;          // one fp32 accumulator: BN TMEM columns
+  static constexpr int kTmemCols = 2 * BN;     // double-buffered
+  static constexpr int kSmemBytes = 1024 /* alignment slack */ + kStages * kStageBytes + 256 /* barriers */;
+  // tcgen05 instruction descriptor, kind::f16: f32 accumulator, bf16 A and B, both K-major,
+  // N = BN (bits 17-22: N >> 3), M = 128 (bits 24-28: M >> 4)
+  static constexpr uint32_t kInstrDesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
+                                         ((uint32_t)(kBM >> 4) << 24);
+};
 
 // Shared-memory matrix descriptor of a K-major tile with the 128-byte swizzle: rows of 128 bytes,
 // 8-row atoms 1024 bytes apart (SBO), leading offset field 1, descriptor version 1, layout 2.
@@ -46,12 +59,13 @@ __device__ __forceinline__ void tma_load_tile(uint32_t dst, const CUtensorMap* m
       : "memory");
 }
 
-__device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t accumulate) {
+__device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc,
+                                          uint32_t accumulate) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-      "l"(da), "l"(db), "r"(kInstrDesc), "r"(accumulate)
+      "l"(da), "l"(db), "r"(idesc), "r"(accumulate)
       : "memory");
 }
 
@@ -83,149 +97,214 @@ struct KvProjParams {
   int32_t heads;
   int32_t head_dim;   // a multiple of 32
   int32_t block_size;
+  int32_t n_tiles;    // output feature tiles (2 * H * D / 128)
+  int32_t tiles;      // n_tiles x token tiles
   unsigned int* err;
 };
 
-__global__ void __launch_bounds__(128, 1) kv_proj_paged_kernel(const __grid_constant__ CUtensorMap amap,
-                                                               const __grid_constant__ CUtensorMap bmap,
-                                                               const KvProjParams p) {
+struct KvSmem {  // after the stage ring
+  uint64_t full[kStages], empty[kStages];
+  uint64_t acc_full[2], acc_empty[2];
+  uint64_t mma_done;
+  uint32_t tmem;
+  int abort;
+  int issued, consumed;  // k-block loads issued by the producer / consumed by the MMA thread
+};
+
+__device__ __forceinline__ bool aborted(const KvSmem& sh) { return *reinterpret_cast<const volatile int*>(&sh.abort); }
+
+__device__ __forceinline__ void give_up(KvSmem& sh, unsigned int* err) {
+  report(err, VFL_DEVERR_TIMEOUT);
+  *reinterpret_cast<volatile int*>(&sh.abort) = 1;
+}
+
+template <int BN>
+__global__ void __launch_bounds__(kThreads, 1) kv_proj_paged_kernel(const __grid_constant__ CUtensorMap amap,
+                                                                   const __grid_constant__ CUtensorMap bmap,
+                                                                   const KvProjParams p) {
+  using Tile = KvTile<BN>;
+  constexpr int kBN = BN, kStageBytes = Tile::kStageBytes, kAccCols = Tile::kAccCols, kTmemCols = Tile::kTmemCols;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const uint32_t a_base = smem_u32(smem);
-  const uint32_t b_base = a_base + kStages * kTileBytes;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + 2 * kStages * kTileBytes);
-  uint64_t* empty = full + kStages;
-  uint64_t* acc_full = empty + kStages;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
-  int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
-  int* issued_slot = abort_flag + 1;
-  int* consumed_slot = issued_slot + 1;
-
+  const uint32_t ring = smem_u32(smem);  // stage s: A tile at ring + s * kStageBytes, B tile after it
+  KvSmem& sh = *reinterpret_cast<KvSmem*>(smem + kStages * kStageBytes);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n0 = blockIdx.x * kBN;
-  const int64_t m0 = (int64_t)blockIdx.y * kBM;
   const int num_kb = p.k_dim / kBK;
 
-  if (warp == 0) {  // TMEM: one warp allocates for the CTA
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+  if (warp == kMmaWarp) {  // TMEM: one warp allocates for the CTA
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&sh.tmem)),
                  "r"(kTmemCols)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
-  if (threadIdx.x == 32) {
+  if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
+      mbar_init(&sh.full[s], 1);
+      mbar_init(&sh.empty[s], 1);
     }
-    mbar_init(acc_full, 1);
-    *abort_flag = 0;
-    *issued_slot = 0;
-    *consumed_slot = 0;
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&sh.acc_full[b], 1);
+      mbar_init(&sh.acc_empty[b], kEpilogueWarps);
+    }
+    mbar_init(&sh.mma_done, 1);
+    sh.abort = 0;
+    sh.issued = sh.consumed = 0;
     fence_barrier_init();
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-  const uint32_t tmem = *tmem_slot;
+  const uint32_t tmem = sh.tmem;
 
-  if (warp == 0 && lane == 0) {
-    // ---- producer: TMA tiles of hidden (rows m0..) and w_kv (rows n0..), K step 64
-    for (int kb = 0; kb < num_kb; ++kb) {
-      const int s = kb % kStages;
-      if (kb >= kStages && !mbar_wait_bounded(&empty[s], ((kb / kStages) - 1) & 1)) {
-        report(p.err, VFL_DEVERR_TIMEOUT);
-        *reinterpret_cast<volatile int*>(abort_flag) = 1;
-        break;
-      }
-      if (*reinterpret_cast<volatile int*>(abort_flag)) break;
-      mbar_arrive_expect_tx(&full[s], 2u * kTileBytes);
-      tma_load_tile(a_base + s * kTileBytes, &amap, kb * kBK, (int)m0, &full[s]);
-      tma_load_tile(b_base + s * kTileBytes, &bmap, kb * kBK, n0, &full[s]);
-      *reinterpret_cast<volatile int*>(issued_slot) = kb + 1;
-    }
-  } else if (warp == 1 && lane == 0) {
-    // ---- MMA issuer: four K-16 steps per stage (the descriptor start moves 32 bytes a step)
-    for (int kb = 0; kb < num_kb; ++kb) {
-      const int s = kb % kStages;
-      if (!mbar_wait_bounded(&full[s], (kb / kStages) & 1)) {
-        report(p.err, VFL_DEVERR_TIMEOUT);
-        *reinterpret_cast<volatile int*>(abort_flag) = 1;
-        break;
-      }
-      *reinterpret_cast<volatile int*>(consumed_slot) = kb + 1;
-      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      const uint32_t a = a_base + s * kTileBytes, b = b_base + s * kTileBytes;
-#pragma unroll
-      for (int k = 0; k < kBK / 16; ++k)
-        umma_bf16(tmem, smem_desc(a + k * 32), smem_desc(b + k * 32), (kb | k) != 0 ? 1u : 0u);
-      umma_commit(&empty[s]);  // the stage is free once these MMAs have read it
-    }
-    umma_commit(acc_full);  // arrives when every MMA issued above has completed
-  }
-  __syncwarp();
-
-  // ---- epilogue: TMEM -> registers -> bias, bf16 -> pages
-  const bool acc_ok = mbar_wait_bounded(acc_full, 0);
-  if (!acc_ok) report(p.err, VFL_DEVERR_TIMEOUT);
-  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-  const bool aborted = *reinterpret_cast<volatile int*>(abort_flag) != 0;
-  const int row = warp * 32 + lane;
-  const int64_t t = m0 + row;
-  int64_t slot = -1;
-  if (t < p.num_tokens) {
-    slot = __ldg(p.slots + t);
-    if (slot >= p.num_blocks * p.block_size) {
-      report(p.err, VFL_DEVERR_SLOT);
-      slot = -1;
-    }
-  }
-  const int hd = p.heads * p.head_dim;
-  if (acc_ok && !aborted) {
-#pragma unroll 1
-    for (int c0 = 0; c0 < kBN; c0 += 32) {
-      uint32_t r[32];
-      tmem_ld_32cols(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0, r);  // every lane takes part
-      const int f = n0 + c0;  // first feature of the chunk; a chunk lies in one head of k or v
-      if (slot < 0 || f >= 2 * hd) continue;
-      const bool is_v = f >= hd;
-      const int within = is_v ? f - hd : f;
-      const int h = within / p.head_dim, d0 = within - h * p.head_dim;
-      const int64_t blk = slot / p.block_size, off = slot - blk * p.block_size;
-      __nv_bfloat16* dst = (is_v ? p.v_cache : p.k_cache) +
-                           (((blk * p.heads + h) * p.block_size + off) * p.head_dim + d0);
-      uint32_t packed[16];
-#pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        float lo = __uint_as_float(r[2 * j]), hi = __uint_as_float(r[2 * j + 1]);
-        if (p.bias != nullptr) {
-          lo += __bfloat162float(p.bias[f + 2 * j]);
-          hi += __bfloat162float(p.bias[f + 2 * j + 1]);
+  if (warp == kProducerWarp) {
+    if (lane == 0) {
+      int q = 0;  // k-block loads across this CTA's tiles
+      for (int tile = blockIdx.x; tile < p.tiles && !aborted(sh); tile += gridDim.x) {
+        const int n0 = (tile % p.n_tiles) * kBN;
+        const int m0 = (tile / p.n_tiles) * kBM;
+        for (int kb = 0; kb < num_kb; ++kb, ++q) {
+          const int s = q % kStages;
+          if (q >= kStages && !mbar_wait_bounded(&sh.empty[s], ((q / kStages) - 1) & 1)) {
+            give_up(sh, p.err);
+            break;
+          }
+          if (aborted(sh)) break;
+          mbar_arrive_expect_tx(&sh.full[s], (uint32_t)kStageBytes);
+          const uint32_t a = ring + s * kStageBytes;
+          tma_load_tile(a, &amap, kb * kBK, m0, &sh.full[s]);
+          tma_load_tile(a + kTileA, &bmap, kb * kBK, n0, &sh.full[s]);
+          *reinterpret_cast<volatile int*>(&sh.issued) = q + 1;
         }
-        packed[j] = (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(lo)) |
-                    ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(hi)) << 16);
       }
-      uint4* d4 = reinterpret_cast<uint4*>(dst);
+    }
+  } else if (warp == kMmaWarp) {
+    if (lane == 0) {
+      int q = 0, i = 0;  // k-blocks consumed, tiles accumulated
+      for (int tile = blockIdx.x; tile < p.tiles && !aborted(sh); tile += gridDim.x, ++i) {
+        const int b = i & 1;
+        // the epilogue must have emptied this accumulator (used two tiles ago)
+        if (i >= 2 && !mbar_wait_bounded(&sh.acc_empty[b], ((i >> 1) - 1) & 1)) {
+          give_up(sh, p.err);
+          break;
+        }
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t acc = tmem + (uint32_t)(b * kAccCols);
+        bool ok = true;
+        for (int kb = 0; kb < num_kb; ++kb, ++q) {
+          const int s = q % kStages;
+          if (!mbar_wait_bounded(&sh.full[s], (q / kStages) & 1)) {
+            give_up(sh, p.err);
+            ok = false;
+            break;
+          }
+          *reinterpret_cast<volatile int*>(&sh.consumed) = q + 1;
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          const uint32_t a = ring + s * kStageBytes, bt = a + kTileA;
 #pragma unroll
-      for (int q = 0; q < 4; ++q)
-        d4[q] = make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
+          for (int k = 0; k < kBK / 16; ++k)
+            umma_bf16(acc, smem_desc(a + k * 32), smem_desc(bt + k * 32), Tile::kInstrDesc, (kb | k) != 0 ? 1u : 0u);
+          umma_commit(&sh.empty[s]);  // the stage is free once these MMAs have read it
+        }
+        if (!ok) break;
+        umma_commit(&sh.acc_full[b]);  // the tile's accumulator is complete
+      }
+      umma_commit(&sh.mma_done);  // arrives once every MMA issued above has completed
+    }
+  } else {
+    // ---- epilogue warps 0-3: TMEM lanes 32w..32w+31 are rows 32w..32w+31 of the tile
+    const int hd = p.heads * p.head_dim;
+    int i = 0;
+    for (int tile = blockIdx.x; tile < p.tiles; tile += gridDim.x, ++i) {
+      const int b = i & 1;
+      if (!mbar_wait_bounded(&sh.acc_full[b], (i >> 1) & 1)) {
+        give_up(sh, p.err);
+        break;
+      }
+      if (aborted(sh)) break;
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const int n0 = (tile % p.n_tiles) * kBN;
+      const int64_t t = (int64_t)(tile / p.n_tiles) * kBM + warp * 32 + lane;
+      int64_t slot = -1;
+      if (t < p.num_tokens) {
+        slot = __ldg(p.slots + t);
+        if (slot >= p.num_blocks * p.block_size) {
+          report(p.err, VFL_DEVERR_SLOT);
+          slot = -1;
+        }
+      }
+      const uint32_t acc = tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(b * kAccCols);
+#pragma unroll 1
+      for (int c0 = 0; c0 < kBN; c0 += 32) {
+        uint32_t r[32];
+        tmem_ld_32cols(acc + (uint32_t)c0, r);  // every lane takes part
+        const int f = n0 + c0;  // first feature of the chunk; a chunk lies in one head of k or v
+        if (slot < 0) continue;
+        const bool is_v = f >= hd;
+        const int within = is_v ? f - hd : f;
+        const int h = within / p.head_dim, d0 = within - h * p.head_dim;
+        const int64_t blk = slot / p.block_size, off = slot - blk * p.block_size;
+        __nv_bfloat16* dst =
+            (is_v ? p.v_cache : p.k_cache) + (((blk * p.heads + h) * p.block_size + off) * p.head_dim + d0);
+        uint32_t packed[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          float lo = __uint_as_float(r[2 * j]), hi = __uint_as_float(r[2 * j + 1]);
+          if (p.bias != nullptr) {
+            lo += __bfloat162float(p.bias[f + 2 * j]);
+            hi += __bfloat162float(p.bias[f + 2 * j + 1]);
+          }
+          packed[j] = (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(lo)) |
+                      ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(hi)) << 16);
+        }
+        uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+        for (int qq = 0; qq < 4; ++qq)
+          d4[qq] = make_uint4(packed[4 * qq], packed[4 * qq + 1], packed[4 * qq + 2], packed[4 * qq + 3]);
+      }
+      // this warp has its rows in registers: the accumulator may take the tile after next
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sh.acc_empty[b]);
     }
   }
-  if (threadIdx.x == 0 && (aborted || !acc_ok)) {
-    // copies issued but never consumed may still land in this CTA's shared memory: wait for
-    // them (bounded) before the CTA exits
-    const int issued = *reinterpret_cast<volatile int*>(issued_slot);
-    for (int kb = *reinterpret_cast<volatile int*>(consumed_slot); kb < issued; ++kb)
-      mbar_wait_bounded(&full[kb % kStages], (kb / kStages) & 1);
-  }
+
+  // ---- teardown: every issued MMA done, every issued copy landed, then TMEM freed
+  __syncwarp();
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
-  if (warp == 0) {
+  if (threadIdx.x == 0) {
+    if (!mbar_wait_bounded(&sh.mma_done, 0)) report(p.err, VFL_DEVERR_TIMEOUT);
+    const int issued = *reinterpret_cast<volatile int*>(&sh.issued);
+    for (int q = *reinterpret_cast<volatile int*>(&sh.consumed); q < issued; ++q)
+      mbar_wait_bounded(&sh.full[q % kStages], (q / kStages) & 1);
+  }
+  __syncthreads();
+  if (warp == kMmaWarp) {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
   }
 }
 
-int g_smem_done[kMaxDevices];
+int g_smem_done[2][kMaxDevices];
+
+template <int BN>
+int launch_kv_proj(const void* hidden, int64_t hidden_stride, const void* w_kv, int64_t n, int64_t m_tiles,
+                   KvProjParams p, cudaStream_t stream) {
+  CUtensorMap amap, bmap;
+  int st = make_tensor_map_2d_bf16(hidden, (uint64_t)p.k_dim, (uint64_t)p.num_tokens, (uint64_t)hidden_stride * 2,
+                                   kBK, kBM, &amap);
+  if (st) return st;
+  st = make_tensor_map_2d_bf16(w_kv, (uint64_t)p.k_dim, (uint64_t)n, (uint64_t)p.k_dim * 2, kBK, BN, &bmap);
+  if (st) return st;
+  st = ensure_smem_attribute(reinterpret_cast<const void*>(&kv_proj_paged_kernel<BN>), KvTile<BN>::kSmemBytes,
+                             g_smem_done[BN == 256 ? 1 : 0]);
+  if (st) return st;
+  p.n_tiles = (int32_t)(n / BN);
+  p.tiles = (int32_t)(m_tiles * p.n_tiles);
+  const int grid = p.tiles < kNumSMs ? p.tiles : kNumSMs;  // one persistent CTA per SM
+  kv_proj_paged_kernel<BN><<<grid, kThreads, KvTile<BN>::kSmemBytes, stream>>>(amap, bmap, p);
+  return cuda_status(cudaGetLastError(), "kv_proj_paged launch");
+}
 
 }  // namespace
 }  // namespace vfl
@@ -236,7 +315,7 @@ extern "C" int vfl_kv_proj_paged(const void* hidden, int64_t hidden_stride, cons
                                  void* k_cache, void* v_cache, const int64_t* slot_mapping, int64_t num_tokens,
                                  int32_t hidden_dim, int32_t num_heads, int32_t head_dim, int32_t block_size,
                                  int64_t num_blocks, void* stream) {
-  if (num_tokens < 0 || num_tokens > (int64_t)65535 * kBM || hidden_dim <= 0 || hidden_dim % kBK != 0 ||
+  if (num_tokens < 0 || num_tokens > (int64_t)1 << 30 || hidden_dim <= 0 || hidden_dim % kBK != 0 ||
       hidden_dim > (1 << 20) || num_heads <= 0 || head_dim <= 0 || head_dim % 32 != 0 || block_size <= 0 ||
       num_blocks <= 0)
     return fail(VFL_ERR_INVALID_ARGUMENT,
@@ -244,23 +323,17 @@ extern "C" int vfl_kv_proj_paged(const void* hidden, int64_t hidden_stride, cons
                 "of 32), block_size %d, blocks %lld",
                 (long long)num_tokens, hidden_dim, num_heads, head_dim, block_size, (long long)num_blocks);
   const int64_t n = 2LL * num_heads * head_dim;
-  if (n % kBN != 0 || n > (1 << 20))
-    return fail(VFL_ERR_UNSUPPORTED, "kv_proj_paged: 2 * heads * head_dim = %lld is not a multiple of %d",
-                (long long)n, kBN);
+  if (n % 128 != 0 || n > (1 << 20))
+    return fail(VFL_ERR_UNSUPPORTED, "kv_proj_paged: 2 * heads * head_dim = %lld is not a multiple of 128",
+                (long long)n);
   if (num_tokens == 0) return VFL_OK;
   if (!hidden || !w_kv || !k_cache || !v_cache || !slot_mapping)
     return fail(VFL_ERR_INVALID_ARGUMENT, "kv_proj_paged: NULL pointer");
   if (!aligned16(hidden) || !aligned16(w_kv) || !aligned16(k_cache) || !aligned16(v_cache) ||
       (hidden_stride * 2) % 16 != 0 || hidden_stride < hidden_dim)
     return fail(VFL_ERR_INVALID_ARGUMENT, "kv_proj_paged: pointers and the hidden row stride must be 16-byte aligned");
-  CUtensorMap amap, bmap;
-  int st = make_tensor_map_2d_bf16(hidden, (uint64_t)hidden_dim, (uint64_t)num_tokens, (uint64_t)hidden_stride * 2,
-                                   kBK, kBM, &amap);
-  if (st) return st;
-  st = make_tensor_map_2d_bf16(w_kv, (uint64_t)hidden_dim, (uint64_t)n, (uint64_t)hidden_dim * 2, kBK, kBN, &bmap);
-  if (st) return st;
-  st = ensure_smem_attribute(reinterpret_cast<const void*>(&kv_proj_paged_kernel), kSmemBytes, g_smem_done);
-  if (st) return st;
+  const int64_t m_tiles = (num_tokens + kBM - 1) / kBM;
+  if (m_tiles * (n / 128) > INT32_MAX) return fail(VFL_ERR_UNSUPPORTED, "kv_proj_paged: too many tiles");
   KvProjParams p{};
   p.bias = static_cast<const __nv_bfloat16*>(bias);
   p.k_cache = static_cast<__nv_bfloat16*>(k_cache);
@@ -272,9 +345,9 @@ extern "C" int vfl_kv_proj_paged(const void* hidden, int64_t hidden_stride, cons
   p.heads = num_heads;
   p.head_dim = head_dim;
   p.block_size = block_size;
-  st = device_error_word(&p.err);
+  int st = device_error_word(&p.err);
   if (st) return st;
-  dim3 grid((unsigned)(n / kBN), (unsigned)((num_tokens + kBM - 1) / kBM));
-  kv_proj_paged_kernel<<<grid, 128, kSmemBytes, static_cast<cudaStream_t>(stream)>>>(amap, bmap, p);
-  return cuda_status(cudaGetLastError(), "kv_proj_paged launch");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (n % 256 == 0) return launch_kv_proj<256>(hidden, hidden_stride, w_kv, n, m_tiles, p, s);
+  return launch_kv_proj<128>(hidden, hidden_stride, w_kv, n, m_tiles, p, s);
 }
