@@ -484,9 +484,13 @@ def decode_measure(name: str, world: int, rank: int, local: int, eager: bool = F
     params = SamplingParams.from_dict(cfg["params"])
     eng = Engine(model, max_num_seqs=cfg["max_num_seqs"], max_decoder_len=cfg["max_decoder_len"],
                  max_encoder_len=cfg["max_encoder_len"], block_size=BS, cuda_graphs=not eager)
-    # warm-up on a few of this rank's requests (allocator, library set-up); graphs for every
-    # batch size this run can reach are captured up front, as a server does at start-up
-    eng.generate(mine[: max(1, min(2, len(mine)))], SamplingParams.from_dict(dict(cfg["params"], max_tokens=4)))
+    # warm-up, as a server does at start-up: one wave of this rank's requests (the encoder and
+    # library kernels for the batch shapes the run meets; first use of a kernel otherwise lands
+    # in the timed region and cost up to seconds), 4 tokens each; graphs for every batch size
+    # this run can reach are captured up front. The timed run then encodes and decodes every
+    # request from scratch.
+    wave = max(1, min(len(mine), cfg["max_num_seqs"] // params.num_beams))
+    eng.generate(mine[:wave], SamplingParams.from_dict(dict(cfg["params"], max_tokens=4)))
     if eng.graphs is not None:
         eng.graphs.capture(min(cfg["max_num_seqs"], len(mine) * params.num_beams), params.num_beams)
     barrier(world)

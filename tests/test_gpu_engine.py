@@ -94,3 +94,25 @@ def test_grouped_beams_match_row_by_row(engine_trace, graphs):
     assert results[0][0] == results[1][0]
     assert results[0][1] == results[1][1]
     assert paged_ops.read_device_errors(DEV) == 0
+
+
+def test_fused_encoder_kv_matches_gemm_then_append(engine_trace):
+    """bf16: the encoder pages written by the fused projection + page write equal (to one bf16
+    step) those of the projection GEMM followed by the append kernel."""
+    from vflorence_b200.engine import Engine, Request, SamplingParams
+
+    run = next(r for r in engine_trace["runs"] if r["name"] == "beam4")
+    model = _hf_model(engine_trace).to(torch.bfloat16)
+    pools = []
+    for fused in (True, False):
+        eng = Engine(model, max_num_seqs=16, max_decoder_len=8, max_encoder_len=model.config.max_position_embeddings,
+                     fused_encoder_kv=fused)
+        assert eng.fused_encoder_kv == fused
+        params = SamplingParams.from_dict(dict(run["sampling"], max_tokens=2))
+        for r in run["requests"]:
+            eng.add_request(Request(r), params)
+        eng.step()  # admits and encodes every request
+        pools.append([torch.stack(c).float() for c in (eng.kv.cross_k_caches, eng.kv.cross_v_caches)])
+    for a, b in zip(*pools):
+        assert bool(((a - b).abs() <= 2e-2 + b.abs() * 2.0 ** -7).all())
+        assert float((a == b).float().mean()) >= 0.99

@@ -4,7 +4,8 @@ One step (the same order as the reference engine, vflorence/engine/llm_engine.py
   1. admit waiting requests while their beams fit in ``max_num_seqs``;
   2. make room for every running row's next token (native runtime; copy-on-write pairs);
   3. encode the step's new requests (one padded batch per image shape) and page their
-     encoder K/V into the cross pool, once per request;
+     encoder K/V into the cross pool, once per request (bf16: projection and page write in one
+     tensor-core launch per layer);
   4. copy-on-write copies (one launch), device-side step metadata (one upload, one kernel),
      cross staging (memoised on the batch's request ids), then one decoder forward;
   5. greedy argmax or beam candidates on the GPU, one small copy back, and the step's
@@ -52,8 +53,13 @@ class _Req:
 class Engine:
     def __init__(self, hf_model, *, max_num_seqs: int, max_decoder_len: int, max_encoder_len: int,
                  block_size: int = 16, num_blocks: int | None = None, decoder_start_token_id: int | None = None,
-                 record_steps: bool = False, cuda_graphs: bool = False, group_beams: bool | str = True):
+                 record_steps: bool = False, cuda_graphs: bool = False, group_beams: bool | str = True,
+                 fused_encoder_kv: bool = True):
         self.model = PagedSeq2Seq(hf_model)
+        # encoder K/V: one tensor-core launch per layer that projects and writes the pages (bf16);
+        # False (or another dtype) runs the projection GEMM, then the append kernel
+        self.fused_encoder_kv = fused_encoder_kv and paged_ops.kv_proj_supported(
+            self.model.dtype, self.model.d_model, self.model.num_heads, self.model.head_dim)
         # beam search: one attention group per request with per-row block tables (bf16, head_dim
         # 64) where enough requests keep the GPU busy ("always": whatever the batch); False
         # attends row by row (the same results, for comparisons)
@@ -246,8 +252,12 @@ class Engine:
             pix = None if px is None else torch.stack([s.pixel_values for s in batch]).to(self.device)
             hidden = self.model.encode(ids, pix, mask.to(self.device) if ragged else None)
             for layer in range(len(self.model.layers)):
-                k, v = self.model.cross_kv(layer, hidden)
-                self.kv.write_encoder_kv(layer, k, v, slots)
+                if self.fused_encoder_kv:
+                    L = self.model.layers[layer]
+                    self.kv.project_encoder_kv(layer, hidden.reshape(-1, self.model.d_model), L.w_kv, L.b_kv, slots)
+                else:
+                    k, v = self.model.cross_kv(layer, hidden)
+                    self.kv.write_encoder_kv(layer, k, v, slots)
 
     def _beam_groups(self, rows: StepRows) -> dict:
         """Self-attention groups of an eager beam step: runs of consecutive rows of one request

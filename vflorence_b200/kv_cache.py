@@ -3,7 +3,7 @@ paged path (vflorence/engine/model_runner.py), on one CUDA device.
 
     allocate_kv_cache   model_runner.py:62-100   per-layer self and cross pools [N, H, bs, D]
     copy_blocks         model_runner.py:162-167  copy-on-write pairs, all layers, one launch
-    CrossPageAllocator, page_requests / write_encoder_kv / clear_request / reset
+    CrossPageAllocator, page_requests / write_encoder_kv / project_encoder_kv / clear_request / reset
                         model_runner.py:169-177, :232-259, :261-271
     prepare_decode      model_runner.py:273-341  one pinned upload + one kernel per step
     stage_cross         model_runner.py:320-327  memoised on the batch's request ids
@@ -148,6 +148,12 @@ class PagedKVCache:
         """Store one layer's encoder K/V rows [G * enc_len, H, D] at ``slots``."""
         paged_ops.reshape_and_cache(key, value, self.cross_k_caches[layer], self.cross_v_caches[layer],
                                     slots, isa=self.isa)
+
+    def project_encoder_kv(self, layer: int, hidden: torch.Tensor, w_kv: torch.Tensor, b_kv: torch.Tensor | None,
+                           slots: torch.Tensor) -> None:
+        """One layer's encoder K/V projected from ``hidden`` [G * S, d_model] and written at
+        ``slots`` in one launch (bf16 tensor cores; vfl_kv_proj_paged)."""
+        paged_ops.kv_proj_paged(hidden, w_kv, b_kv, self.cross_k_caches[layer], self.cross_v_caches[layer], slots)
 
     def clear_request(self, request_id: int) -> None:
         self.cross.release(request_id)
