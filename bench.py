@@ -13,8 +13,10 @@ needed between steps.
 ``value`` = algorithmic HBM bytes per step / device time per step (GB/s), inputs resident in HBM.
 ``e2e``   = the same bytes over the time of the public API path with host buffers: every step
             uploads its inputs from pinned host memory, plans on the host, runs the ops and reads
-            both outputs back.
-``roofline`` = the paged self-attention kernel (main + split combine), timed with CUDA events in
+            both outputs back - pipelined as a serving loop runs it (uploads and read-backs on
+            their own streams with double buffers, overlapping the neighbouring steps' kernels;
+            the host waits for each step's results one step later).
+``roofline`` = the paged self-attention kernel (split partials merged as planned), timed with CUDA events in
             the timed region, against the measured HBM copy bandwidth.
 ``cpu_baseline`` = the C oracle (the restated vllm_cpu_attn arithmetic; the library itself cannot
             be installed) on the host cores, on a bounded sample of the same workload.
@@ -649,37 +651,66 @@ def main():
     total_bytes = sum_over_ranks(float(nb["total"] * args.steps))
     value = total_bytes / (elapsed_max / 1e3) / 1e9
 
-    # ---- e2e leg: public API with host buffers (pinned inputs up, outputs down, host planning)
+    # ---- e2e leg: public API with host buffers (pinned inputs up, outputs down, host planning),
+    # pipelined as a serving loop runs it: step i's inputs go up on a copy stream into one of two
+    # device buffer sets while step i-1 computes, its outputs come down on another stream into
+    # one of two pinned buffers, and the host waits for step i-1's results before issuing step
+    # i+1. Every step still moves all of its bytes, and the host reads every result.
     host_in = {k: w[k].cpu().pin_memory() for k in ("q", "k_new", "v_new", "qc")}
     host_meta = {k: w[k].pin_memory() for k in ("table", "cross_table", "slots", "ctx", "cross_lens", "qsl")}
-    host_out = torch.empty_like(host_in["q"]).pin_memory()
-    host_out_c = torch.empty_like(host_in["qc"]).pin_memory()
-    h2d = sum(t.nbytes for t in host_in.values()) + sum(t.nbytes for t in host_meta.values())
-    d2h = host_out.nbytes + host_out_c.nbytes
+    host_all = {**host_in, **host_meta}
+    dev_sets = [{k: torch.empty_like(t, device=device) for k, t in host_all.items()} for _ in range(2)]
+    dev_outs = [(torch.empty_like(step.out), torch.empty_like(step.out_c)) for _ in range(2)]
+    host_outs = [(torch.empty_like(host_in["q"]).pin_memory(), torch.empty_like(host_in["qc"]).pin_memory())
+                 for _ in range(2)]
+    h2d = sum(t.nbytes for t in host_all.values())
+    d2h = host_outs[0][0].nbytes + host_outs[0][1].nbytes
     e2e_steps = max(3, min(args.steps, 100))
+    copy_in, copy_out = torch.cuda.Stream(device), torch.cuda.Stream(device)
+    ev_in = [torch.cuda.Event() for _ in range(2)]
+    ev_done = [torch.cuda.Event() for _ in range(2)]
+    ev_out = [torch.cuda.Event() for _ in range(2)]
 
-    def e2e_step():
-        dv = {k: t.to(device, non_blocking=True) for k, t in {**host_in, **host_meta}.items()}
-        meta_s = ops.get_scheduler_metadata(args.batch, H, H, D, host_meta["ctx"], DTYPE, host_meta["qsl"],
-                                            False, "sm100", BS)
-        meta_c = ops.get_scheduler_metadata(args.batch, H, H, D, host_meta["cross_lens"], DTYPE,
-                                            host_meta["qsl"], False, "sm100", BS)
-        step.append(dv["k_new"], dv["v_new"], dv["slots"])
-        step.self_attn(dv["q"], step.out, meta_s, dv["ctx"], dv["qsl"], dv["table"])
-        step.cross_attn(dv["qc"], step.out_c, meta_c, dv["cross_lens"], dv["qsl"], dv["cross_table"])
-        host_out.copy_(step.out, non_blocking=True)
-        host_out_c.copy_(step.out_c, non_blocking=True)
-        torch.cuda.current_stream(device).synchronize()  # the caller reads the results
+    def e2e_run(n, start_ev=None, end_ev=None):
+        if start_ev is not None:
+            start_ev.record(stream)
+            copy_in.wait_event(start_ev)
+        for i in range(n):
+            b = i % 2
+            dv, (o, oc), (ho, hoc) = dev_sets[b], dev_outs[b], host_outs[b]
+            with torch.cuda.stream(copy_in):
+                if i >= 2:
+                    copy_in.wait_event(ev_done[b])  # step i-2 has finished reading set b
+                for k, t in host_all.items():
+                    dv[k].copy_(t, non_blocking=True)
+                ev_in[b].record(copy_in)
+            meta_s = ops.get_scheduler_metadata(args.batch, H, H, D, host_meta["ctx"], DTYPE, host_meta["qsl"],
+                                                False, "sm100", BS)
+            meta_c = ops.get_scheduler_metadata(args.batch, H, H, D, host_meta["cross_lens"], DTYPE,
+                                                host_meta["qsl"], False, "sm100", BS)
+            stream.wait_event(ev_in[b])
+            if i >= 2:
+                stream.wait_event(ev_out[b])  # step i-2's outputs have left buffer b
+            step.append(dv["k_new"], dv["v_new"], dv["slots"])
+            step.self_attn(dv["q"], o, meta_s, dv["ctx"], dv["qsl"], dv["table"])
+            step.cross_attn(dv["qc"], oc, meta_c, dv["cross_lens"], dv["qsl"], dv["cross_table"])
+            ev_done[b].record(stream)
+            with torch.cuda.stream(copy_out):
+                copy_out.wait_event(ev_done[b])
+                ho.copy_(o, non_blocking=True)
+                hoc.copy_(oc, non_blocking=True)
+                ev_out[b].record(copy_out)
+            if i >= 1:
+                ev_out[(i - 1) % 2].synchronize()  # the caller reads step i-1's results
+        if end_ev is not None:
+            end_ev.record(copy_out)
+        ev_out[(n - 1) % 2].synchronize()
 
-    for _ in range(3):
-        e2e_step()
+    e2e_run(3)
     barrier(world)
     torch.cuda.synchronize()
     s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    s2.record(stream)
-    for _ in range(e2e_steps):
-        e2e_step()
-    e2.record(stream)
+    e2e_run(e2e_steps, s2, e2)
     torch.cuda.synchronize()
     barrier(world)
     e2e_ms = max_over_ranks(s2.elapsed_time(e2))
@@ -698,7 +729,7 @@ def main():
     launches = step.launches * args.steps
     decode = None
     if args.decode_config != "none":
-        del w, step, d, host_in, host_meta, host_out, host_out_c
+        del w, step, d, host_in, host_meta, host_all, dev_sets, dev_outs, host_outs
         torch.cuda.empty_cache()
         try:
             decode = decode_measure(args.decode_config, world, rank, local)
