@@ -173,7 +173,7 @@ class Engine:
         fresh = np.flatnonzero(rows.positions == 0)
         if len(fresh):
             self._encode([self.requests[int(r)] for r in rows.request_ids[fresh]])
-        self.kv.copy_blocks(copies)
+        self.kv.copy_blocks(copies, checked=True)
         if self.record is not None:
             tables = g.host_views()[0] if g is not None else host[: n * W].reshape(n, W)
             self.record.append({"request_ids": rows.request_ids.tolist(), "positions": rows.positions.tolist(),

@@ -116,16 +116,19 @@ class PagedKVCache:
         return sum(t.nbytes for t in self.k_caches + self.v_caches + self.cross_k_caches + self.cross_v_caches)
 
     # ------------------------------------------------------------------------ copy-on-write
-    def copy_blocks(self, copies) -> None:
+    def copy_blocks(self, copies, checked: bool = False) -> None:
         """Copy whole self-attention blocks src -> dst in every layer (before the step's append).
         ``copies``: (src, dst) pairs, a list or an integer [P, 2] array (uploaded through one
-        reused pinned buffer)."""
+        reused pinned buffer). ``checked``: the pairs come from the native runtime, which only
+        makes in-range pairs with distinct destinations disjoint from the sources (the kernel
+        still skips and flags out-of-range pairs); others are checked on the host."""
         if isinstance(copies, np.ndarray):
             pairs = np.asarray(copies, dtype=np.int64).reshape(-1, 2)
             P = len(pairs)
             if P == 0:
                 return
-            paged_ops.check_copy_pairs_array(pairs, self.num_blocks)
+            if not checked:
+                paged_ops.check_copy_pairs_array(pairs, self.num_blocks)
             if self._pairs_host is None or self._pairs_host.numel() < 2 * P:
                 self._pairs_host = torch.zeros(max(2 * P, 1024), dtype=torch.int64).pin_memory()
                 self._pairs_dev = torch.zeros_like(self._pairs_host, device=self.device)
