@@ -174,15 +174,18 @@ __global__ void __launch_bounds__(160, QPC == 1 ? 3 : 2) paged_attention_kernel(
   const int bs = p.block_size;
   const int bps = p.blocks_per_split;
 
-  if (load_volatile(p.err) & VFL_DEVERR_TIMEOUT) return;
+  // the item's independent reads in one round trip: the error word, its query range, its length
+  const unsigned int err_now = load_volatile(p.err);
+  const int q_begin = __ldg(p.qsl + r);
+  const int q_end = __ldg(p.qsl + r + 1);
+  int L = __ldg(p.seq_lens + r);
+  if (err_now & VFL_DEVERR_TIMEOUT) return;  // an earlier CTA gave up waiting
   if (bps < 1 || bps > kMaxBlocksPerSplit || p.stages < 2 || p.stages > kMaxStages) {  // the host checks the plan too
     if (threadIdx.x == 0) report(p.err, VFL_DEVERR_CONTEXT);
     return;
-  }  // an earlier CTA gave up waiting
+  }
 
   // ---- this CTA's query rows and visible lengths (uniform across the CTA)
-  const int q_begin = __ldg(p.qsl + r);
-  const int q_end = __ldg(p.qsl + r + 1);
   if (q_begin < 0 || q_end < q_begin || q_end > p.total_q) {
     if (threadIdx.x == 0 && split == 0 && blockIdx.z == 0) report(p.err, VFL_DEVERR_QUERY);
     return;
@@ -190,7 +193,6 @@ __global__ void __launch_bounds__(160, QPC == 1 ? 3 : 2) paged_attention_kernel(
   const int q0 = q_begin + blockIdx.z * QPC;
   const int nq = min(QPC, q_end - q0);
   if (nq <= 0) return;
-  int L = __ldg(p.seq_lens + r);
   const int cap = min(p.table_cols * bs, p.max_seq_len);
   if (L > cap) {
     if (threadIdx.x == 0 && split == 0 && blockIdx.z == 0) report(p.err, VFL_DEVERR_CONTEXT);
