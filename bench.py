@@ -483,6 +483,9 @@ def decode_measure(name: str, world: int, rank: int, local: int, eager: bool = F
     reqs = decode_requests(cfg, device)
     costs = [len(r.input_ids) + cfg["params"]["num_beams"] * cfg["params"]["max_tokens"] for r in reqs]
     mine = [reqs[i] for i in assign_requests(costs, world)[rank]]
+    for r in mine:  # images wait in pinned host memory, as a pinned data loader hands them over
+        if r.pixel_values is not None:
+            r.pixel_values = r.pixel_values.pin_memory()
     params = SamplingParams.from_dict(cfg["params"])
     eng = Engine(model, max_num_seqs=cfg["max_num_seqs"], max_decoder_len=cfg["max_decoder_len"],
                  max_encoder_len=cfg["max_encoder_len"], block_size=BS, cuda_graphs=not eager)

@@ -116,3 +116,49 @@ def test_fused_encoder_kv_matches_gemm_then_append(engine_trace):
     for a, b in zip(*pools):
         assert bool(((a - b).abs() <= 2e-2 + b.abs() * 2.0 ** -7).all())
         assert float((a == b).float().mean()) >= 0.99
+
+
+def _tiny_florence2():
+    """Florence-2-shaped model (DaViT vision tower + BART), random init, fp32: 64 x 64 images
+    give 5 image tokens; head_dim 64."""
+    from transformers import Florence2Config, Florence2ForConditionalGeneration
+
+    text = dict(vocab_size=51290, d_model=128, encoder_layers=2, decoder_layers=2, encoder_attention_heads=2,
+                decoder_attention_heads=2, encoder_ffn_dim=256, decoder_ffn_dim=256, max_position_embeddings=128,
+                activation_function="gelu", decoder_start_token_id=2, eos_token_id=2, bos_token_id=0, pad_token_id=1)
+    vision = dict(embed_dim=[32, 64, 96, 128], num_heads=[2, 2, 2, 4], num_groups=[2, 2, 2, 4], depths=[1, 1, 1, 1],
+                  projection_dim=128)
+    torch.manual_seed(0)
+    with torch.device(DEV):
+        model = Florence2ForConditionalGeneration(Florence2Config(text_config=text, vision_config=vision,
+                                                                  image_token_id=51289))
+    return model.eval()
+
+
+def test_encoder_prepared_mask_matches_hf_padding_mask():
+    """Ragged prompts with images, fp32: the engine's encoder (images copied one by one into the
+    batch, the padding mask passed as a prepared 4-D mask, no host read of it) gives the hidden
+    states of HuggingFace's own encoder with the 2-D padding mask, at every real position."""
+    from vflorence_b200.engine.model import PagedSeq2Seq
+
+    torch.backends.cuda.matmul.allow_tf32 = False
+    torch.backends.cudnn.allow_tf32 = False
+    hf = _tiny_florence2()
+    m = PagedSeq2Seq(hf)
+    g = torch.Generator().manual_seed(5)
+    lens = [3, 8, 5, 8]
+    ids = torch.full((len(lens), 5 + max(lens)), 1, dtype=torch.long)
+    mask = torch.zeros_like(ids)
+    for i, n in enumerate(lens):
+        ids[i, :5 + n] = torch.tensor([51289] * 5 + torch.randint(4, 51289, (n,), generator=g).tolist())
+        mask[i, :5 + n] = 1
+    px = torch.randn(len(lens), 3, 64, 64, generator=g).to(DEV)
+    ids, mask = ids.to(DEV), mask.to(DEV)
+    with torch.inference_mode():
+        mine = m.encode(ids, px, mask)
+        feats = hf.model.get_image_features(px).pooler_output
+        emb = m.lm.get_input_embeddings()(ids)
+        emb = emb.masked_scatter((ids == 51289).unsqueeze(-1).expand_as(emb), feats)
+        ref = m.lm.encoder(inputs_embeds=emb, attention_mask=mask).last_hidden_state
+    real = mask.bool()
+    torch.testing.assert_close(mine[real], ref[real], rtol=1e-5, atol=1e-5)

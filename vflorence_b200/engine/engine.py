@@ -248,9 +248,15 @@ class Engine:
                 t = torch.arange(n)
                 slots[i, :n] = pages[t // bs] * bs + t % bs
             ragged = bool((mask == 0).any())
-            ids, slots = ids.to(self.device), slots.view(-1).to(self.device)
-            pix = None if px is None else torch.stack([s.pixel_values for s in batch]).to(self.device)
-            hidden = self.model.encode(ids, pix, mask.to(self.device) if ragged else None)
+            # pinned staging: the uploads queue on the stream without waiting for it
+            up = lambda t: t.pin_memory().to(self.device, non_blocking=True)  # noqa: E731
+            ids, slots = up(ids), up(slots.view(-1))
+            pix = None
+            if px is not None:  # one copy per image into the batch (asynchronous from pinned memory)
+                pix = torch.empty((len(batch),) + px, dtype=batch[0].pixel_values.dtype, device=self.device)
+                for i, s in enumerate(batch):
+                    pix[i].copy_(s.pixel_values, non_blocking=True)
+            hidden = self.model.encode(ids, pix, up(mask) if ragged else None)
             for layer in range(len(self.model.layers)):
                 if self.fused_encoder_kv:
                     L = self.model.layers[layer]

@@ -84,6 +84,7 @@ class PagedSeq2Seq:
                attention_mask: torch.Tensor | None = None) -> torch.Tensor:
         """Encoder hidden states [G, S, d_model] for a batch of prompts (right-padded and masked
         when their lengths differ; padded positions are never paged)."""
+        attention_mask = self._encoder_mask(attention_mask)
         if pixel_values is None:
             return self.lm.encoder(input_ids=input_ids, attention_mask=attention_mask).last_hidden_state
         feats = self.hf.model.get_image_features(pixel_values.to(self.dtype)).pooler_output
@@ -91,6 +92,22 @@ class PagedSeq2Seq:
         mask = (input_ids == self.image_token_id).unsqueeze(-1).expand_as(embeds)
         embeds = embeds.masked_scatter(mask, feats.to(embeds.dtype))
         return self.lm.encoder(inputs_embeds=embeds, attention_mask=attention_mask).last_hidden_state
+
+    def _encoder_mask(self, mask: torch.Tensor | None):
+        """The padding mask [G, S] as the prepared 4-D mask the encoder's attention takes (a 4-D
+        mask is passed on as is), so that no host read of the mask stalls the stream: boolean
+        (True = attend) for sdpa, additive for eager; other implementations get the 2-D mask."""
+        if mask is None:
+            return None
+        impl = self.lm.config._attn_implementation
+        g, s = mask.shape
+        keep = mask.bool()[:, None, None, :].expand(g, 1, s, s)
+        if impl == "sdpa":
+            return keep
+        if impl == "eager":
+            add = torch.zeros(keep.shape, dtype=self.dtype, device=mask.device)
+            return add.masked_fill(~keep, torch.finfo(self.dtype).min)
+        return mask
 
     def cross_kv(self, layer: int, hidden: torch.Tensor):
         """Encoder K/V of one decoder layer as [G*S, H, head_dim] views of one fused GEMM."""
