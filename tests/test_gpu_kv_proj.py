@@ -2,9 +2,10 @@
 PyTorch fp32 reference of the same op: kv = hidden @ w_kv.T + bias, rounded to bf16, scattered
 by slot into [num_blocks, H, block_size, D] pools (vflorence/engine/model_runner.py:248-259).
 
-Tolerance: bf16, 2e-2 absolute plus one bf16 step (2^-7 relative) - both sides round the same
-fp32 value after sums in different orders, so an entry at a rounding boundary may differ by one
-step; at least 99 % of entries must be bit-equal."""
+Token counts from 6144 up, with 256-multiple feature counts, run the 2-SM (cta_group::2)
+kernel; smaller ones the one-CTA kernel. Tolerance: bf16, 2e-2 absolute plus one bf16 step
+(2^-7 relative) - both sides round the same fp32 value after sums in different orders, so an
+entry at a rounding boundary may differ by one step; at least 99 % of entries must be bit-equal."""
 
 from __future__ import annotations
 
@@ -50,8 +51,12 @@ def _reference(hidden, w, bias, kc, vc, slots):
     (1000, 768, 12, 64, 16, True),     # Florence-2-base
     (128, 1024, 16, 64, 32, False),    # one full tile, block 32, no bias
     (77, 64, 2, 32, 16, True),         # one K step, head_dim 32
-    (5000, 1024, 16, 64, 16, True),    # enough tokens for 256-feature tiles
-    (4500, 768, 12, 64, 16, False),    # 256-feature tiles over 1536 features
+    (5000, 1024, 16, 64, 16, True),    # one-CTA kernel, 256-feature tiles, several tiles per CTA
+    (4500, 768, 12, 64, 16, False),    # one-CTA kernel over 1536 features
+    (6322, 768, 12, 64, 16, False),    # 2-SM pair tiles (256 tokens x 256 features); the last
+                                       # tile's second CTA has 50 tokens
+    (6200, 1024, 16, 64, 16, True),    # pair tiles; the last tile's second CTA has no tokens
+    (20000, 1024, 16, 64, 32, True),   # many tiles per pair: both accumulators reused
 ])
 def test_kv_proj_paged_matches_fp32_reference(tokens, hidden_dim, heads, head_dim, block_size, with_bias):
     from vflorence_b200 import paged_ops as ops
@@ -84,11 +89,12 @@ def test_kv_proj_paged_equals_gemm_then_append():
         assert bool(((got.float() - want.float()).abs() <= 2e-2 + want.float().abs() * 2.0 ** -7).all())
 
 
-def test_kv_proj_paged_flags_slots_past_the_pool():
+@pytest.mark.parametrize("tokens", [40, 7000], ids=["one_cta", "pair"])
+def test_kv_proj_paged_flags_slots_past_the_pool(tokens):
     from vflorence_b200 import _native
     from vflorence_b200 import paged_ops as ops
 
-    hidden, w, bias, kc, vc, slots = _case(40, 128, 2, 64, 16, seed=9, skip_every=0)
+    hidden, w, bias, kc, vc, slots = _case(tokens, 128, 2, 64, 16, seed=9, skip_every=0)
     before_k, before_v = kc.clone(), vc.clone()
     slots[5] = kc.shape[0] * kc.shape[2]  # one past the last slot: flagged, not written
     ek, ev = _reference(hidden, w, bias, before_k, before_v, torch.where(slots == slots[5], -1, slots))
