@@ -210,6 +210,22 @@ int vfl_kv_proj_paged(const void* hidden, int64_t hidden_stride, const void* w_k
                       int32_t hidden_dim, int32_t num_heads, int32_t head_dim, int32_t block_size,
                       int64_t num_blocks, void* stream);
 
+/* replaces the post-norm residual of the decoder that calls the paged ops
+ *   (vflorence/models/bart.py:192-201, LayerNorm(hidden + sublayer(hidden)) after the
+ *   self-attention, the cross-attention and the FFN; and bart.py:260-264, the embedding's
+ *   LayerNorm(tokens + positions)): out = LayerNorm(h + x) * weight + bias over rows of
+ *   hidden_dim elements, in one launch. h + x is rounded to dtype first, as a separate add does;
+ *   mean and biased variance in fp32; eps as torch.nn.LayerNorm. bias may be NULL. Strides are
+ *   in elements; pointers and strides 16-byte aligned. hidden_dim must satisfy
+ *   vfl_add_layernorm_supported (a multiple of 256 elements up to 2048 for bf16, of 128 up to
+ *   1024 for fp32), VFL_ERR_UNSUPPORTED otherwise. out may alias h or x. */
+int vfl_add_layernorm(const void* h, int64_t h_stride, const void* x, int64_t x_stride,
+                      const void* weight, const void* bias, void* out, int64_t out_stride,
+                      int32_t rows, int32_t hidden_dim, float eps, int32_t dtype, void* stream);
+
+/* 1 when vfl_add_layernorm is built for this dtype and hidden_dim, else 0. */
+int vfl_add_layernorm_supported(int dtype, int hidden_dim);
+
 /* replaces the encoder slot computation of ModelRunner._encode
  *   (vflorence/engine/model_runner.py:240-242): for request g and token t < seq_len,
  *   slot_mapping[g * seq_len + t] = pages[g, t // block_size] * block_size + t % block_size. */

@@ -192,3 +192,27 @@ def test_ops_refuse_cpu_tensors(native):
         ops.reshape_and_cache(k, k, kc, kc, torch.zeros(1, dtype=torch.int64))
     with pytest.raises(ValueError, match="CUDA"):
         ops.copy_blocks([kc], [kc], [(0, 1)])
+
+
+def test_add_layernorm_host_checks(native):
+    """Which widths the fused add + LayerNorm is built for, and refusals before any launch."""
+    from vflorence_b200 import _native
+
+    bf16, f32 = _native.DTYPE_BF16, _native.DTYPE_F32
+    for d in (256, 512, 768, 1024, 2048):
+        assert native.vfl_add_layernorm_supported(bf16, d) == 1
+    for d in (128, 640, 4096):
+        assert native.vfl_add_layernorm_supported(bf16, d) == 0
+    for d in (128, 768, 1024):
+        assert native.vfl_add_layernorm_supported(f32, d) == 1
+    assert native.vfl_add_layernorm_supported(f32, 2048) == 0
+    assert native.vfl_add_layernorm_supported(7, 1024) == 0
+    fake = ctypes.c_void_p(16)
+    st = native.vfl_add_layernorm(fake, 640, fake, 640, fake, None, fake, 640, 4, 640, 1e-5, bf16, None)
+    assert st == _native.VFL_ERR_UNSUPPORTED, native.vfl_last_error_message()
+    st = native.vfl_add_layernorm(fake, 1024, fake, 1024, fake, None, fake, 1024, -1, 1024, 1e-5, bf16, None)
+    assert st == _native.VFL_ERR_INVALID_ARGUMENT
+    st = native.vfl_add_layernorm(ctypes.c_void_p(18), 1024, fake, 1024, fake, None, fake, 1024, 4, 1024, 1e-5,
+                                  bf16, None)  # misaligned rows
+    assert st == _native.VFL_ERR_INVALID_ARGUMENT
+    assert native.vfl_add_layernorm(None, 1024, None, 1024, None, None, None, 1024, 0, 1024, 1e-5, bf16, None) == 0

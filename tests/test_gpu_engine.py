@@ -162,3 +162,28 @@ def test_encoder_prepared_mask_matches_hf_padding_mask():
         ref = m.lm.encoder(inputs_embeds=emb, attention_mask=mask).last_hidden_state
     real = mask.bool()
     torch.testing.assert_close(mine[real], ref[real], rtol=1e-5, atol=1e-5)
+
+
+@pytest.mark.parametrize("graphs", [False, True], ids=["eager", "cuda_graphs"])
+def test_fused_layernorm_same_tokens(graphs):
+    """fp32 Florence-2-shaped model: the decoder with each LayerNorm(h + x) in one launch
+    generates the tokens of the decoder with the add and the torch modules."""
+    from vflorence_b200.engine import Engine, Request, SamplingParams
+
+    torch.backends.cuda.matmul.allow_tf32 = False
+    torch.backends.cudnn.allow_tf32 = False
+    model = _tiny_florence2()
+    g = torch.Generator().manual_seed(11)
+    reqs = [Request([51289] * 5 + torch.randint(4, 51289, (n,), generator=g).tolist(),
+                    torch.randn(3, 64, 64, generator=g)) for n in (3, 6, 4, 8, 5)]
+    results = []
+    for fused in (True, False):
+        eng = Engine(model, max_num_seqs=6, max_decoder_len=24, max_encoder_len=32, cuda_graphs=graphs,
+                     fused_layernorm=fused)
+        assert eng.model.fused_layernorm == fused
+        results.append(eng.generate(reqs, SamplingParams.from_dict(dict(max_tokens=20, num_beams=2,
+                                                                        eos_token_id=[]))))
+    assert results[0] == results[1]
+    from vflorence_b200 import paged_ops
+
+    assert paged_ops.read_device_errors(DEV) == 0

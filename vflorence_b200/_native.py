@@ -50,6 +50,8 @@ EXPORTS = (
     "vfl_copy_blocks",
     "vfl_prepare_decode",
     "vfl_kv_proj_paged",
+    "vfl_add_layernorm",
+    "vfl_add_layernorm_supported",
     "vfl_paged_slots",
     "vfl_row_topk",
     "vfl_row_topk_workspace_size",
@@ -169,6 +171,8 @@ def _declare(L):
         "vfl_prepare_decode": (i32, [vp, i64, i32, vp, i32, i32, vp, vp, vp, vp]),
         "vfl_paged_slots": (i32, [vp, i64, i32, i32, i32, i32, vp, vp]),
         "vfl_kv_proj_paged": (i32, [vp, i64, vp, vp, vp, vp, vp, i64, i32, i32, i32, i32, i64, vp]),
+        "vfl_add_layernorm": (i32, [vp, i64, vp, i64, vp, vp, vp, i64, i32, i32, f32, i32, vp]),
+        "vfl_add_layernorm_supported": (i32, [i32, i32]),
         "vfl_row_topk": (i32, [vp, i32, i64, i64, i64, i32, vp, i32, vp, vp, vp, sz, vp]),
         "vfl_row_topk_workspace_size": (sz, [i64, i64, i32]),
         "vfl_beam_merge": (i32, [vp, vp, i64, i32, vp, vp, i32, i32, vp, vp]),

@@ -7,7 +7,9 @@ sequence: its self-attention goes through ``vflorence::self_attention`` (KV appe
 decode) and its cross-attention through ``vflorence::cross_attention`` (paged encoder K/V), the
 ops the reference's decoder calls (vflorence/models/bart.py:106-146). The q/k/v projections of
 each decoder layer are fused into one GEMM and the encoder k/v projections into another, and the
-kernels take the strided q/k/v views of the fused outputs directly.
+kernels take the strided q/k/v views of the fused outputs directly. Each post-norm residual,
+LayerNorm(h + sublayer(h)), and the embedding's LayerNorm(tokens + positions) run as one
+launch of ``paged_ops.add_layernorm`` where it is built for the model's width and dtype.
 """
 
 from __future__ import annotations
@@ -18,6 +20,7 @@ import torch
 import torch.nn.functional as F
 from transformers.activations import ACT2FN
 
+from .. import paged_ops
 from ..attention import decoder_cross_attention, decoder_self_attention
 
 
@@ -42,7 +45,7 @@ class _Layer:
 
 
 class PagedSeq2Seq:
-    def __init__(self, hf_model):
+    def __init__(self, hf_model, fused_layernorm: bool = True):
         cfg = hf_model.config
         self.is_florence2 = cfg.model_type == "florence2"
         lm_cfg = cfg.get_text_config()
@@ -77,6 +80,11 @@ class PagedSeq2Seq:
         self.dtype = self.pos_weight.dtype
         self.device = self.pos_weight.device
         self.image_token_id = getattr(cfg, "image_token_id", None)
+        norms = [self.ln_embed] + [n for L in self.layers for n in (L.ln_self, L.ln_cross, L.ln_final)]
+        self.fused_layernorm = (fused_layernorm and self.device.type == "cuda"
+                                and all(isinstance(n, torch.nn.LayerNorm) and n.weight is not None
+                                        and tuple(n.normalized_shape) == (self.d_model,) for n in norms)
+                                and paged_ops.add_layernorm_supported(self.dtype, self.d_model))
 
     # ------------------------------------------------------------------------------- encoder
     @torch.inference_mode()
@@ -118,21 +126,27 @@ class PagedSeq2Seq:
         return k.reshape(shape), v.reshape(shape)
 
     # ------------------------------------------------------------------------------- decoder
+    def _add_norm(self, h: torch.Tensor, x: torch.Tensor, norm: torch.nn.LayerNorm) -> torch.Tensor:
+        """``norm(h + x)``: one fused launch, or the add and the module."""
+        if self.fused_layernorm:
+            return paged_ops.add_layernorm(h, x, norm.weight, norm.bias, norm.eps)
+        return norm(h + x)
+
     @torch.inference_mode()
     def decode(self, input_ids: torch.Tensor, positions: torch.Tensor) -> torch.Tensor:
         """One decoder step: logits [B, vocab] for one new token per sequence. The per-step
         Context (slot mapping, block tables, cross staging) must be set."""
         B = input_ids.shape[0]
-        h = self.embed_tokens(input_ids) + F.embedding(positions + self.pos_offset, self.pos_weight)
-        h = self.ln_embed(h)
+        h = self._add_norm(self.embed_tokens(input_ids), F.embedding(positions + self.pos_offset, self.pos_weight),
+                           self.ln_embed)
         shape = (B, self.num_heads, self.head_dim)
         for i, L in enumerate(self.layers):
             q, k, v = (t.reshape(shape) for t in F.linear(h, L.w_qkv, L.b_qkv).chunk(3, dim=-1))
             a = decoder_self_attention(q, k, v, L.self_attn.k_cache, L.self_attn.v_cache, self.scale)
-            h = L.ln_self(h + L.self_out(a.reshape(B, self.d_model)))
+            h = self._add_norm(h, L.self_out(a.reshape(B, self.d_model)), L.ln_self)
             c = decoder_cross_attention(L.cross_q(h).reshape(shape), i, self.scale)
-            h = L.ln_cross(h + L.cross_out(c.reshape(B, self.d_model)))
-            h = L.ln_final(h + L.fc2(self.act(L.fc1(h))))
+            h = self._add_norm(h, L.cross_out(c.reshape(B, self.d_model)), L.ln_cross)
+            h = self._add_norm(h, L.fc2(self.act(L.fc1(h))), L.ln_final)
         logits = F.linear(h, self.w_head, self.b_head)[:, : self.vocab_size]
         if self.final_logits_bias is not None:
             logits = logits + self.final_logits_bias

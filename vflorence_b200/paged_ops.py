@@ -316,6 +316,41 @@ def prepare_decode(block_table: torch.Tensor, positions: torch.Tensor, block_siz
     N.check(st, "prepare_decode")
 
 
+def add_layernorm_supported(dtype: torch.dtype, hidden_dim: int) -> bool:
+    """Whether the fused residual add + LayerNorm is built for this dtype and row width."""
+    return dtype in (torch.float32, torch.bfloat16) and bool(
+        N.lib().vfl_add_layernorm_supported(_dtype_code(dtype), int(hidden_dim)))
+
+
+def add_layernorm(h: torch.Tensor, x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None,
+                  eps: float, out: torch.Tensor | None = None) -> torch.Tensor:
+    """``LayerNorm(h + x) * weight + bias`` over the last dimension of [rows, d] tensors, in one
+    launch - the post-norm residual of the decoder (vflorence/models/bart.py:192-201). ``h + x``
+    is rounded to the dtype first, as ``h + x`` is; statistics in fp32. Returns ``out`` (new
+    unless given; it may be ``h`` or ``x``)."""
+    dev = h.device
+    for name, t in (("h", h), ("x", x), ("weight", weight)):
+        _require_cuda(name, t, dev)
+    if h.dim() != 2 or x.shape != h.shape or h.stride(1) != 1 or x.stride(1) != 1:
+        raise ValueError("vflorence_b200: add_layernorm wants h and x [rows, d] with unit column stride")
+    rows, d = h.shape
+    if x.dtype != h.dtype or weight.dtype != h.dtype or weight.shape != (d,) or not weight.is_contiguous():
+        raise ValueError("vflorence_b200: add_layernorm weight must be contiguous [d] of the rows' dtype")
+    if bias is not None:
+        _require_cuda("bias", bias, dev)
+        if bias.dtype != h.dtype or bias.shape != (d,) or not bias.is_contiguous():
+            raise ValueError("vflorence_b200: add_layernorm bias must be contiguous [d] of the rows' dtype")
+    if out is None:
+        out = torch.empty_like(h, memory_format=torch.contiguous_format)
+    elif out.shape != h.shape or out.dtype != h.dtype or out.stride(1) != 1 or out.device != dev:
+        raise ValueError("vflorence_b200: add_layernorm out must match h")
+    st = N.lib().vfl_add_layernorm(h.data_ptr(), h.stride(0), x.data_ptr(), x.stride(0), weight.data_ptr(),
+                                   None if bias is None else bias.data_ptr(), out.data_ptr(), out.stride(0),
+                                   rows, d, float(eps), _dtype_code(h.dtype), _stream(dev))
+    N.check(st, "add_layernorm")
+    return out
+
+
 def kv_proj_supported(dtype: torch.dtype, hidden_dim: int, num_heads: int, head_dim: int) -> bool:
     """Whether the fused projection + page write is built for this shape (bf16 tensor cores)."""
     return (dtype == torch.bfloat16 and hidden_dim % 64 == 0 and head_dim % 32 == 0
