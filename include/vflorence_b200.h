@@ -263,6 +263,15 @@ int vfl_beam_merge(const float* values, const int32_t* indices, int64_t rows, in
                    const int32_t* groups, const int32_t* ranks, int32_t num_groups, int32_t keep,
                    int32_t* out, void* stream);
 
+/* replaces Sequence.fork's child.token_ids = [*parent.token_ids, token]
+ *   (vflorence/engine/sequence.py:53-55) for the device token rows of a beam step: for each
+ *   born child i, tokens[child_i, :width] = tokens[parent_i, :width] with tokens[child_i, pos_i]
+ *   = token_i. born: device int32 [4, num_born] (parents, children, positions, tokens). No child
+ *   may be a parent of the same call (the decode runtime's slots never are). Rows out of range
+ *   or a position past width are skipped and flagged with VFL_DEVERR_SLOT. */
+int vfl_fork_token_rows(int32_t* tokens, int64_t row_stride, int32_t num_rows, int32_t width,
+                        const int32_t* born, int32_t num_born, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -120,3 +120,36 @@ def test_beam_merge_matches_stable_sort(beams, k, keep, contiguous):
         assert torch.equal(out[1, r][: len(got)], toks[r][valid])
         assert torch.equal(out[2, r][: len(got)].view(torch.float32), vals[r][valid])
         assert (out[0, r][len(got):] == -1).all() and len(got) <= min(keep, m)
+
+
+def test_fork_token_rows_matches_index_ops():
+    """Children's token rows in one launch equal the two torch index ops they replace
+    (Sequence.fork, vflorence/engine/sequence.py:53-55); bad rows are skipped and flagged."""
+    from vflorence_b200 import _native
+    from vflorence_b200 import paged_ops as ops
+
+    g = torch.Generator().manual_seed(4)
+    slots, width = 40, 1026
+    tokens = torch.randint(0, 51289, (slots, width), generator=g, dtype=torch.int32).to(DEV)
+    perm = torch.randperm(slots, generator=g)
+    parents = perm[:10].repeat(2)[:17]                     # a parent may have several children
+    children = perm[10:27]                                  # never a parent of the same step
+    pos = torch.randint(0, width, (17,), generator=g)
+    tok = torch.randint(0, 51289, (17,), generator=g)
+    born = torch.stack([parents, children, pos, tok]).to(torch.int32).contiguous().to(DEV)
+    want = tokens.clone()
+    b = born.long()
+    want[b[1]] = want[b[0]]
+    want[b[1], b[2]] = b[3].to(torch.int32)
+    ops.fork_token_rows(tokens, born)
+    assert torch.equal(tokens, want)
+    assert ops.read_device_errors(DEV) == 0
+    bad = born[:, :2].clone()
+    bad[1, 1] = slots  # a child row past the buffer: skipped, flagged
+    before = tokens.clone()
+    ops.fork_token_rows(tokens, bad)
+    assert ops.read_device_errors(DEV) & _native.DEVERR_SLOT
+    expect = before.clone()
+    expect[bad[1, 0].long()] = before[bad[0, 0].long()]
+    expect[bad[1, 0].long(), bad[2, 0].long()] = bad[3, 0]
+    assert torch.equal(tokens, expect)

@@ -56,6 +56,7 @@ EXPORTS = (
     "vfl_row_topk",
     "vfl_row_topk_workspace_size",
     "vfl_beam_merge",
+    "vfl_fork_token_rows",
     # host decode runtime (vflorence_b200_runtime.h)
     "vfl_rt_create",
     "vfl_rt_destroy",
@@ -176,6 +177,7 @@ def _declare(L):
         "vfl_row_topk": (i32, [vp, i32, i64, i64, i64, i32, vp, i32, vp, vp, vp, sz, vp]),
         "vfl_row_topk_workspace_size": (sz, [i64, i64, i32]),
         "vfl_beam_merge": (i32, [vp, vp, i64, i32, vp, vp, i32, i32, vp, vp]),
+        "vfl_fork_token_rows": (i32, [vp, i64, i32, i32, vp, i32, vp]),
         "vfl_rt_create": (i32, [i32, i32, i32, i32, ctypes.POINTER(vp)]),
         "vfl_rt_destroy": (None, [vp]),
         "vfl_rt_reset": (i32, [vp]),

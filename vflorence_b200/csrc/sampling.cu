@@ -649,3 +649,43 @@ extern "C" int vfl_beam_merge(const float* values, const int32_t* indices, int64
                                                                       num_groups, keep, out);
   return cuda_status(cudaGetLastError(), "beam_merge launch");
 }
+
+namespace vfl {
+namespace {
+
+// One CTA per born child: tokens[child, :] = tokens[parent, :] with tokens[child, pos] = token.
+// The runtime hands children slots off its free stack while every parent still holds its own,
+// so no child row is a parent row of the same step and one pass is enough.
+__global__ void __launch_bounds__(128) fork_token_rows_kernel(int32_t* tokens, int64_t row_stride, int32_t num_rows,
+                                                              int32_t width, const int32_t* born, int32_t num_born,
+                                                              unsigned int* err) {
+  const int i = blockIdx.x;
+  const int32_t parent = __ldg(born + i), child = __ldg(born + num_born + i);
+  const int32_t pos = __ldg(born + 2 * (int64_t)num_born + i), token = __ldg(born + 3 * (int64_t)num_born + i);
+  if (parent < 0 || parent >= num_rows || child < 0 || child >= num_rows || parent == child || pos < 0 ||
+      pos >= width) {
+    if (threadIdx.x == 0) report(err, VFL_DEVERR_SLOT);
+    return;
+  }
+  const int32_t* src = tokens + parent * row_stride;
+  int32_t* dst = tokens + child * row_stride;
+  for (int c = threadIdx.x; c < width; c += blockDim.x) dst[c] = c == pos ? token : src[c];
+}
+
+}  // namespace
+}  // namespace vfl
+
+extern "C" int vfl_fork_token_rows(int32_t* tokens, int64_t row_stride, int32_t num_rows, int32_t width,
+                                   const int32_t* born, int32_t num_born, void* stream) {
+  if (num_rows < 0 || width < 1 || row_stride < width || num_born < 0 || num_born > (1 << 30))
+    return fail(VFL_ERR_INVALID_ARGUMENT, "fork_token_rows: rows %d, width %d, row_stride %lld, born %d", num_rows,
+                width, (long long)row_stride, num_born);
+  if (num_born == 0) return VFL_OK;
+  if (tokens == nullptr || born == nullptr) return fail(VFL_ERR_INVALID_ARGUMENT, "fork_token_rows: NULL pointer");
+  unsigned int* err = nullptr;
+  int st = device_error_word(&err);
+  if (st) return st;
+  fork_token_rows_kernel<<<(unsigned)num_born, 128, 0, static_cast<cudaStream_t>(stream)>>>(
+      tokens, row_stride, num_rows, width, born, num_born, err);
+  return cuda_status(cudaGetLastError(), "fork_token_rows launch");
+}

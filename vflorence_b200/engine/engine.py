@@ -358,7 +358,5 @@ class Engine:
             host[0], host[1], host[2], host[3] = res.born_parent, res.born_child, res.born_pos, res.born_token
             dev = self._born_dev[: 4 * nb]
             dev.copy_(self._born_host[: 4 * nb], non_blocking=True)
-            b = dev.view(4, nb).long()
-            self.tokens[b[1]] = self.tokens[b[0]]
-            self.tokens[b[1], b[2]] = b[3].to(torch.int32)
+            paged_ops.fork_token_rows(self.tokens, dev.view(4, nb))
         return self._emit(res)

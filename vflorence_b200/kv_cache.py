@@ -102,6 +102,7 @@ class PagedKVCache:
         self._cross_key = None
         self._cross_staged = None
         self._pairs_host = self._pairs_dev = None
+        self._copy = None  # CopyBlocksTarget over the self-attention pools, made on first use
 
     # ----------------------------------------------------------------------------- binding
     def bind(self, decoder_layers) -> None:
@@ -135,9 +136,14 @@ class PagedKVCache:
             self._pairs_host.numpy()[: 2 * P] = pairs.reshape(-1)
             dev = self._pairs_dev[: 2 * P]
             dev.copy_(self._pairs_host[: 2 * P], non_blocking=True)
-            paged_ops.copy_blocks(self.k_caches, self.v_caches, dev.view(P, 2))
+            self._copy_target().launch(dev, P)
         elif copies:
-            paged_ops.copy_blocks(self.k_caches, self.v_caches, copies)
+            paged_ops.copy_blocks(self._copy_target(), None, copies)
+
+    def _copy_target(self) -> paged_ops.CopyBlocksTarget:
+        if self._copy is None:  # the pools are checked once, not per step
+            self._copy = paged_ops.CopyBlocksTarget(self.k_caches, self.v_caches)
+        return self._copy
 
     # ------------------------------------------------------------------------ encoder pages
     def page_requests(self, request_ids, enc_len: int) -> torch.Tensor:

@@ -252,43 +252,59 @@ def check_copy_pairs_array(pairs, num_blocks: int) -> None:
         raise ValueError("vflorence_b200: copy_blocks sources and destinations must be disjoint")
 
 
+class CopyBlocksTarget:
+    """A fixed set of per-layer K/V caches checked once for copy_blocks, with the pointer arrays
+    the launches take (an engine's pools do not change between steps)."""
+
+    def __init__(self, k_caches, v_caches):
+        k_caches, v_caches = list(k_caches), list(v_caches)
+        if len(k_caches) != len(v_caches) or not k_caches:
+            raise ValueError("vflorence_b200: copy_blocks needs matching, non-empty K and V cache lists")
+        c0 = k_caches[0]
+        self.device = dev = c0.device
+        for c in k_caches + v_caches:
+            _require_cuda("cache", c, dev)
+            if c.shape != c0.shape or c.dtype != c0.dtype or not c.is_contiguous():
+                raise ValueError("vflorence_b200: copy_blocks caches must share one contiguous shape and dtype")
+        self.caches = (k_caches, v_caches)  # keeps the pools alive while the pointers are held
+        self.num_blocks = c0.shape[0]
+        self.block_bytes = c0[0].numel() * c0.element_size()
+        self.chunks = []
+        for start in range(0, len(k_caches), N.MAX_COPY_LAYERS):
+            ks, vs = k_caches[start:start + N.MAX_COPY_LAYERS], v_caches[start:start + N.MAX_COPY_LAYERS]
+            self.chunks.append(((ctypes.c_void_p * len(ks))(*[c.data_ptr() for c in ks]),
+                                (ctypes.c_void_p * len(vs))(*[c.data_ptr() for c in vs]), len(ks)))
+
+    def launch(self, pairs_t: torch.Tensor, num_pairs: int) -> None:
+        """Copy ``num_pairs`` (src, dst) rows of the device int64 tensor ``pairs_t`` [>= P, 2]."""
+        if num_pairs == 0:
+            return
+        lib, stream = N.lib(), _stream(self.device)
+        for kp, vp, n in self.chunks:
+            st = lib.vfl_copy_blocks(kp, vp, n, pairs_t.data_ptr(), num_pairs, self.num_blocks, self.block_bytes,
+                                     stream)
+            N.check(st, "copy_blocks")
+
+
 def copy_blocks(k_caches, v_caches, block_pairs) -> None:
     """For every layer: ``k_caches[l][dst] = k_caches[l][src]`` (and V) for each (src, dst).
 
     ``block_pairs`` is a list of (src, dst) (validated on the host and uploaded) or a device int64
     tensor [P, 2] (validated by the kernel only: out-of-range pairs are skipped and flagged).
-    One launch covers all layers and pairs.
+    One launch covers all layers and pairs. ``k_caches`` may also be a CopyBlocksTarget (then
+    ``v_caches`` is ignored), which skips re-checking the caches.
     """
-    k_caches, v_caches = list(k_caches), list(v_caches)
-    if len(k_caches) != len(v_caches) or not k_caches:
-        raise ValueError("vflorence_b200: copy_blocks needs matching, non-empty K and V cache lists")
-    c0 = k_caches[0]
-    dev = c0.device
-    for c in k_caches + v_caches:
-        _require_cuda("cache", c, dev)
-        if c.shape != c0.shape or c.dtype != c0.dtype or not c.is_contiguous():
-            raise ValueError("vflorence_b200: copy_blocks caches must share one contiguous shape and dtype")
+    target = k_caches if isinstance(k_caches, CopyBlocksTarget) else CopyBlocksTarget(k_caches, v_caches)
+    dev = target.device
     if isinstance(block_pairs, torch.Tensor):
         _require_cuda("block_pairs", block_pairs, dev)
         pairs_t = block_pairs.to(torch.int64).reshape(-1, 2).contiguous()
     else:
-        pairs = check_copy_pairs(block_pairs, c0.shape[0])
+        pairs = check_copy_pairs(block_pairs, target.num_blocks)
         if not pairs:
             return
         pairs_t = torch.tensor(pairs, dtype=torch.int64).pin_memory().to(dev, non_blocking=True)
-    num_pairs = pairs_t.shape[0]
-    if num_pairs == 0:
-        return
-    L = len(k_caches)
-    block_bytes = c0[0].numel() * c0.element_size()
-    lib = N.lib()
-    for start in range(0, L, N.MAX_COPY_LAYERS):
-        ks, vs = k_caches[start:start + N.MAX_COPY_LAYERS], v_caches[start:start + N.MAX_COPY_LAYERS]
-        kp = (ctypes.c_void_p * len(ks))(*[c.data_ptr() for c in ks])
-        vp = (ctypes.c_void_p * len(vs))(*[c.data_ptr() for c in vs])
-        st = lib.vfl_copy_blocks(kp, vp, len(ks), pairs_t.data_ptr(), num_pairs, c0.shape[0], block_bytes,
-                                 _stream(dev))
-        N.check(st, "copy_blocks")
+    target.launch(pairs_t, pairs_t.shape[0])
 
 
 # ---------------------------------------------------------------------------- step metadata
@@ -450,6 +466,23 @@ def beam_merge(values: torch.Tensor, indices: torch.Tensor, groups: torch.Tensor
                                 int(num_groups), int(keep), out.data_ptr(), _stream(dev))
     N.check(st, "beam_merge")
     return out
+
+
+def fork_token_rows(tokens: torch.Tensor, born: torch.Tensor) -> None:
+    """Beam children's token rows in one launch: ``tokens[child] = tokens[parent]`` with
+    ``tokens[child, pos] = token`` for each column of ``born`` (device int32 [4, n]: parents,
+    children, positions, tokens) - Sequence.fork (vflorence/engine/sequence.py:53-55). No child
+    may be a parent in the same call."""
+    dev = tokens.device
+    _require_cuda("tokens", tokens, dev)
+    _require_cuda("born", born, dev)
+    if tokens.dtype != torch.int32 or tokens.dim() != 2 or tokens.stride(1) != 1:
+        raise ValueError("vflorence_b200: tokens must be int32 [rows, width] with unit column stride")
+    if born.dtype != torch.int32 or born.dim() != 2 or born.shape[0] != 4 or not born.is_contiguous():
+        raise ValueError("vflorence_b200: born must be contiguous int32 [4, n]")
+    st = N.lib().vfl_fork_token_rows(tokens.data_ptr(), tokens.stride(0), tokens.shape[0], tokens.shape[1],
+                                     born.data_ptr(), born.shape[1], _stream(dev))
+    N.check(st, "fork_token_rows")
 
 
 def read_device_errors(device: torch.device | int | None = None, clear: bool = True) -> int:
