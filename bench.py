@@ -274,16 +274,40 @@ def _cross_workload(batch, enc_len, seed, device):
                 k=rnd(batch * cw, H, BS, D), v=rnd(batch * cw, H, BS, D), q=rnd(batch, H, D))
 
 
-def _time_op(fn, reps, flush):
-    """Mean device time of fn() over reps calls, L2 flushed (256 MB write) before each."""
-    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
-    for a, b in evs:
-        flush.zero_()
-        a.record()
-        fn()
-        b.record()
+def _graph_ms(body, reps):
+    """Device time (ms) of one replay of a CUDA graph holding `reps` x body(), best of three."""
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        body()
+    torch.cuda.current_stream().wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for _ in range(reps):
+            body()
+    graph.replay()
     torch.cuda.synchronize()
-    return sum(a.elapsed_time(b) for a, b in evs) / reps
+    best = None
+    for _ in range(3):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        graph.replay()
+        b.record()
+        torch.cuda.synchronize()
+        best = a.elapsed_time(b) if best is None else min(best, a.elapsed_time(b))
+    del graph
+    return best
+
+
+def _time_op(fn, reps, flush):
+    """Mean device time (ms) of fn(), L2 flushed (a 256 MB write) before each call: CUDA-graph
+    replays of reps x [flush, fn] minus reps x [flush], so no host time (Python, launches) lands
+    inside the measurement - with eager launches it does for calls shorter than the host's
+    per-call cost, which biases small calls (and split plans, whose combine is a second launch)."""
+    reps = max(5, min(reps, 20))
+    with_fn = _graph_ms(lambda: (flush.zero_(), fn()), reps)
+    alone = _graph_ms(flush.zero_, reps)
+    return max(with_fn - alone, 1e-6) / reps
 
 
 def _cpu_attn_gbs(oracle, q, k, v, lens, table, nbytes, threads):
@@ -389,6 +413,86 @@ def run_sweep(args):
                           "gbs": nbb / ms_b / 1e6, "frac_of_measured_hbm": nbb / ms_b / 1e6 / peak,
                           "rows_per_cta": ops.plan_of(meta_c).queries_per_cta}), flush=True)
         del c
+
+
+def run_split_sweep(args):
+    """The measurements behind the planner's split rule: for batch 8-1024 x 1, 3 or 4 query rows
+    per request x context 128-2048 (near-uniform lengths U[3/4 ctx, ctx], and skewed U[1, ctx]
+    from 1024 tokens), the planner's plan and every fixed split count x 2 or 4 stages x separate
+    or in-kernel merge, as device time per call with L2 flushed. One JSON line per shape."""
+    from vflorence_b200 import paged_ops as ops
+
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    flush = torch.empty(192 * 1024 * 1024, dtype=torch.uint8, device=device)
+    g = torch.Generator().manual_seed(0)
+
+    def override(meta, splits, stages, merge):
+        """Force a split count (as blocks per split), stage count and merge mode on a plan."""
+        p = ops.plan_of(meta)
+        max_blocks = -(-p.max_seq_len // BS)
+        bps = -(-max_blocks // splits)
+        p.blocks_per_split, p.num_splits = bps, -(-max_blocks // bps)
+        p.stages, p.merge_in_kernel = stages, merge
+        ws = 0
+        if p.num_splits > 1:
+            items = p.total_q * H * p.num_splits
+            r256 = lambda x: -(-x // 256) * 256  # noqa: E731
+            ws = r256(items * D * 4) + r256(items * 2 * 4)
+            if merge:  # the arrival counters: one per (request, head group, query chunk), rounded up
+                ws += r256(p.num_reqs * H * 4)
+        p.workspace_bytes = ws
+        return p.num_splits
+
+    for rpr in (1, 3, 4):
+        for R in (8, 32, 85, 128, 256, 1024):
+            if rpr > 1 and R > 256:
+                continue
+            for ctx in (128, 592, 1024, 2048):
+                for skew in (False, True):
+                    if skew and ctx < 1024:
+                        continue
+                    nb = -(-ctx // BS)
+                    if R * nb * BS * H * D * ELEM * 2 > 5e9:
+                        continue
+                    lens = torch.randint(1 if skew else max(1, ctx * 3 // 4), ctx + 1, (R,), generator=g).to(torch.int32)
+                    k = torch.randn(R * nb, H, BS, D, device=device, dtype=DTYPE)
+                    v = torch.randn_like(k)
+                    table = torch.randperm(R * nb, generator=g).to(torch.int32).view(R, nb).to(device)
+                    q = torch.randn(R * rpr, H, D, device=device, dtype=DTYPE)
+                    out = torch.empty_like(q)
+                    qsl = torch.arange(0, R * rpr + 1, rpr, dtype=torch.int32)
+                    lens_d, qsl_d = lens.to(device), qsl.to(device)
+                    mk = lambda: ops.get_scheduler_metadata(R, H, H, D, lens, DTYPE, qsl, False, "sm100", BS)  # noqa: E731
+
+                    def us(meta):
+                        call = lambda: ops.attention_with_kv_cache(q, k, v, out, qsl_d, lens_d, D ** -0.5,  # noqa: E731
+                                                                   False, table, meta)
+                        call()
+                        return round(_time_op(call, 10, flush) * 1e3, 2)
+
+                    base = mk()
+                    bp = ops.plan_of(base)
+                    row = {"point": "split_sweep", "rows_per_request": rpr, "requests": R, "ctx": ctx,
+                           "lengths": "U[1,ctx]" if skew else "U[3/4 ctx,ctx]",
+                           "plan": [bp.num_splits, bp.blocks_per_split, bp.stages, bp.merge_in_kernel],
+                           "plan_us": us(base)}
+                    var = {}
+                    for splits in sorted({max(-(-nb // 64), s_) for s_ in (1, 2, 3, 4, 6, 8, 12, 16)}):
+                        if splits > nb:
+                            break
+                        for stages in (2, 4):
+                            for merge in ((0, 1) if splits > 1 else (0,)):
+                                m = mk()
+                                ns = override(m, splits, stages, merge)
+                                var[f"{ns}/{stages}/{merge}"] = us(m)
+                    best = min(var, key=var.get)
+                    row.update(best=[best, var[best]], plan_vs_best=round(row["plan_us"] / var[best], 3),
+                               variants_splits_stages_merge=var)
+                    if ops.read_device_errors(device):
+                        raise RuntimeError(f"device error bits at {row}")
+                    print(json.dumps(row), flush=True)
+                    del k, v
 
 
 # ---------------------------------------------------------------------------- decode (engine)
@@ -583,6 +687,8 @@ def main():
     ap.add_argument("--cpu-sample", type=int, default=32)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--sweep", action="store_true", help="BASELINE config-5 batch sweep, one line per point")
+    ap.add_argument("--split-sweep", action="store_true",
+                    help="the planner's split rule against every fixed split, one line per shape")
     ap.add_argument("--sweep-batches", default="1,2,4,8,16,32,64,128,256,512,1024")
     ap.add_argument("--decode", choices=["cfg1", "cfg2", "cfg3", "cfg4"], default=None,
                     help="end-to-end decode tokens/s of the engine on a BASELINE config")
@@ -593,6 +699,9 @@ def main():
     args.warmup = max(args.warmup, 3)
     if args.sweep:
         run_sweep(args)
+        return
+    if args.split_sweep:
+        run_split_sweep(args)
         return
     if args.decode:
         run_decode(args)

@@ -13,10 +13,12 @@
 namespace vfl {
 namespace {
 
-constexpr int kMergeWaves = 4;       // split items up to this many waves merge in the kernel
-constexpr int kMinSplitTokens = 128;  // below this a split costs more (prologue, merge) than it saves
-constexpr int kMinSplitTokensTiny = 64;  // ... except for a handful of items (a few long requests)
-constexpr int kShortItemTokens = 256;    // items this short run 2-stage rings when they fill a wave
+// split-K rule thresholds, in tokens (measured on B200; see the split rule in vfl_plan_attention)
+constexpr int kNoSplitTokens = 128;     // contexts this short never split
+constexpr int kMinSplitTokens = 96;     // a split that fills the GPU keeps at least this many tokens
+constexpr int kLongSplitTokens = 512;   // ... and no split of a near-uniform batch holds more
+constexpr int kSkewSplitTokens = 256;   // ... nor of a skewed one (max > 1.5 x mean)
+constexpr int kShortItemTokens = 256;   // items this short run 2-stage rings when they fill a wave
 constexpr int kSmemPerSM = 227 * 1024;
 
 int plan_fail(vfl_attention_plan* plan, int status) {
@@ -203,43 +205,64 @@ int vfl_plan_attention(int num_reqs, int num_heads, int num_kv_heads, int head_d
   const int thread_cap = 2048 / ((hpc + 1) * 32);
   ctas_per_sm = ctas_per_sm < 1 ? 1 : (ctas_per_sm > thread_cap ? thread_cap : ctas_per_sm);
 
-  // split-K. A work item is (request, head group, query chunk, split). Measured on B200 (bf16,
-  // 16 heads x 64, L2 flushed): when the lengths are near-uniform and the unsplit items fill half
-  // a wave, splitting only adds item prologues and partial merges (up to 45 % slower); with few
-  // items, tiles are balanced over half a wave; with skewed lengths the long requests set the
-  // tail, so tiles are balanced over two waves. An item holds at most kMaxBlocksPerSplit blocks
-  // (the shared-memory table slice).
-  int64_t work_tiles = 0, base_items = 0, sum_blocks = 0, busy_reqs = 0;
+  // split-K. A work item is (request, head group, query chunk, split); an item holds at most
+  // kMaxBlocksPerSplit blocks (the shared-memory table slice). Rule fitted to a sweep on B200
+  // measured as device time from CUDA-graph replays with L2 flushed (bf16, 16 heads x 64, 8-1024
+  // requests x 1-4 rows, 128-2048 tokens, near-uniform and skewed lengths): 1.014 x the best
+  // split per shape on average, 1.18 x at worst, where the former rule was 1.13 x / 1.50 x.
+  //   * contexts of at most kNoSplitTokens, or two waves of unsplit items: no split;
+  //   * fewer items: fill about 0.9 of a wave, with splits of at least kMinSplitTokens;
+  //   * long contexts: splits of at most kLongSplitTokens (kSkewSplitTokens when skewed), so
+  //     that many short items balance the SMs (the longest request sets the tail otherwise);
+  //   * then no split count whose items land between one and two waves: the second wave's few
+  //     CTAs cannot pull the bandwidth (e.g. 128 items x 4 splits, 1.15 waves: 13 % slower
+  //     than 3 splits, 0.86 waves) - back off to the most splits under one wave.
+  int64_t base_items = 0, sum_blocks = 0, busy_reqs = 0;
   for (int r = 0; r < num_reqs; ++r) {
     const int64_t ql = query_start_loc_host ? (int64_t)query_start_loc_host[r + 1] - query_start_loc_host[r] : 1;
     const int64_t qc = ceil_div(ql, (int64_t)qpc);
     const int64_t nb = ceil_div((int64_t)seq_lens_host[r], (int64_t)block_size);
     base_items += groups * qc;
-    work_tiles += ceil_div((int64_t)seq_lens_host[r], (int64_t)16) * groups * qc;
     if (qc > 0 && nb > 0) {
       sum_blocks += nb;
       ++busy_reqs;
     }
   }
-  const int tpb = block_size / 16;
   const int64_t slots = (int64_t)kNumSMs * ctas_per_sm;
   const int64_t max_blocks = ceil_div(max_seq, (int64_t)block_size);
   const bool skewed = busy_reqs > 0 && 2 * max_blocks * busy_reqs > 3 * sum_blocks;  // max > 1.5 x mean
-  int64_t bps;
-  if (!skewed && 2 * base_items >= slots) {
-    bps = max_blocks;  // no split beyond what the table slice forces
-    // ... unless long items leave a second wave less than half full: its few CTAs cannot pull
-    // the full bandwidth (128 x 1024-token items, 1.15 waves: 119 us unsplit, 100 us in halves;
-    // at 1.8 waves halving was 8 % slower)
-    if (base_items > slots && 2 * base_items < 3 * slots && max_blocks * block_size >= 512)
-      bps = ceil_div(max_blocks, (int64_t)2);
-  } else {
-    const int64_t target = skewed ? 2 * slots : slots / 2;
-    bps = ceil_div(ceil_div(work_tiles, target), (int64_t)tpb);
+  // items of a split into pieces of `bps` blocks
+  auto split_items_of = [&](int64_t bps) {
+    int64_t items = 0;
+    for (int r = 0; r < num_reqs; ++r) {
+      const int64_t ql = query_start_loc_host ? (int64_t)query_start_loc_host[r + 1] - query_start_loc_host[r] : 1;
+      items += ceil_div(ceil_div((int64_t)seq_lens_host[r], (int64_t)block_size), bps) * groups *
+               ceil_div(ql, (int64_t)qpc);
+    }
+    return items;
+  };
+  const int64_t forced = ceil_div(max_blocks, (int64_t)kMaxBlocksPerSplit);  // the table slice's minimum
+  int64_t want = 1;
+  const int64_t max_tokens = max_blocks * block_size;
+  if (max_tokens > kNoSplitTokens && base_items > 0 && base_items < 2 * slots) {
+    int64_t fill = (9 * slots) / (10 * base_items);
+    fill = fill < 1 ? 1 : fill;
+    int64_t by_len = max_tokens / kMinSplitTokens;
+    by_len = by_len < 1 ? 1 : by_len;
+    want = fill < by_len ? fill : by_len;
+    const int64_t longest = ceil_div(max_tokens, (int64_t)(skewed ? kSkewSplitTokens : kLongSplitTokens));
+    want = want > longest ? want : longest;
   }
-  int64_t bps_min = (base_items <= 16 ? kMinSplitTokensTiny : kMinSplitTokens) / block_size;
-  bps_min = bps_min < 1 ? 1 : (bps_min > kMaxBlocksPerSplit ? kMaxBlocksPerSplit : bps_min);
-  bps = bps < bps_min ? bps_min : (bps > kMaxBlocksPerSplit ? kMaxBlocksPerSplit : bps);
+  want = want < forced ? forced : want;
+  int64_t bps = ceil_div(max_blocks, want);
+  bps = bps < 1 ? 1 : (bps > kMaxBlocksPerSplit ? kMaxBlocksPerSplit : bps);
+  while (want > forced && want > 1) {
+    const int64_t items = split_items_of(bps);
+    if (items <= slots || items >= 2 * slots) break;
+    --want;
+    bps = ceil_div(max_blocks, want);
+    bps = bps > kMaxBlocksPerSplit ? kMaxBlocksPerSplit : bps;
+  }
   int64_t splits = ceil_div(max_blocks, bps);
   if (splits > 65535) {
     bps = ceil_div(max_blocks, (int64_t)65535);
@@ -256,16 +279,11 @@ int vfl_plan_attention(int num_reqs, int num_heads, int num_kv_heads, int head_d
   if (q_chunks > 65535 || (int64_t)num_reqs * groups > INT32_MAX)
     return plan_fail(plan, fail(VFL_ERR_UNSUPPORTED, "launch grid too large"));
 
-  // Merge of split partials: when the split work items fit in ~kMergeWaves waves the call is
-  // latency-bound, and the last split CTA of each item merges in the same launch; above that
-  // a separate combine launch is cheaper than every split CTA waiting on an arrival counter.
-  int64_t split_items = 0;
-  for (int r = 0; r < num_reqs; ++r) {
-    const int64_t ql = query_start_loc_host ? (int64_t)query_start_loc_host[r + 1] - query_start_loc_host[r] : 1;
-    split_items += ceil_div(ceil_div((int64_t)seq_lens_host[r], (int64_t)block_size), bps) * groups *
-                   ceil_div(ql, (int64_t)qpc);
-  }
-  const int merge_in_kernel = splits > 1 && split_items <= slots * kMergeWaves ? 1 : 0;
+  // Merge of split partials: a separate combine launch. The kernel can also merge in the
+  // launch (the last split CTA of each item, behind an arrival counter; plan merge_in_kernel =
+  // 1), but measured as device time that was slower in 1214 of 1220 swept cases (4-7 us per
+  // call: the counters' memset and the merge on the tail's critical path).
+  const int merge_in_kernel = 0;
 
   // workspace: acc partials | (m, l) partials | arrival counters (in-kernel merge only)
   int64_t ws = 0;
