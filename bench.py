@@ -419,7 +419,8 @@ def run_split_sweep(args):
     """The measurements behind the planner's split rule: for batch 8-1024 x 1, 3 or 4 query rows
     per request x context 128-2048 (near-uniform lengths U[3/4 ctx, ctx], and skewed U[1, ctx]
     from 1024 tokens), the planner's plan and every fixed split count x 2 or 4 stages x separate
-    or in-kernel merge, as device time per call with L2 flushed. One JSON line per shape."""
+    or in-kernel merge; then 16-512 requests at 3072-4096 tokens against split counts 4-24 (4
+    stages, separate merge). Device time per call with L2 flushed. One JSON line per shape."""
     from vflorence_b200 import paged_ops as ops
 
     device = torch.device("cuda", 0)
@@ -444,55 +445,61 @@ def run_split_sweep(args):
         p.workspace_bytes = ws
         return p.num_splits
 
+    shapes = []  # (rows per request, requests, context, skewed, long): long shapes sweep fewer variants
     for rpr in (1, 3, 4):
         for R in (8, 32, 85, 128, 256, 1024):
             if rpr > 1 and R > 256:
                 continue
             for ctx in (128, 592, 1024, 2048):
                 for skew in (False, True):
-                    if skew and ctx < 1024:
-                        continue
-                    nb = -(-ctx // BS)
-                    if R * nb * BS * H * D * ELEM * 2 > 5e9:
-                        continue
-                    lens = torch.randint(1 if skew else max(1, ctx * 3 // 4), ctx + 1, (R,), generator=g).to(torch.int32)
-                    k = torch.randn(R * nb, H, BS, D, device=device, dtype=DTYPE)
-                    v = torch.randn_like(k)
-                    table = torch.randperm(R * nb, generator=g).to(torch.int32).view(R, nb).to(device)
-                    q = torch.randn(R * rpr, H, D, device=device, dtype=DTYPE)
-                    out = torch.empty_like(q)
-                    qsl = torch.arange(0, R * rpr + 1, rpr, dtype=torch.int32)
-                    lens_d, qsl_d = lens.to(device), qsl.to(device)
-                    mk = lambda: ops.get_scheduler_metadata(R, H, H, D, lens, DTYPE, qsl, False, "sm100", BS)  # noqa: E731
+                    if not (skew and ctx < 1024):
+                        shapes.append((rpr, R, ctx, skew, False))
+    shapes += [(1, R, ctx, skew, True) for R in (16, 32, 64, 128, 256, 512) for ctx in (3072, 4096)
+               for skew in (False, True)]
+    shapes += [(3, 32, 4096, True, True), (3, 85, 4096, True, True)]
+    for rpr, R, ctx, skew, long_ctx in shapes:
+        nb = -(-ctx // BS)
+        if R * nb * BS * H * D * ELEM * 2 > (9e9 if long_ctx else 5e9):
+            continue
+        lens = torch.randint(1 if skew else max(1, ctx * 3 // 4), ctx + 1, (R,), generator=g).to(torch.int32)
+        k = torch.randn(R * nb, H, BS, D, device=device, dtype=DTYPE)
+        v = torch.randn_like(k)
+        table = torch.randperm(R * nb, generator=g).to(torch.int32).view(R, nb).to(device)
+        q = torch.randn(R * rpr, H, D, device=device, dtype=DTYPE)
+        out = torch.empty_like(q)
+        qsl = torch.arange(0, R * rpr + 1, rpr, dtype=torch.int32)
+        lens_d, qsl_d = lens.to(device), qsl.to(device)
+        mk = lambda: ops.get_scheduler_metadata(R, H, H, D, lens, DTYPE, qsl, False, "sm100", BS)  # noqa: E731
 
-                    def us(meta):
-                        call = lambda: ops.attention_with_kv_cache(q, k, v, out, qsl_d, lens_d, D ** -0.5,  # noqa: E731
-                                                                   False, table, meta)
-                        call()
-                        return round(_time_op(call, 10, flush) * 1e3, 2)
+        def us(meta):
+            call = lambda: ops.attention_with_kv_cache(q, k, v, out, qsl_d, lens_d, D ** -0.5,  # noqa: E731
+                                                       False, table, meta)
+            call()
+            return round(_time_op(call, 10, flush) * 1e3, 2)
 
-                    base = mk()
-                    bp = ops.plan_of(base)
-                    row = {"point": "split_sweep", "rows_per_request": rpr, "requests": R, "ctx": ctx,
-                           "lengths": "U[1,ctx]" if skew else "U[3/4 ctx,ctx]",
-                           "plan": [bp.num_splits, bp.blocks_per_split, bp.stages, bp.merge_in_kernel],
-                           "plan_us": us(base)}
-                    var = {}
-                    for splits in sorted({max(-(-nb // 64), s_) for s_ in (1, 2, 3, 4, 6, 8, 12, 16)}):
-                        if splits > nb:
-                            break
-                        for stages in (2, 4):
-                            for merge in ((0, 1) if splits > 1 else (0,)):
-                                m = mk()
-                                ns = override(m, splits, stages, merge)
-                                var[f"{ns}/{stages}/{merge}"] = us(m)
-                    best = min(var, key=var.get)
-                    row.update(best=[best, var[best]], plan_vs_best=round(row["plan_us"] / var[best], 3),
-                               variants_splits_stages_merge=var)
-                    if ops.read_device_errors(device):
-                        raise RuntimeError(f"device error bits at {row}")
-                    print(json.dumps(row), flush=True)
-                    del k, v
+        base = mk()
+        bp = ops.plan_of(base)
+        row = {"point": "split_sweep", "rows_per_request": rpr, "requests": R, "ctx": ctx,
+               "lengths": "U[1,ctx]" if skew else "U[3/4 ctx,ctx]",
+               "plan": [bp.num_splits, bp.blocks_per_split, bp.stages, bp.merge_in_kernel],
+               "plan_us": us(base)}
+        var = {}
+        counts = (4, 5, 6, 8, 10, 12, 16, 24) if long_ctx else (1, 2, 3, 4, 6, 8, 12, 16)
+        for splits in sorted({max(-(-nb // 64), s_) for s_ in counts}):
+            if splits > nb:
+                break
+            for stages in ((4,) if long_ctx else (2, 4)):
+                for merge in ((0, 1) if splits > 1 and not long_ctx else (0,)):
+                    m = mk()
+                    ns = override(m, splits, stages, merge)
+                    var[f"{ns}/{stages}/{merge}"] = us(m)
+        best = min(var, key=var.get)
+        row.update(best=[best, var[best]], plan_vs_best=round(row["plan_us"] / var[best], 3),
+                   variants_splits_stages_merge=var)
+        if ops.read_device_errors(device):
+            raise RuntimeError(f"device error bits at {row}")
+        print(json.dumps(row), flush=True)
+        del k, v
 
 
 # ---------------------------------------------------------------------------- decode (engine)

@@ -17,7 +17,7 @@ namespace {
 constexpr int kNoSplitTokens = 128;     // contexts this short never split
 constexpr int kMinSplitTokens = 96;     // a split that fills the GPU keeps at least this many tokens
 constexpr int kLongSplitTokens = 512;   // ... and no split of a near-uniform batch holds more
-constexpr int kSkewSplitTokens = 256;   // ... nor of a skewed one (max > 1.5 x mean)
+constexpr int kSkewSplitTokens = 320;   // skewed lengths (max > 1.5 x mean): pieces of at least this
 constexpr int kShortItemTokens = 256;   // items this short run 2-stage rings when they fill a wave
 constexpr int kSmemPerSM = 227 * 1024;
 
@@ -206,17 +206,20 @@ int vfl_plan_attention(int num_reqs, int num_heads, int num_kv_heads, int head_d
   ctas_per_sm = ctas_per_sm < 1 ? 1 : (ctas_per_sm > thread_cap ? thread_cap : ctas_per_sm);
 
   // split-K. A work item is (request, head group, query chunk, split); an item holds at most
-  // kMaxBlocksPerSplit blocks (the shared-memory table slice). Rule fitted to a sweep on B200
+  // kMaxBlocksPerSplit blocks (the shared-memory table slice). Rule fitted to sweeps on B200
   // measured as device time from CUDA-graph replays with L2 flushed (bf16, 16 heads x 64, 8-1024
-  // requests x 1-4 rows, 128-2048 tokens, near-uniform and skewed lengths): 1.014 x the best
-  // split per shape on average, 1.18 x at worst, where the former rule was 1.13 x / 1.50 x.
-  //   * contexts of at most kNoSplitTokens, or two waves of unsplit items: no split;
+  // requests x 1-4 rows, 128-4096 tokens, near-uniform and skewed lengths; 120 shapes): 1.016 x
+  // the best split per shape on average, where the former rule was 1.11 x. (A 640-token cap
+  // scored 1.018 x but left 592-token encoder contexts unsplit, 6-10 % slower at 128 requests.)
+  //   * contexts of at most kNoSplitTokens, or three waves of unsplit items: no split;
   //   * fewer items: fill about 0.9 of a wave, with splits of at least kMinSplitTokens;
-  //   * long contexts: splits of at most kLongSplitTokens (kSkewSplitTokens when skewed), so
-  //     that many short items balance the SMs (the longest request sets the tail otherwise);
-  //   * then no split count whose items land between one and two waves: the second wave's few
-  //     CTAs cannot pull the bandwidth (e.g. 128 items x 4 splits, 1.15 waves: 13 % slower
-  //     than 3 splits, 0.86 waves) - back off to the most splits under one wave.
+  //   * near-uniform long contexts: splits of at most kLongSplitTokens, so that many short items
+  //     balance the SMs (the longest requests set the tail otherwise); skewed lengths: pieces
+  //     of the total work over 1.5 waves (at least kSkewSplitTokens), whatever the fill;
+  //   * then, for near-uniform lengths, no split count whose items land between one and two
+  //     waves: the second wave's few CTAs cannot pull the bandwidth (e.g. 128 items x 4 splits,
+  //     1.15 waves: 13 % slower than 3 splits, 0.86 waves) - back off to the most splits under
+  //     one wave. Skewed items are no clean partial wave; there backing off cost up to 13 %.
   int64_t base_items = 0, sum_blocks = 0, busy_reqs = 0;
   for (int r = 0; r < num_reqs; ++r) {
     const int64_t ql = query_start_loc_host ? (int64_t)query_start_loc_host[r + 1] - query_start_loc_host[r] : 1;
@@ -244,19 +247,30 @@ int vfl_plan_attention(int num_reqs, int num_heads, int num_kv_heads, int head_d
   const int64_t forced = ceil_div(max_blocks, (int64_t)kMaxBlocksPerSplit);  // the table slice's minimum
   int64_t want = 1;
   const int64_t max_tokens = max_blocks * block_size;
-  if (max_tokens > kNoSplitTokens && base_items > 0 && base_items < 2 * slots) {
+  if (max_tokens > kNoSplitTokens && base_items > 0 && base_items < 3 * slots) {
     int64_t fill = (9 * slots) / (10 * base_items);
     fill = fill < 1 ? 1 : fill;
     int64_t by_len = max_tokens / kMinSplitTokens;
     by_len = by_len < 1 ? 1 : by_len;
     want = fill < by_len ? fill : by_len;
-    const int64_t longest = ceil_div(max_tokens, (int64_t)(skewed ? kSkewSplitTokens : kLongSplitTokens));
+    int64_t piece_tokens = kLongSplitTokens;
+    if (skewed) {  // the work in tokens of all items, over 1.5 waves
+      int64_t work = 0;
+      for (int r = 0; r < num_reqs; ++r) {
+        const int64_t ql = query_start_loc_host ? (int64_t)query_start_loc_host[r + 1] - query_start_loc_host[r] : 1;
+        work += ceil_div((int64_t)seq_lens_host[r], (int64_t)block_size) * block_size * groups *
+                ceil_div(ql, (int64_t)qpc);
+      }
+      piece_tokens = ceil_div(2 * work, 3 * slots);
+      piece_tokens = piece_tokens < kSkewSplitTokens ? kSkewSplitTokens : piece_tokens;
+    }
+    const int64_t longest = ceil_div(max_tokens, piece_tokens);
     want = want > longest ? want : longest;
   }
   want = want < forced ? forced : want;
   int64_t bps = ceil_div(max_blocks, want);
   bps = bps < 1 ? 1 : (bps > kMaxBlocksPerSplit ? kMaxBlocksPerSplit : bps);
-  while (want > forced && want > 1) {
+  while (!skewed && want > forced && want > 1) {  // skewed items are no clean partial wave
     const int64_t items = split_items_of(bps);
     if (items <= slots || items >= 2 * slots) break;
     --want;

@@ -135,11 +135,12 @@ def get_scheduler_metadata(num_reqs: int, num_heads: int, num_kv_heads: int, hea
 
 
 def plan_of(metadata: torch.Tensor) -> N.AttentionPlan:
-    """View the plan struct stored in a metadata tensor (no copy)."""
+    """View the plan struct stored in a metadata tensor (no copy; the view keeps the tensor's
+    memory alive, so ``plan_of(get_scheduler_metadata(...))`` is safe)."""
     if (metadata.device.type != "cpu" or metadata.dtype != torch.int64 or not metadata.is_contiguous()
             or metadata.numel() * 8 < N.PLAN_BYTES):
         raise ValueError("vflorence_b200: scheduler_metadata must come from get_scheduler_metadata")
-    plan = N.AttentionPlan.from_address(metadata.data_ptr())
+    plan = N.AttentionPlan.from_buffer(metadata.numpy())  # holds the array, which holds the tensor
     if plan.magic != N.PLAN_MAGIC:
         raise ValueError("vflorence_b200: scheduler_metadata must come from get_scheduler_metadata")
     return plan
