@@ -152,6 +152,28 @@ int vfl_attention_with_kv_cache(const vfl_attention_plan* plan, const void* quer
                                 int64_t table_stride, int32_t table_cols, float scale,
                                 void* workspace, size_t workspace_bytes, void* stream);
 
+/* replaces the two calls of the decoder's self-attention op, vllm_cpu_attn.reshape_and_cache
+ *   then vllm_cpu_attn.attention_with_kv_cache (vflorence/layers/attention.py:55-72), with one
+ *   launch: query row t brings one new token, key / value [num_heads, head_dim] dense at key +
+ *   t * key_token_stride (elements), written to slot_mapping[t] (negative: none; past the pool:
+ *   skipped and flagged VFL_DEVERR_SLOT) before the attention reads it. The token is the newest
+ *   position of its sequence (seq_lens - 1), or for causal rows the successive positions ending
+ *   there. Otherwise as vfl_attention_with_kv_cache; the slot's block must be the row's own (not
+ *   shared with another row of the call, as after copy-on-write). Plans where
+ *   vfl_attention_append_supported is 0 get VFL_ERR_UNSUPPORTED: then append, then attend. */
+int vfl_attention_with_kv_cache_append(const vfl_attention_plan* plan, const void* query,
+                                       int64_t query_token_stride, const void* key, int64_t key_token_stride,
+                                       const void* value, int64_t value_token_stride,
+                                       const int64_t* slot_mapping, const void* k_cache, const void* v_cache,
+                                       int64_t num_blocks, void* output, int64_t output_token_stride,
+                                       const int32_t* query_start_loc, const int32_t* seq_lens,
+                                       const int32_t* block_table, int64_t table_stride, int32_t table_cols,
+                                       float scale, void* workspace, size_t workspace_bytes, void* stream);
+
+/* 1 when vfl_attention_with_kv_cache_append takes this plan: the tensor-core kernel (bf16,
+ * head_dim 64) and one new token per query row (causal, row tables, or one row per request). */
+int vfl_attention_append_supported(const vfl_attention_plan* plan);
+
 /* No counterpart in the reference (vllm_cpu_attn allocates on the host heap as it likes).
  * The same attention as vfl_attention_with_kv_cache, for callers that cannot allocate device
  * memory - a C/C++ or FFI host without a device allocator of its own, where every scratch

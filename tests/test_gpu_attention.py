@@ -341,3 +341,130 @@ def test_row_tables_refused_where_not_built():
         o.get_scheduler_metadata(2, 16, 16, 64, lens, torch.float32, qsl, False, "sm100", 16, row_tables=True)
     with pytest.raises(ValueError, match="causal"):
         o.get_scheduler_metadata(2, 16, 16, 64, lens, torch.bfloat16, qsl, True, "sm100", 16, row_tables=True)
+
+
+# ------------------------------------------------------------- fused KV append + attention
+
+def _appended_case(kind, seed, block_size, max_len, requests):
+    """Pools, tables and one step's new tokens: every query row appends its newest token into
+    a block of its own (after copy-on-write no row shares the block it writes)."""
+    g = torch.Generator().manual_seed(seed)
+    gd = torch.Generator(device=DEV).manual_seed(seed)
+    H, D = 16, 64
+    if kind == "beams":
+        counts = [int(torch.randint(1, 5, (1,), generator=g)) for _ in range(requests)]
+    elif kind == "causal":
+        counts = [int(torch.randint(1, 9, (1,), generator=g)) for _ in range(requests)]
+    else:
+        counts = [1] * requests
+    lens = torch.randint(1, max_len + 1, (requests,), generator=g, dtype=torch.int32)
+    lens[::5] = torch.tensor([block_size * k + 1 for k in range(1, 1 + len(lens[::5]))], dtype=torch.int32)[
+        : len(lens[::5])].clamp(max=max_len)  # some new tokens open a block
+    if kind == "causal":
+        lens = torch.maximum(lens, torch.tensor(counts, dtype=torch.int32))
+    nbs = [math.ceil(int(n) / block_size) for n in lens]
+    rows = sum(counts) if kind == "beams" else requests
+    width = max(nbs)
+    table = torch.zeros(rows, width, dtype=torch.int32)
+    nxt, row = 0, 0
+    for r, (c, nb) in enumerate(zip(counts, nbs)):
+        base = torch.arange(nxt, nxt + nb, dtype=torch.int32)
+        nxt += nb
+        for b in range(c if kind == "beams" else 1):
+            t = base.clone()
+            if b:  # a forked beam: shared prefix, own blocks from a random point, always its own last
+                first = int(torch.randint(0, nb, (1,), generator=g))
+                for j in range(first, nb):
+                    t[j] = nxt
+                    nxt += 1
+            table[row, :nb] = t
+            row += 1
+    pool = nxt + 4
+    perm = torch.randperm(pool, generator=g).to(torch.int32)
+    table = perm[table.long()]
+    kc = torch.randn(pool, H, block_size, D, generator=gd, device=DEV, dtype=torch.bfloat16)
+    vc = torch.randn_like(kc)
+    qsl = torch.tensor([0] + torch.tensor(counts).cumsum(0).tolist(), dtype=torch.int32)
+    nq = int(qsl[-1])
+    # the new tokens' slots: row i's newest position (causal: the request's last counts[r] positions)
+    slots = torch.empty(nq, dtype=torch.int64)
+    for r in range(requests):
+        for j in range(int(qsl[r]), int(qsl[r + 1])):
+            trow = j if kind == "beams" else r
+            pos = int(lens[r]) - 1 if kind != "causal" else int(lens[r]) - (int(qsl[r + 1]) - j)
+            slots[j] = int(table[trow, pos // block_size]) * block_size + pos % block_size
+    fused = torch.randn(nq, 3 * H * D, generator=gd, device=DEV, dtype=torch.bfloat16)  # a q/k/v projection
+    q, key, value = (x.reshape(nq, H, D) for x in fused.chunk(3, dim=-1))
+    return q, key, value, kc, vc, qsl, lens, table, slots
+
+
+@pytest.mark.parametrize("kind,seed,block_size,max_len,requests", [
+    ("rows", 1, 16, 200, 40), ("rows", 2, 16, 4000, 9), ("rows", 3, 32, 1500, 17),
+    ("beams", 4, 16, 300, 30), ("beams", 5, 16, 3000, 6), ("causal", 6, 16, 600, 12), ("causal", 7, 32, 2000, 5)])
+def test_attention_append_equals_append_then_attend(kind, seed, block_size, max_len, requests):
+    """One launch that stores each row's new K/V and attends over it gives the output and the
+    pools of reshape_and_cache followed by attention_with_kv_cache, bit for bit (the same plan
+    reads the same bytes); long contexts exercise the split that holds the new position."""
+    o = ops()
+    q, key, value, kc, vc, qsl, lens, table, slots = _appended_case(kind, seed, block_size, max_len, requests)
+    n, h, bs, d = kc.shape
+    causal = kind == "causal"
+    meta = o.get_scheduler_metadata(requests, h, h, d, lens, torch.bfloat16, qsl, causal, "sm100", bs,
+                                    row_tables=kind == "beams")
+    assert o.attention_append_supported(meta)
+    dq, dl, dt, ds = qsl.to(DEV), lens.to(DEV), table.to(DEV), slots.to(DEV)
+    kc2, vc2 = kc.clone(), vc.clone()
+    o.reshape_and_cache(key, value, kc2, vc2, ds)
+    want = torch.full(q.shape, float("nan"), dtype=q.dtype, device=DEV)
+    o.attention_with_kv_cache(q, kc2, vc2, want, dq, dl, d ** -0.5, causal, dt, meta)
+    got = torch.full(q.shape, float("nan"), dtype=q.dtype, device=DEV)
+    o.attention_with_kv_cache_append(q, key, value, kc, vc, got, ds, dq, dl, d ** -0.5, causal, dt, meta)
+    torch.cuda.synchronize()
+    assert o.read_device_errors(DEV) == 0
+    assert torch.equal(kc, kc2) and torch.equal(vc, vc2)
+    assert torch.equal(got, want)
+    if max_len >= 3000:
+        assert o.plan_of(meta).num_splits > 1
+
+
+def test_attention_append_skips_padding_and_flags_bad_slots():
+    o = ops()
+    q, key, value, kc, vc, qsl, lens, table, slots = _appended_case("rows", 8, 16, 100, 6)
+    n, h, bs, d = kc.shape
+    lens[2] = 0          # a padding row: no token, no write
+    slots[2] = -1
+    slots[4] = n * bs    # one past the pool: skipped and flagged
+    meta = o.get_scheduler_metadata(6, h, h, d, lens, torch.bfloat16, qsl, False, "sm100", bs)
+    before_k, before_v = kc.clone(), vc.clone()
+    out = torch.empty_like(q)
+    o.attention_with_kv_cache_append(q, key, value, kc, vc, out, slots.to(DEV), qsl.to(DEV), lens.to(DEV),
+                                     d ** -0.5, False, table.to(DEV), meta)
+    from vflorence_b200 import _native
+
+    assert o.read_device_errors(DEV) & _native.DEVERR_SLOT
+    want_k, want_v = before_k.clone(), before_v.clone()
+    keep = torch.tensor([i not in (2, 4) for i in range(6)])
+    o.reshape_and_cache(key[keep.to(DEV)], value[keep.to(DEV)], want_k, want_v, slots[keep].to(DEV))
+    assert torch.equal(kc, want_k) and torch.equal(vc, want_v)
+    assert bool((out[2] == 0).all())  # a row with no tokens gives zeros
+
+
+def test_attention_append_refused_where_not_built():
+    o = ops()
+    from vflorence_b200._native import VflError
+
+    lens = torch.tensor([10, 20], dtype=torch.int32)
+    f32 = o.get_scheduler_metadata(2, 16, 16, 64, lens, torch.float32, None, False, "sm100", 16)
+    assert not o.attention_append_supported(f32)
+    # several non-causal rows sharing one table would all write its newest position
+    grouped = o.get_scheduler_metadata(2, 16, 16, 64, lens, torch.bfloat16, torch.tensor([0, 2, 4], dtype=torch.int32),
+                                       False, "sm100", 16)
+    assert not o.attention_append_supported(grouped)
+    kc = torch.zeros(4, 16, 16, 64, device=DEV, dtype=torch.bfloat16)
+    q = torch.zeros(4, 16, 64, device=DEV, dtype=torch.bfloat16)
+    with pytest.raises(VflError, match="attention_append"):
+        o.attention_with_kv_cache_append(q, q, q, kc, kc.clone(), torch.empty_like(q),
+                                         torch.zeros(4, dtype=torch.int64, device=DEV),
+                                         torch.tensor([0, 2, 4], dtype=torch.int32, device=DEV),
+                                         lens.to(DEV), 0.125, False, torch.zeros(2, 2, dtype=torch.int32, device=DEV),
+                                         grouped)

@@ -46,6 +46,8 @@ EXPORTS = (
     "vfl_plan_attention_row_tables",
     "vfl_reshape_and_cache",
     "vfl_attention_with_kv_cache",
+    "vfl_attention_with_kv_cache_append",
+    "vfl_attention_append_supported",
     "vfl_attention_with_kv_cache_no_alloc",
     "vfl_copy_blocks",
     "vfl_prepare_decode",
@@ -166,6 +168,9 @@ def _declare(L):
         "vfl_reshape_and_cache": (i32, [vp, vp, vp, vp, vp, i64, i32, i32, i32, i64, i64, i64, i32, vp]),
         "vfl_attention_with_kv_cache": (i32, [vp, vp, i64, vp, vp, i64, vp, i64, vp, vp, vp, i64, i32,
                                               f32, vp, sz, vp]),
+        "vfl_attention_with_kv_cache_append": (i32, [plan_p, vp, i64, vp, i64, vp, i64, vp, vp, vp, i64, vp, i64, vp,
+                                                     vp, vp, i64, i32, f32, vp, sz, vp]),
+        "vfl_attention_append_supported": (i32, [plan_p]),
         "vfl_attention_with_kv_cache_no_alloc": (i32, [plan_p, vp, i64, vp, vp, i64, vp, i64, vp, vp, vp,
                                                        i64, i32, f32, vp]),
         "vfl_copy_blocks": (i32, [vp, vp, i32, vp, i32, i64, i64, vp]),

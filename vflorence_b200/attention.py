@@ -68,9 +68,10 @@ def stage_cross(layers, pages, enc_lens, block_size: int, isa: str):
 @torch.library.custom_op("vflorence::self_attention", mutates_args={"k_cache", "v_cache"})
 def decoder_self_attention(query: torch.Tensor, key: torch.Tensor, value: torch.Tensor,
                            k_cache: torch.Tensor, v_cache: torch.Tensor, scale: float) -> torch.Tensor:
-    """Write this step's K/V into the paged cache, then attend over each sequence's cache."""
+    """Write this step's K/V into the paged cache, then attend over each sequence's cache - in
+    one launch where the plan allows it (the tensor-core kernel stores each row's new K/V ahead
+    of reading its last block), else the append kernel and then the attention."""
     ctx = get_context()
-    paged_ops.reshape_and_cache(key, value, k_cache, v_cache, ctx.slot_mapping, isa=ctx.isa)
     out = torch.empty_like(query)
     # causal=False is still causal: each sequence queries only its newest token, and the cache
     # holds nothing after it.
@@ -78,6 +79,12 @@ def decoder_self_attention(query: torch.Tensor, key: torch.Tensor, value: torch.
         qsl, lens = ctx.self_groups, ctx.self_group_lens
     else:
         qsl, lens = ctx.query_start_loc, ctx.context_lens
+    if paged_ops.attention_append_supported(ctx.self_metadata):
+        paged_ops.attention_with_kv_cache_append(query, key, value, k_cache, v_cache, out, ctx.slot_mapping, qsl,
+                                                 lens, scale=scale, causal=False, block_table=ctx.block_tables,
+                                                 scheduler_metadata=ctx.self_metadata)
+        return out
+    paged_ops.reshape_and_cache(key, value, k_cache, v_cache, ctx.slot_mapping, isa=ctx.isa)
     paged_ops.attention_with_kv_cache(query, k_cache, v_cache, out, qsl, lens, scale=scale, causal=False,
                                       block_table=ctx.block_tables, scheduler_metadata=ctx.self_metadata)
     return out

@@ -343,13 +343,24 @@ int vfl_plan_attention_row_tables(int num_reqs, int num_heads, int num_kv_heads,
   return VFL_OK;
 }
 
-int vfl_attention_with_kv_cache(const vfl_attention_plan* plan, const void* query,
-                                int64_t query_token_stride, const void* k_cache,
-                                const void* v_cache, int64_t num_blocks, void* output,
-                                int64_t output_token_stride, const int32_t* query_start_loc,
-                                const int32_t* seq_lens, const int32_t* block_table,
-                                int64_t table_stride, int32_t table_cols, float scale,
-                                void* workspace, size_t workspace_bytes, void* stream) {
+}  // extern "C"
+
+namespace {
+
+// The tokens a fused call appends: query row t's key / value rows and its slot.
+struct AppendSource {
+  const void* key;
+  int64_t key_stride;
+  const void* value;
+  int64_t value_stride;
+  const int64_t* slots;
+};
+
+int attention_run(const vfl_attention_plan* plan, const void* query, int64_t query_token_stride, const void* k_cache,
+                  const void* v_cache, int64_t num_blocks, void* output, int64_t output_token_stride,
+                  const int32_t* query_start_loc, const int32_t* seq_lens, const int32_t* block_table,
+                  int64_t table_stride, int32_t table_cols, float scale, void* workspace, size_t workspace_bytes,
+                  void* stream, const AppendSource* append) {
   if (plan == nullptr || plan->magic != VFL_PLAN_MAGIC)
     return fail(VFL_ERR_INVALID_ARGUMENT, "attention: plan missing or not built by vfl_plan_attention");
   int st0 = check_attention_plan(plan);
@@ -400,6 +411,13 @@ int vfl_attention_with_kv_cache(const vfl_attention_plan* plan, const void* quer
   p.max_seq_len = plan->max_seq_len;
   p.row_tables = plan->row_tables;
   p.scale_log2 = scale * 1.4426950408889634f;
+  if (append != nullptr) {
+    p.new_k = append->key;
+    p.new_k_stride = append->key_stride;
+    p.new_v = append->value;
+    p.new_v_stride = append->value_stride;
+    p.slots = append->slots;
+  }
   int st = device_error_word(&p.err);
   if (st) return st;
   const int hpc = plan->heads_per_cta;
@@ -436,6 +454,59 @@ int vfl_attention_with_kv_cache(const vfl_attention_plan* plan, const void* quer
   }
   if (plan->dtype == VFL_DTYPE_F32) return launch_paged_attention_f32(p, D, qpc, grid, threads, smem, s);
   return launch_paged_attention_bf16(p, D, qpc, grid, threads, smem, s);
+}
+
+}  // namespace
+
+extern "C" {
+
+int vfl_attention_with_kv_cache(const vfl_attention_plan* plan, const void* query,
+                                int64_t query_token_stride, const void* k_cache,
+                                const void* v_cache, int64_t num_blocks, void* output,
+                                int64_t output_token_stride, const int32_t* query_start_loc,
+                                const int32_t* seq_lens, const int32_t* block_table,
+                                int64_t table_stride, int32_t table_cols, float scale,
+                                void* workspace, size_t workspace_bytes, void* stream) {
+  return attention_run(plan, query, query_token_stride, k_cache, v_cache, num_blocks, output, output_token_stride,
+                       query_start_loc, seq_lens, block_table, table_stride, table_cols, scale, workspace,
+                       workspace_bytes, stream, nullptr);
+}
+
+int vfl_attention_append_supported(const vfl_attention_plan* plan) {
+  return plan != nullptr && plan->magic == VFL_PLAN_MAGIC && plan->queries_per_cta == kTcRows &&
+                 (plan->causal || plan->row_tables || plan->max_q_len <= 1)
+             ? 1
+             : 0;
+}
+
+int vfl_attention_with_kv_cache_append(const vfl_attention_plan* plan, const void* query,
+                                       int64_t query_token_stride, const void* key, int64_t key_token_stride,
+                                       const void* value, int64_t value_token_stride,
+                                       const int64_t* slot_mapping, const void* k_cache, const void* v_cache,
+                                       int64_t num_blocks, void* output, int64_t output_token_stride,
+                                       const int32_t* query_start_loc, const int32_t* seq_lens,
+                                       const int32_t* block_table, int64_t table_stride, int32_t table_cols,
+                                       float scale, void* workspace, size_t workspace_bytes, void* stream) {
+  if (plan == nullptr || plan->magic != VFL_PLAN_MAGIC)
+    return fail(VFL_ERR_INVALID_ARGUMENT, "attention_append: plan missing or not built by vfl_plan_attention");
+  if (!vfl_attention_append_supported(plan))
+    return fail(VFL_ERR_UNSUPPORTED,
+                "attention_append: built for the tensor-core kernel (bf16, head_dim 64), with one new token per "
+                "query row (causal rows, row tables, or one row per request)");
+  if (plan->num_reqs == 0 || plan->total_q == 0) return attention_run(plan, query, query_token_stride, k_cache,
+      v_cache, num_blocks, output, output_token_stride, query_start_loc, seq_lens, block_table, table_stride,
+      table_cols, scale, workspace, workspace_bytes, stream, nullptr);
+  const int64_t row = (int64_t)plan->num_heads * plan->head_dim;
+  if (!key || !value || !slot_mapping)
+    return fail(VFL_ERR_INVALID_ARGUMENT, "attention_append: NULL key, value or slot_mapping");
+  if (!aligned16(key) || !aligned16(value) || (key_token_stride * 2) % 16 != 0 ||
+      (value_token_stride * 2) % 16 != 0 || key_token_stride < row || value_token_stride < row)
+    return fail(VFL_ERR_INVALID_ARGUMENT,
+                "attention_append: key/value must be 16-byte aligned with token strides of at least heads x head_dim");
+  const AppendSource src{key, key_token_stride, value, value_token_stride, slot_mapping};
+  return attention_run(plan, query, query_token_stride, k_cache, v_cache, num_blocks, output, output_token_stride,
+                       query_start_loc, seq_lens, block_table, table_stride, table_cols, scale, workspace,
+                       workspace_bytes, stream, &src);
 }
 
 }  // extern "C"

@@ -58,6 +58,14 @@ struct AttnParams {
   float* ws_ml;      // [total_q, H, num_splits, 2]
   int* ws_arrivals;  // [num_reqs, H / heads_per_cta, q_chunks], zero at launch; null: the
                      // combine kernel merges the partials instead
+  // fused KV append (tensor-core kernel only; null: the caches already hold every token): query
+  // row t's new key / value, [H, D] dense at new_k + t * new_k_stride, go to slot slots[t] (< 0:
+  // none) before the item reads the block that holds them
+  const void* new_k;
+  const void* new_v;
+  int64_t new_k_stride;
+  int64_t new_v_stride;
+  const int64_t* slots;
   unsigned int* err;
 };
 
@@ -74,6 +82,8 @@ struct SmemHeader {
   int abort;                          // a bounded wait gave up
   int consumed;                       // tiles consumed before an abort
   int is_last;                        // this CTA is the last split of its item to finish
+  uint64_t appended;                  // fused KV append: every consumer warp stored its head's
+                                      // new K/V (tensor-core kernel)
 };
 static_assert(sizeof(SmemHeader) <= kHeaderBytes, "header");
 

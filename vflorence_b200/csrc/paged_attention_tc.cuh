@@ -156,6 +156,17 @@ __global__ void __launch_bounds__(160, 3) paged_attention_tc_kernel(const AttnPa
   const uint32_t head_tile_bytes = TILE * sizeof(T);
 
   int32_t* row_tab = reinterpret_cast<int32_t*>(smem + kTcRowTableOffset);
+  // fused KV append: each of this CTA's query rows brings one token (the newest position of its
+  // sequence; successive positions for causal rows). The split that holds a row's position
+  // stores its head group's K and V there - each consumer warp its own head, while the producer
+  // already streams the earlier blocks - and the producer waits for those stores before the
+  // first unit from the tile of the earliest new position. The block is the row's own (copy-on-
+  // write ran before the step), so no other CTA reads these bytes.
+  const int new_lo = p.causal ? L - (q_end - q0) : L - 1;   // earliest new position of the rows
+  const int new_hi = p.causal ? L - (q_end - (q0 + nq - 1)) : L - 1;
+  const int split_lo = blk_begin * bs, split_hi = (blk_begin + bps) * bs;
+  const bool appends = p.new_k != nullptr && new_hi >= 0 && new_hi >= split_lo && new_lo < split_hi;
+  const int first_new_tile = (new_lo > split_lo ? new_lo : split_lo) / 16;
   if (producer) {
     const int nb = min(bps, nblk - blk_begin);
     const int nrows = p.row_tables ? nq : 1;
@@ -181,6 +192,7 @@ __global__ void __launch_bounds__(160, 3) paged_attention_tc_kernel(const AttnPa
     }
     hdr.abort = 0;
     hdr.consumed = 0;
+    mbar_init(&hdr.appended, hpc);
     fence_barrier_init();
   }
   __syncthreads();
@@ -191,11 +203,19 @@ __global__ void __launch_bounds__(160, 3) paged_attention_tc_kernel(const AttnPa
     if (lane == 0) {
       const uint64_t policy = p.row_tables ? l2_evict_normal_policy() : l2_evict_first_policy();
       int u = 0;
-      bool stop = false;
+      bool stop = false, appended = !appends;
       for (int i = 0; i < ntiles && !stop; ++i) {
         const int tile = tile_begin + i;
         const int blk = tile / tpb;
         const int sub_tile = tile - blk * tpb;
+        if (!appended && tile >= first_new_tile) {  // the consumers' stores of the new K/V first
+          appended = true;
+          if (!mbar_wait_bounded(&hdr.appended, 0)) {
+            report(p.err, VFL_DEVERR_TIMEOUT);
+            hdr.abort = 1;
+            break;
+          }
+        }
         unsigned done = 0;
         int64_t phys;
         unsigned mask;
@@ -254,6 +274,33 @@ __global__ void __launch_bounds__(160, 3) paged_attention_tc_kernel(const AttnPa
       bq[kk][0] = __ldg(reinterpret_cast<const unsigned int*>(src));
       bq[kk][1] = __ldg(reinterpret_cast<const unsigned int*>(src + 8));
     }
+  }
+  if (appends) {  // this warp's head of each row whose new position this split holds
+    const int64_t capacity = p.num_blocks * (int64_t)bs;
+    for (int j = 0; j < nq; ++j) {
+      const int t = q0 + j;
+      const int pos = p.causal ? L - (q_end - t) : L - 1;
+      if (pos < split_lo || pos >= split_hi) continue;
+      const int64_t slot = __ldg(p.slots + t);
+      if (slot < 0) continue;  // padding row
+      if (slot >= capacity) {
+        if (warp == 0 && lane == 0) report(p.err, VFL_DEVERR_SLOT);
+        continue;
+      }
+      if (lane < 2 * (D / 8)) {  // 16-byte pieces: lanes 0-7 the key, 8-15 the value
+        const int kv = lane >> 3, c = lane & 7;
+        const int64_t blk = slot / bs, off = slot - blk * bs;
+        const T* src = static_cast<const T*>(kv ? p.new_v : p.new_k) + t * (kv ? p.new_v_stride : p.new_k_stride) +
+                       h * D + c * 8;
+        T* dst = static_cast<T*>(const_cast<void*>(kv ? p.v_cache : p.k_cache)) +
+                 ((blk * p.num_heads + h) * bs + off) * D + c * 8;
+        *reinterpret_cast<uint4*>(dst) = ldg_nc_v4(src);
+      }
+    }
+    // the stores above, before the producer's TMA (async proxy) reads of the same block
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&hdr.appended);
   }
   // this thread's two query columns 2tq, 2tq+1
   int vis_c[2];

@@ -176,12 +176,7 @@ def reshape_and_cache(key: torch.Tensor, value: torch.Tensor, k_cache: torch.Ten
 
 # ------------------------------------------------------------------- attention_with_kv_cache
 
-def attention_with_kv_cache(query: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
-                            output: torch.Tensor, query_start_loc: torch.Tensor,
-                            seq_lens: torch.Tensor, scale: float, causal: bool,
-                            block_table: torch.Tensor, scheduler_metadata: torch.Tensor) -> None:
-    """``output = softmax(scale * q K^T) V`` per request over its paged tokens (writes ``output``)."""
-    plan = plan_of(scheduler_metadata)
+def _attention_checks(plan, query, k_cache, v_cache, output, query_start_loc, seq_lens, causal, block_table):
     dev = k_cache.device
     for name, t in (("query", query), ("k_cache", k_cache), ("v_cache", v_cache), ("output", output),
                     ("query_start_loc", query_start_loc), ("seq_lens", seq_lens),
@@ -211,6 +206,17 @@ def attention_with_kv_cache(query: torch.Tensor, k_cache: torch.Tensor, v_cache:
     ws = None
     if plan.workspace_bytes > 0:
         ws = torch.empty(plan.workspace_bytes, dtype=torch.uint8, device=dev)
+    return dev, n, ws
+
+
+def attention_with_kv_cache(query: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                            output: torch.Tensor, query_start_loc: torch.Tensor,
+                            seq_lens: torch.Tensor, scale: float, causal: bool,
+                            block_table: torch.Tensor, scheduler_metadata: torch.Tensor) -> None:
+    """``output = softmax(scale * q K^T) V`` per request over its paged tokens (writes ``output``)."""
+    plan = plan_of(scheduler_metadata)
+    dev, n, ws = _attention_checks(plan, query, k_cache, v_cache, output, query_start_loc, seq_lens, causal,
+                                   block_table)
     st = N.lib().vfl_attention_with_kv_cache(
         ctypes.byref(plan), query.data_ptr(), query.stride(0), k_cache.data_ptr(), v_cache.data_ptr(), n,
         output.data_ptr(), output.stride(0), query_start_loc.data_ptr(), seq_lens.data_ptr(),
@@ -218,6 +224,46 @@ def attention_with_kv_cache(query: torch.Tensor, k_cache: torch.Tensor, v_cache:
         ws.data_ptr() if ws is not None else None, plan.workspace_bytes if ws is not None else 0,
         _stream(dev))
     N.check(st, "attention_with_kv_cache")
+
+
+def attention_append_supported(scheduler_metadata: torch.Tensor) -> bool:
+    """Whether ``attention_with_kv_cache_append`` takes this plan (the tensor-core kernel: bf16,
+    head_dim 64; one new token per query row)."""
+    return bool(N.lib().vfl_attention_append_supported(ctypes.byref(plan_of(scheduler_metadata))))
+
+
+def attention_with_kv_cache_append(query: torch.Tensor, key: torch.Tensor, value: torch.Tensor,
+                                   k_cache: torch.Tensor, v_cache: torch.Tensor, output: torch.Tensor,
+                                   slot_mapping: torch.Tensor, query_start_loc: torch.Tensor,
+                                   seq_lens: torch.Tensor, scale: float, causal: bool, block_table: torch.Tensor,
+                                   scheduler_metadata: torch.Tensor) -> None:
+    """``reshape_and_cache(key, value, k_cache, v_cache, slot_mapping)`` then
+    ``attention_with_kv_cache(...)`` in one launch (vflorence/layers/attention.py:55-72): query row
+    t's new key / value rows go to ``slot_mapping[t]`` before the attention reads them. Each
+    row's new token is the newest position of its sequence, or for causal rows the successive
+    positions ending there, in a block no other row of the call holds. Plans for which
+    ``attention_append_supported`` is False raise VflError."""
+    plan = plan_of(scheduler_metadata)
+    dev, n, ws = _attention_checks(plan, query, k_cache, v_cache, output, query_start_loc, seq_lens, causal,
+                                   block_table)
+    for name, t in (("key", key), ("value", value), ("slot_mapping", slot_mapping)):
+        _require_cuda(name, t, dev)
+    _require_dense_rows("key", key)
+    _require_dense_rows("value", value)
+    if key.shape != value.shape or key.shape[1:] != query.shape[1:] or key.shape[0] < plan.total_q \
+            or key.dtype != k_cache.dtype or value.dtype != k_cache.dtype:
+        raise ValueError("vflorence_b200: key/value must be [query rows, heads, head_dim] of the cache dtype")
+    if slot_mapping.dtype != torch.int64 or slot_mapping.dim() != 1 or slot_mapping.numel() < plan.total_q \
+            or not slot_mapping.is_contiguous():
+        raise ValueError("vflorence_b200: slot_mapping must be contiguous int64 [query rows]")
+    st = N.lib().vfl_attention_with_kv_cache_append(
+        ctypes.byref(plan), query.data_ptr(), query.stride(0), key.data_ptr(), key.stride(0), value.data_ptr(),
+        value.stride(0), slot_mapping.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), n, output.data_ptr(),
+        output.stride(0), query_start_loc.data_ptr(), seq_lens.data_ptr(), block_table.data_ptr(),
+        block_table.stride(0), block_table.shape[1], float(scale),
+        ws.data_ptr() if ws is not None else None, plan.workspace_bytes if ws is not None else 0,
+        _stream(dev))
+    N.check(st, "attention_with_kv_cache_append")
 
 
 # ------------------------------------------------------------------------------- copy_blocks
