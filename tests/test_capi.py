@@ -226,3 +226,36 @@ def test_add_layernorm_host_checks(native):
                                   bf16, None)  # misaligned rows
     assert st == _native.VFL_ERR_INVALID_ARGUMENT
     assert native.vfl_add_layernorm(None, 1024, None, 1024, None, None, None, 1024, 0, 1024, 1e-5, bf16, None) == 0
+
+
+def test_attention_append_host_checks(native):
+    """Which plans the fused append takes, and refusals before any launch."""
+    from vflorence_b200 import _native
+    from vflorence_b200 import paged_ops as ops
+
+    def meta(lens, qsl=None, dtype=torch.bfloat16, causal=False, row_tables=False, d=64):
+        q = None if qsl is None else torch.tensor(qsl, dtype=torch.int32)
+        return ops.get_scheduler_metadata(len(lens), 16, 16, d, torch.tensor(lens, dtype=torch.int32), dtype, q,
+                                          causal, "sm100", 16, row_tables=row_tables)
+
+    assert ops.attention_append_supported(meta([100, 200]))                              # one row per request
+    assert ops.attention_append_supported(meta([100, 200], [0, 3, 5], row_tables=True))  # beam groups
+    assert ops.attention_append_supported(meta([100, 200], [0, 3, 5], causal=True))      # causal rows
+    assert not ops.attention_append_supported(meta([100, 200], [0, 3, 5]))               # rows sharing a table
+    assert not ops.attention_append_supported(meta([100, 200], dtype=torch.float32))     # CUDA-core kernel
+    assert not ops.attention_append_supported(meta([100, 200], d=128))
+    fake = ctypes.c_void_p(256)
+    bad = ops.plan_of(meta([100, 200], dtype=torch.float32))
+    st = native.vfl_attention_with_kv_cache_append(ctypes.byref(bad), fake, 1024, fake, 1024, fake, 1024, fake, fake,
+                                                   fake, 100, fake, 1024, fake, fake, fake, 16, 16, 0.125, None, 0,
+                                                   None)
+    assert st == _native.VFL_ERR_UNSUPPORTED, native.vfl_last_error_message()
+    good = ops.plan_of(meta([100, 200]))
+    st = native.vfl_attention_with_kv_cache_append(ctypes.byref(good), fake, 1024, None, 1024, fake, 1024, fake,
+                                                   fake, fake, 100, fake, 1024, fake, fake, fake, 16, 16, 0.125, None,
+                                                   0, None)
+    assert st == _native.VFL_ERR_INVALID_ARGUMENT and b"NULL" in native.vfl_last_error_message()
+    st = native.vfl_attention_with_kv_cache_append(ctypes.byref(good), fake, 1024, ctypes.c_void_p(264), 1024, fake,
+                                                   1024, fake, fake, fake, 100, fake, 1024, fake, fake, fake, 16, 16,
+                                                   0.125, None, 0, None)
+    assert st == _native.VFL_ERR_INVALID_ARGUMENT  # a key not 16-byte aligned
