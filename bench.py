@@ -31,6 +31,7 @@ import os
 import statistics
 import subprocess
 import sys
+import tempfile
 import time
 
 import torch
@@ -157,8 +158,9 @@ class ClockSampler:
                 phys = int(ids[device_index])
         self.phys = phys
         self.proc = None
-        self.path = os.path.join(REPO, "gpurun_out", f"clocks_gpu{phys}.csv") if os.path.isdir(
-            os.path.join(REPO, "gpurun_out")) else f"/tmp/vfl_clocks_{os.getpid()}.csv"
+        # the raw trace: VFL_CLOCKS_DIR when set (to keep it), else a temporary file
+        out_dir = os.environ.get("VFL_CLOCKS_DIR") or tempfile.gettempdir()
+        self.path = os.path.join(out_dir, f"vfl_clocks_gpu{phys}_{os.getpid()}.csv")
 
     def __enter__(self):
         try:
