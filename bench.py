@@ -504,6 +504,63 @@ def run_split_sweep(args):
         del k, v
 
 
+def run_profile_step(args):
+    """The workload of the decode-step launch list: the config's engine with CUDA graphs, one
+    wave of requests, 120 steps, then one step between torch.cuda.profiler.start() and stop()
+    (capture it with ncu --profile-from-start off)."""
+    from vflorence_b200.engine import Engine, SamplingParams
+
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    cfg = decode_config(args.profile_step)
+    params = SamplingParams.from_dict(cfg["params"])
+    cfg["num_requests"] = min(cfg["num_requests"], cfg["max_num_seqs"] // params.num_beams)
+    model = build_decode_model(cfg, device)
+    if cfg["kind"] == "florence2":
+        with torch.inference_mode():
+            px = torch.zeros(1, 3, 768, 768, device=device, dtype=cfg["dtype"])
+            cfg["image_tokens"] = model.model.get_image_features(px).pooler_output.shape[1]
+    eng = Engine(model, max_num_seqs=cfg["max_num_seqs"], max_decoder_len=cfg["max_decoder_len"],
+                 max_encoder_len=cfg["max_encoder_len"], block_size=BS, cuda_graphs=True)
+    eng.graphs.capture(cfg["max_num_seqs"], params.num_beams)
+    for r in decode_requests(cfg, device):
+        eng.add_request(r, params)
+    with torch.inference_mode():
+        for _ in range(120):
+            eng.step()
+        torch.cuda.synchronize()
+        torch.cuda.profiler.start()
+        eng.step()
+        torch.cuda.synchronize()
+        torch.cuda.profiler.stop()
+    print(json.dumps({"point": "profile_step", "config": args.profile_step, "rows": eng.rt.num_running}))
+
+
+def run_profile_kv_proj(args):
+    """The workload of the K/V projection captures: three calls of kv_proj_paged at the given
+    token count (hidden 1024, 16 heads x 64, block 16, random slots; from 6144 tokens the 2-SM
+    kernel)."""
+    from vflorence_b200 import paged_ops as ops
+
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    T, K, heads = args.profile_kv_proj, 1024, 16
+    g = torch.Generator(device=device).manual_seed(0)
+    hidden = torch.randn(T, K, generator=g, device=device).to(torch.bfloat16)
+    w = (torch.randn(2 * heads * D, K, generator=g, device=device) / K ** 0.5).to(torch.bfloat16)
+    b = torch.randn(2 * heads * D, generator=g, device=device).to(torch.bfloat16)
+    nb = -(-T // BS) + 1
+    kc = torch.zeros(nb, heads, BS, D, device=device, dtype=torch.bfloat16)
+    vc = torch.zeros_like(kc)
+    slots = torch.randperm(nb * BS, generator=g, device=device)[:T].to(torch.int64)
+    for _ in range(3):
+        ops.kv_proj_paged(hidden, w, b, kc, vc, slots)
+    torch.cuda.synchronize()
+    if ops.read_device_errors(device):
+        raise RuntimeError("kv_proj_paged raised device error bits")
+    print(json.dumps({"point": "profile_kv_proj", "tokens": T}))
+
+
 # ---------------------------------------------------------------------------- decode (engine)
 
 def decode_config(name: str):
@@ -699,6 +756,10 @@ def main():
     ap.add_argument("--split-sweep", action="store_true",
                     help="the planner's split rule against every fixed split, one line per shape")
     ap.add_argument("--sweep-batches", default="1,2,4,8,16,32,64,128,256,512,1024")
+    ap.add_argument("--profile-step", choices=["cfg1", "cfg2", "cfg3", "cfg4"], default=None,
+                    help="one decode step of the config's engine inside a profiler range (for ncu)")
+    ap.add_argument("--profile-kv-proj", type=int, default=0, metavar="TOKENS",
+                    help="three encoder K/V projection calls at TOKENS tokens (for ncu)")
     ap.add_argument("--decode", choices=["cfg1", "cfg2", "cfg3", "cfg4"], default=None,
                     help="end-to-end decode tokens/s of the engine on a BASELINE config")
     ap.add_argument("--eager", action="store_true", help="decode without CUDA graphs")
@@ -711,6 +772,12 @@ def main():
         return
     if args.split_sweep:
         run_split_sweep(args)
+        return
+    if args.profile_step:
+        run_profile_step(args)
+        return
+    if args.profile_kv_proj:
+        run_profile_kv_proj(args)
         return
     if args.decode:
         run_decode(args)
