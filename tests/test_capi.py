@@ -241,6 +241,8 @@ def test_attention_append_host_checks(native):
     assert ops.attention_append_supported(meta([100, 200]))                              # one row per request
     assert ops.attention_append_supported(meta([100, 200], [0, 3, 5], row_tables=True))  # beam groups
     assert ops.attention_append_supported(meta([100, 200], [0, 3, 5], causal=True))      # causal rows
+    # more than 8 causal rows of a request span two CTAs, and later rows read earlier rows' tokens
+    assert not ops.attention_append_supported(meta([100, 200], [0, 12, 14], causal=True))
     assert not ops.attention_append_supported(meta([100, 200], [0, 3, 5]))               # rows sharing a table
     assert not ops.attention_append_supported(meta([100, 200], dtype=torch.float32))     # CUDA-core kernel
     assert not ops.attention_append_supported(meta([100, 200], d=128))

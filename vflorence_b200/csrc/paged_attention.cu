@@ -473,8 +473,11 @@ int vfl_attention_with_kv_cache(const vfl_attention_plan* plan, const void* quer
 }
 
 int vfl_attention_append_supported(const vfl_attention_plan* plan) {
+  // Causal rows read the new tokens of earlier rows: all of a request's rows must be in one CTA
+  // (one query chunk), or another CTA's stores would race this one's reads. Rows with their own
+  // tables (beam groups) and single rows read only their own new token.
   return plan != nullptr && plan->magic == VFL_PLAN_MAGIC && plan->queries_per_cta == kTcRows &&
-                 (plan->causal || plan->row_tables || plan->max_q_len <= 1)
+                 (plan->causal ? plan->max_q_len <= kTcRows : (plan->row_tables || plan->max_q_len <= 1))
              ? 1
              : 0;
 }
@@ -492,7 +495,7 @@ int vfl_attention_with_kv_cache_append(const vfl_attention_plan* plan, const voi
   if (!vfl_attention_append_supported(plan))
     return fail(VFL_ERR_UNSUPPORTED,
                 "attention_append: built for the tensor-core kernel (bf16, head_dim 64), with one new token per "
-                "query row (causal rows, row tables, or one row per request)");
+                "query row (at most 8 causal rows per request, row tables, or one row per request)");
   if (plan->num_reqs == 0 || plan->total_q == 0) return attention_run(plan, query, query_token_stride, k_cache,
       v_cache, num_blocks, output, output_token_stride, query_start_loc, seq_lens, block_table, table_stride,
       table_cols, scale, workspace, workspace_bytes, stream, nullptr);

@@ -228,7 +228,8 @@ def attention_with_kv_cache(query: torch.Tensor, k_cache: torch.Tensor, v_cache:
 
 def attention_append_supported(scheduler_metadata: torch.Tensor) -> bool:
     """Whether ``attention_with_kv_cache_append`` takes this plan (the tensor-core kernel: bf16,
-    head_dim 64; one new token per query row)."""
+    head_dim 64; one new token per query row: at most 8 causal rows per request, rows with their
+    own tables, or one row per request)."""
     return bool(N.lib().vfl_attention_append_supported(ctypes.byref(plan_of(scheduler_metadata))))
 
 
