@@ -79,7 +79,9 @@ def decoder_self_attention(query: torch.Tensor, key: torch.Tensor, value: torch.
         qsl, lens = ctx.self_groups, ctx.self_group_lens
     else:
         qsl, lens = ctx.query_start_loc, ctx.context_lens
-    if paged_ops.attention_append_supported(ctx.self_metadata):
+    if ctx.self_append is None:
+        ctx.self_append = paged_ops.attention_append_supported(ctx.self_metadata)
+    if ctx.self_append:
         paged_ops.attention_with_kv_cache_append(query, key, value, k_cache, v_cache, out, ctx.slot_mapping, qsl,
                                                  lens, scale=scale, causal=False, block_table=ctx.block_tables,
                                                  scheduler_metadata=ctx.self_metadata)

@@ -25,6 +25,8 @@ class Context:
     # one group with per-row block tables (self_metadata is then a row-tables plan)
     self_groups: torch.Tensor | None = None      # int32 [G + 1], device: row offsets of the groups
     self_group_lens: torch.Tensor | None = None  # int32 [G], device: each group's context length
+    # whether self_metadata takes the fused KV append (asked once per step, not once per layer)
+    self_append: bool | None = None
 
 
 _CONTEXT: Context | None = None
