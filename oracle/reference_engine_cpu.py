@@ -1,0 +1,122 @@
+"""ORACLE — test infrastructure only: the reference's own CPU decode engine, timed.
+
+    python oracle/reference_engine_cpu.py --reference-root <vflorence checkout> [--configs cfg1,cfg2]
+                                          [--threads N] [--requests K]
+
+Runs the UNMODIFIED vflorence engine (``vflorence.LLM``, imported from ``--reference-root``) on
+this machine's CPU cores, with ``oracle/vllm_cpu_attn`` (the C restatement of the attention
+library, whose SIMD build is not installable here) standing in for ``vllm_cpu_attn``. The
+workloads are BASELINE configs 1 and 2 exactly as ``bench.py --decode cfgN`` builds them: the
+same BART-large-shaped random-init weights (seed 0), the same seeded requests, the same sampling
+(EOS disabled, so every request decodes ``max_tokens``), block size 16. One JSON line per config:
+decode tokens/s = completion tokens of all requests / wall time of the whole job (encoding
+included), as the reference counts them (vflorence/engine/llm_engine.py:114-118), with the
+thread count. A short warm-up job (two requests, 4 tokens) runs first.
+
+The reference does not travel to the GPU boxes, so this runs where the reference is checked out;
+the figure it prints is a reported CPU baseline, not something the product calls.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import sys
+import time
+from tempfile import TemporaryDirectory
+
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+BART_LARGE = dict(vocab_size=50265, d_model=1024, encoder_layers=12, decoder_layers=12,
+                  encoder_attention_heads=16, decoder_attention_heads=16, encoder_ffn_dim=4096,
+                  decoder_ffn_dim=4096, max_position_embeddings=1024, activation_function="gelu",
+                  decoder_start_token_id=2, eos_token_id=2, bos_token_id=0, pad_token_id=1, init_std=0.02)
+
+# BASELINE configs 1 and 2 (the BART-large shape), as bench.py's decode_config defines them.
+CONFIGS = {
+    "cfg1": dict(dtype=torch.float32, num_requests=8, lens=(200, 1000), ids=(4, 50264), id_seed=0,
+                 params=dict(max_tokens=64, num_beams=1, eos_token_id=[]),
+                 max_num_seqs=8, max_decoder_len=64, max_encoder_len=1000),
+    "cfg2": dict(dtype=torch.bfloat16, num_requests=32, lens=(300, 1024), ids=(4, 50264), id_seed=1,
+                 params=dict(max_tokens=142, num_beams=4, length_penalty=2.0, no_repeat_ngram_size=3,
+                             eos_token_id=[]),
+                 max_num_seqs=128, max_decoder_len=144, max_encoder_len=1024),
+}
+
+
+def requests_of(cfg):
+    """The seeded requests of bench.py's decode_requests for a BART config."""
+    g = torch.Generator().manual_seed(cfg["id_seed"])
+    reqs = []
+    for _ in range(cfg["num_requests"]):
+        n = int(torch.randint(cfg["lens"][0], cfg["lens"][1] + 1, (1,), generator=g))
+        reqs.append(torch.randint(*cfg["ids"], (n,), generator=g).tolist())
+    return reqs
+
+
+def _cpu_name() -> str:
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference-root", required=True, help="vflorence checkout")
+    ap.add_argument("--configs", default="cfg1,cfg2")
+    ap.add_argument("--threads", type=int, default=os.cpu_count())
+    ap.add_argument("--requests", type=int, default=0,
+                    help="time only the first K requests of each config (0: all of them)")
+    args = ap.parse_args()
+    torch.set_num_threads(args.threads)
+
+    sys.path.insert(0, HERE)                 # the vllm_cpu_attn stand-in (oracle/vllm_cpu_attn)
+    sys.path.insert(0, args.reference_root)
+    import vllm_cpu_attn  # noqa: F401
+    import vflorence.config as vconfig
+
+    vconfig.AARCH64 = True  # block size 16, the BASELINE block size
+    from transformers import BartConfig, BartForConditionalGeneration
+
+    from vflorence import LLM, Request, SamplingParams
+
+    torch.manual_seed(0)
+    hf = BartForConditionalGeneration(BartConfig(**BART_LARGE)).eval()
+    with TemporaryDirectory() as path:
+        hf.save_pretrained(path)
+        del hf
+        for name in args.configs.split(","):
+            cfg = CONFIGS[name]
+            reqs = requests_of(cfg)
+            if args.requests:
+                reqs = reqs[: args.requests]
+            llm = LLM(path, max_num_seqs=cfg["max_num_seqs"], dtype=cfg["dtype"], compile=False,
+                      max_decoder_len=cfg["max_decoder_len"], max_encoder_len=cfg["max_encoder_len"])
+            assert llm.config.block_size == 16
+            params = SamplingParams(**cfg["params"])
+            llm.generate([Request(r) for r in reqs[:2]], SamplingParams(**dict(cfg["params"], max_tokens=4)),
+                         use_tqdm=False)
+            t0 = time.perf_counter()
+            outs = llm.generate([Request(r) for r in reqs], params, use_tqdm=False)
+            wall = time.perf_counter() - t0
+            tokens = sum(len(o.completion_token_ids) for o in outs)
+            print(json.dumps({
+                "metric": "decode tokens/s", "config": name, "value": tokens / wall, "unit": "tokens/s",
+                "impl": "reference engine (vflorence, unmodified) + C restatement of vllm_cpu_attn",
+                "threads": args.threads, "requests": len(reqs), "of_requests": cfg["num_requests"],
+                "completion_tokens": tokens, "wall_s": wall, "params": cfg["params"],
+                "dtype": str(cfg["dtype"]).replace("torch.", ""), "compile": False,
+                "cpu": _cpu_name()}), flush=True)
+            del llm
+
+
+if __name__ == "__main__":
+    main()
