@@ -56,3 +56,17 @@ def test_group_rows_by_shared_pages(engine_trace):
             # beams of a request are consecutive rows, which is what group_rows relies on
             for idx in rows.values():
                 assert idx == list(range(idx[0], idx[0] + len(idx)))
+
+
+def test_cpu_engine_baseline_times_the_bench_workload():
+    """The reference CPU engine timing (oracle/reference_engine_cpu.py) runs configs 1 and 2 on
+    the same model shape, requests, sampling and pool sizes as bench.py --decode cfgN."""
+    import bench
+    import reference_engine_cpu as ref
+
+    for name in ("cfg1", "cfg2"):
+        ours, theirs = bench.decode_config(name), ref.CONFIGS[name]
+        assert ours["text"] == ref.BART_LARGE
+        for key in ("dtype", "num_requests", "params", "max_num_seqs", "max_decoder_len", "max_encoder_len"):
+            assert ours[key] == theirs[key], (name, key)
+        assert [r.input_ids for r in bench.decode_requests(ours, "cpu")] == ref.requests_of(theirs)
