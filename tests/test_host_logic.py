@@ -59,14 +59,26 @@ def test_group_rows_by_shared_pages(engine_trace):
 
 
 def test_cpu_engine_baseline_times_the_bench_workload():
-    """The reference CPU engine timing (oracle/reference_engine_cpu.py) runs configs 1 and 2 on
-    the same model shape, requests, sampling and pool sizes as bench.py --decode cfgN."""
+    """The reference CPU engine timing (oracle/reference_engine_cpu.py) runs configs 1-4 on the
+    same model shapes, requests (ids and images), sampling and pool sizes as bench.py --decode cfgN."""
     import bench
     import reference_engine_cpu as ref
 
-    for name in ("cfg1", "cfg2"):
+    for name in ("cfg1", "cfg2", "cfg3", "cfg4"):
         ours, theirs = bench.decode_config(name), ref.CONFIGS[name]
-        assert ours["text"] == ref.BART_LARGE
+        kind = theirs.get("kind", "bart")
+        if kind == "bart":
+            assert ours["text"] == ref.BART_LARGE
+        else:
+            assert (ours["text"], ours["vision"]) == ref.SHAPES[kind]
+            ours["image_tokens"] = ref.IMAGE_TOKENS  # bench reads it off the built tower
         for key in ("dtype", "num_requests", "params", "max_num_seqs", "max_decoder_len", "max_encoder_len"):
             assert ours[key] == theirs[key], (name, key)
-        assert [r.input_ids for r in bench.decode_requests(ours, "cpu")] == ref.requests_of(theirs)
+        if name == "cfg4":  # 512 images: compare the first few
+            ours["num_requests"] = 6
+            theirs = dict(theirs, num_requests=6)
+        mine = bench.decode_requests(ours, "cpu")
+        want = ref.requests_of(theirs)
+        assert [r.input_ids for r in mine] == [ids for ids, _ in want]
+        for r, (_, px) in zip(mine, want):
+            assert (r.pixel_values is None and px is None) or torch.equal(r.pixel_values, px)
