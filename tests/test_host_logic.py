@@ -1,8 +1,15 @@
 """Host-side bookkeeping around the kernels, checked against the reference engine's recorded
 trace: encoder page allocation (vflorence/engine/model_runner.py:169-177, :232-265), step
-packing (:290-306) and the beam grouping of the cross-attention staging (attention.py:9-39)."""
+packing (:290-306) and the beam grouping of the cross-attention staging (attention.py:9-39).
+Also the measurement harness's CPU-side contracts: bench.py's reference arm, and the CPU engine
+baseline's workload against bench.py's decode workload."""
 
 from __future__ import annotations
+
+import json
+import os
+import subprocess
+import sys
 
 import torch
 
@@ -82,3 +89,30 @@ def test_cpu_engine_baseline_times_the_bench_workload():
         assert [r.input_ids for r in mine] == [ids for ids, _ in want]
         for r, (_, px) in zip(mine, want):
             assert (r.pixel_values is None and px is None) or torch.equal(r.pixel_values, px)
+
+
+def _bench_reference(env_extra):
+    repo = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    env = dict(os.environ, **env_extra)
+    res = subprocess.run([sys.executable, os.path.join(repo, "bench.py"), "--impl", "reference", "--steps", "3",
+                          "--warmup", "3", "--batch", "64", "--cpu-sample", "4"],
+                         capture_output=True, text=True, timeout=300, env=env, cwd=repo)
+    assert res.returncode == 0, res.stderr[-2000:]
+    return [json.loads(line) for line in res.stdout.splitlines() if line.startswith("{")]
+
+
+def test_bench_reference_arm_prints_one_line():
+    """bench.py --impl reference (the reference's CPU path, no GPU needed) prints one JSON line
+    with the metric of the GPU arm, a cpu_baseline describing the run and a zero-copy e2e."""
+    (line,) = _bench_reference({})
+    assert line["impl"] == "reference" and line["unit"] == "GB/s" and line["value"] > 0
+    assert line["metric"] == "paged-attn HBM GB/s vs 8 TB/s" and line["higher_is_better"] is True
+    assert line["cpu_baseline"]["kind"] == "port" and line["cpu_baseline"]["cores"] >= 1
+    assert line["cpu_baseline"]["value"] == line["value"]
+    assert line["e2e"] == {"value": line["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
+    assert line["config"]["batch_per_gpu"] == 64
+
+
+def test_bench_reference_arm_other_ranks_exit_quietly():
+    """Under torchrun only rank 0 runs the reference arm; the other ranks print nothing."""
+    assert _bench_reference({"WORLD_SIZE": "2", "RANK": "1", "LOCAL_RANK": "1"}) == []
