@@ -144,11 +144,11 @@ class _Ref:
         return done
 
 
-def _run(seed, nb, num_requests, max_rows, max_tokens, lp, early, bs=4, vocab=9):
+def _run(seed, nb, num_requests, max_rows, max_tokens, lp, early, bs=4, vocab=9, ref_cls=_Ref):
     rng = random.Random(seed)
     num_blocks = 4 * max_rows * (-(-max_tokens // bs) + 1)
     K = 2 * nb
-    ref = _Ref(num_blocks, bs, nb, max_tokens, lp, early, {EOS})
+    ref = ref_cls(num_blocks, bs, nb, max_tokens, lp, early, {EOS})
     rt = DecodeRuntime(num_blocks, bs, (2 + K // nb) * max_rows + 4, -(-(max_tokens + 1) // bs))
     rules = DecodeRules(nb, max_tokens, lp, early, [EOS])
     waiting = deque(range(num_requests))
@@ -217,6 +217,44 @@ def _run(seed, nb, num_requests, max_rows, max_tokens, lp, early, bs=4, vocab=9)
     assert rt.num_free_blocks == num_blocks and not any(rt.ref_counts())
     assert rt.free_block_ids() == list(ref.free)
     return steps
+
+
+class _ReleaseFirstBlockFirst(_Ref):
+    """Planted mistake: a finished sequence's blocks go back to the free list first block first
+    (block_manager.py releases the last block first)."""
+
+    def dealloc(self, s):
+        for b in s.table:
+            self.rc[b] -= 1
+            if self.rc[b] == 0:
+                self.free.append(b)
+        s.table = []
+
+
+class _PenaltyCountsStartToken(_Ref):
+    """Planted mistake: the length penalty counts the decoder start token (sequence.py divides
+    by the number of generated tokens)."""
+
+    def score(self, s):
+        return s.cum / (len(s.tokens) ** self.lp)
+
+
+class _OneTokenLate(_Ref):
+    """Planted mistake: a sequence finishes one token after max_tokens."""
+
+    def done(self, s):
+        return s.tokens[-1] in self.eos or len(s.tokens) - 1 > self.max_tokens
+
+
+@pytest.mark.parametrize("mutant,nb,lp", [(_ReleaseFirstBlockFirst, 1, 1.0), (_ReleaseFirstBlockFirst, 3, 1.0),
+                                          (_PenaltyCountsStartToken, 3, 2.0), (_OneTokenLate, 1, 1.0)])
+def test_planted_mistakes_in_the_restatement_are_caught(mutant, nb, lp):
+    """The comparison is sharp enough to see a one-rule slip in the restatement (the mistake is
+    planted on the CPU side, in the Python restatement, never in the library)."""
+    with pytest.raises(AssertionError):
+        for seed in range(3):
+            _run(200 + seed, nb=nb, num_requests=7, max_rows=3 * nb, max_tokens=10, lp=lp, early=False,
+                 ref_cls=mutant)
 
 
 @pytest.mark.parametrize("seed", range(4))

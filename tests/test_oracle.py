@@ -29,6 +29,27 @@ def test_attention_matches_float64(oracle_lib, case):
     assert_attention_close(out, t["expected"], dt, case["name"])
 
 
+F32_CASES = [c for c in CASES if c["dtype"] == "f32" and int(max(c["seq_lens"])) >= 2]
+
+
+@pytest.mark.parametrize("case", F32_CASES, ids=[c["name"] for c in F32_CASES])
+@pytest.mark.parametrize("mistake", ["one_token_short", "scale_off_1pct"])
+def test_planted_oracle_mistakes_fail_the_golden_check(oracle_lib, case, mistake):
+    """A slip planted in the call of the oracle (one token short of each context, or a scale off
+    by 1 %) fails the float64 golden check: the fixture and the fp32 bar can tell them apart."""
+    t = case_tensors(case)
+    lens, scale = t["seq_lens"].clone(), case["scale"]
+    if mistake == "one_token_short":
+        lens = (lens - 1).clamp(min=0)
+    else:
+        scale *= 1.01
+    out = torch.empty_like(t["q"])
+    oracle_lib.attention(t["q"], t["k_cache"], t["v_cache"], out, t["query_start_loc"], lens, scale,
+                         bool(case["causal"]), t["block_table"])
+    with pytest.raises(AssertionError):
+        assert_attention_close(out, t["expected"], torch.float32, case["name"])
+
+
 def test_engine_tokens_equal_hf_generate(engine_trace):
     for run in engine_trace["runs"]:
         assert run["tokens"] == run["hf_tokens"], run["name"]
