@@ -95,6 +95,11 @@ class DecodeRuntime:
         self._out2 = ctypes.c_int32()
         self._res = N.StepResult(*(b.ctypes.data for b in self._born), S, 0, self._done_rid.ctypes.data,
                                  self._done[0].ctypes.data, self._done[1].ctypes.data, S, 0)
+        # the per-step output buffers live as long as the runtime: their addresses are taken once
+        # (numpy's .ctypes.data costs about 2 us a call, and a step passes a dozen of them)
+        self._addr = {name: a.ctypes.data for name, a in self._i32.items()}
+        self._addr_rids, self._addr_cum = self._rids.ctypes.data, self._cum.ctypes.data
+        self._ng, self._mr = ctypes.c_int32(), ctypes.c_int32()
 
     def __del__(self):
         h = getattr(self, "_h", None)
@@ -191,11 +196,11 @@ class DecodeRuntime:
         else:
             stride, width, cap = 0, 0, self.num_slots
         cap = min(cap, len(pos), len(tok))
-        ng = ctypes.c_int32()
-        mr = ctypes.c_int32()
+        ad, ng, mr = self._addr, self._ng, self._mr
         self._check(self._lib.vfl_rt_pack_step(
-            self._h, cap, _ptr(tables), stride, width, _ptr(a["table_lens"]), _ptr(pos), _ptr(tok), _ptr(a["slots"]),
-            _ptr(a["lengths"]), _ptr(self._rids), _ptr(a["groups"]), _ptr(a["ranks"]), _ptr(self._cum),
+            self._h, cap, _ptr(tables), stride, width, ad["table_lens"],
+            ad["positions"] if positions is None else _ptr(pos), ad["tokens"] if tokens is None else _ptr(tok),
+            ad["slots"], ad["lengths"], self._addr_rids, ad["groups"], ad["ranks"], self._addr_cum,
             ctypes.byref(ng), ctypes.byref(mr)), "pack_step")
         n = self.num_running
         return StepRows(n, a["table_lens"][:n], pos[:n], tok[:n], a["slots"][:n], a["lengths"][:n], self._rids[:n],
