@@ -299,3 +299,47 @@ def test_runtime_argument_checks():
         rt2.advance_beam(rules, bad, np.zeros_like(bad), np.zeros(bad.shape, np.float32))
     with pytest.raises(VflError, match="no candidate"):
         rt2.advance_beam(rules, -np.ones_like(bad), np.zeros_like(bad), np.zeros(bad.shape, np.float32))
+
+
+def test_pack_step_into_caller_buffers_matches_own_buffers():
+    """The engine packs a step's rows straight into its pinned upload buffer: tables, positions
+    and token ids as views of one int32 array. Those rows must equal the rows packed into the
+    runtime's own buffers, step after step of a beam search."""
+    nb, K, bs, max_tokens = 3, 6, 4, 10
+    rt = DecodeRuntime(256, bs, 64, -(-(max_tokens + 1) // bs))
+    rules = DecodeRules(nb, max_tokens, 1.0, False, [EOS])
+    rng = random.Random(5)
+    for rid in range(4):
+        rt.admit(rid, START)
+    B, M = 16, rt.max_blocks_per_seq
+    flat = np.full(B * M + 2 * B, -7, dtype=np.int32)
+    fields = ("table_lens", "positions", "tokens", "slots", "lengths", "request_ids", "groups", "ranks",
+              "cum_logprobs")
+    for _ in range(8):
+        rt.prepare_step()
+        own_tables = np.zeros((B, M), dtype=np.int32)
+        own = rt.pack_step(own_tables)
+        want = {f: np.copy(getattr(own, f)) for f in fields}
+        want_groups, n = own.num_groups, own.n
+        if n == 0:
+            break
+        tables, pos, tok = flat[: B * M].reshape(B, M), flat[B * M: B * M + B], flat[B * M + B:]
+        got = rt.pack_step(tables, pos, tok)
+        assert got.n == n and got.num_groups == want_groups
+        for f in fields:
+            assert np.array_equal(getattr(got, f), want[f]), f
+        assert np.array_equal(tables[:n], own_tables[:n])
+        assert np.array_equal(pos[:n], want["positions"]) and np.array_equal(tok[:n], want["tokens"])
+        G = got.num_groups
+        rows = np.full((G, K), -1, dtype=np.int32)
+        toks = np.zeros((G, K), dtype=np.int32)
+        scores = np.full((G, K), -np.inf, dtype=np.float32)
+        for g in range(G):
+            members = [i for i in range(n) if got.groups[i] == g]
+            picks = sorted(((rng.choice(members), rng.randrange(3, 9), -rng.random() - 0.1) for _ in range(K)),
+                           key=lambda c: -c[2])
+            for j, (r, t, sc) in enumerate(picks):
+                rows[g, j], toks[g, j], scores[g, j] = r, t, float(got.cum_logprobs[r]) + sc
+            order = np.argsort(-scores[g], kind="stable")
+            rows[g], toks[g], scores[g] = rows[g][order], toks[g][order], scores[g][order]
+        rt.advance_beam(rules, rows, toks, scores)
