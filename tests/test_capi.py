@@ -261,3 +261,49 @@ def test_attention_append_host_checks(native):
                                                    1024, fake, fake, fake, 100, fake, 1024, fake, fake, fake, 16, 16,
                                                    0.125, None, 0, None)
     assert st == _native.VFL_ERR_INVALID_ARGUMENT  # a key not 16-byte aligned
+
+
+def test_cache_ops_refuse_bad_arguments_before_the_device(native):
+    """reshape_and_cache, prepare_decode and paged_slots check sizes, dtypes, NULL pointers,
+    alignment and strides on the host and return a status without a launch; empty work is a
+    no-op. The addresses below are never dereferenced: every case fails a host check first."""
+    from vflorence_b200 import _native as N
+
+    A = 0x10000  # a 16-byte aligned stand-in address
+    H, D, BS = 2, 64, 16
+
+    def rc(key=A, value=A, kc=A, vc=A, slots=A, tokens=3, heads=H, head_dim=D, block_size=BS, blocks=8,
+           kstride=H * D, vstride=H * D, dtype=N.DTYPE_BF16):
+        return native.vfl_reshape_and_cache(key, value, kc, vc, slots, tokens, heads, head_dim, block_size,
+                                            blocks, kstride, vstride, dtype, None)
+
+    assert rc(dtype=7) == N.VFL_ERR_UNSUPPORTED
+    assert rc(heads=0) == N.VFL_ERR_INVALID_ARGUMENT
+    assert rc(blocks=0) == N.VFL_ERR_INVALID_ARGUMENT
+    assert rc(tokens=-1) == N.VFL_ERR_INVALID_ARGUMENT
+    assert rc(tokens=0, key=None, value=None, kc=None, vc=None, slots=None) == N.VFL_OK  # nothing to append
+    assert rc(head_dim=6) == N.VFL_ERR_UNSUPPORTED  # 12-byte rows: not a 16-byte multiple
+    assert rc(key=None) == N.VFL_ERR_INVALID_ARGUMENT
+    assert rc(slots=None) == N.VFL_ERR_INVALID_ARGUMENT
+    assert rc(kc=A + 8) == N.VFL_ERR_INVALID_ARGUMENT  # misaligned pool
+    assert rc(kstride=H * D + 4) == N.VFL_ERR_INVALID_ARGUMENT  # 8-byte token stride step in bf16
+    assert rc(vstride=H * D - 8) == N.VFL_ERR_INVALID_ARGUMENT  # shorter than a token
+    assert b"reshape_and_cache" in native.vfl_last_error_message()
+
+    def prep(table=A, stride=4, cols=4, positions=A, seqs=2, block_size=BS, slots=A):
+        return native.vfl_prepare_decode(table, stride, cols, positions, seqs, block_size, slots, A, A, None)
+
+    assert prep(seqs=-1) == N.VFL_ERR_INVALID_ARGUMENT
+    assert prep(block_size=0) == N.VFL_ERR_INVALID_ARGUMENT
+    assert prep(stride=3) == N.VFL_ERR_INVALID_ARGUMENT  # stride below the column count
+    assert prep(positions=None) == N.VFL_ERR_INVALID_ARGUMENT
+    assert prep(table=None) == N.VFL_ERR_INVALID_ARGUMENT  # slots asked for without a table
+
+    def slots(pages=A, stride=4, cols=4, reqs=2, seq_len=50, block_size=BS, out=A):
+        return native.vfl_paged_slots(pages, stride, cols, reqs, seq_len, block_size, out, None)
+
+    assert slots(reqs=-1) == N.VFL_ERR_INVALID_ARGUMENT
+    assert slots(block_size=0) == N.VFL_ERR_INVALID_ARGUMENT
+    assert slots(stride=2) == N.VFL_ERR_INVALID_ARGUMENT
+    assert slots(seq_len=0, pages=None, out=None) == N.VFL_OK  # no tokens
+    assert slots(out=None) == N.VFL_ERR_INVALID_ARGUMENT
