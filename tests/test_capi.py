@@ -307,3 +307,46 @@ def test_cache_ops_refuse_bad_arguments_before_the_device(native):
     assert slots(stride=2) == N.VFL_ERR_INVALID_ARGUMENT
     assert slots(seq_len=0, pages=None, out=None) == N.VFL_OK  # no tokens
     assert slots(out=None) == N.VFL_ERR_INVALID_ARGUMENT
+
+
+def test_selection_ops_refuse_bad_arguments_before_the_device(native):
+    """row_topk, beam_merge and fork_token_rows check dtypes, sizes, k and NULL pointers on the
+    host; empty work is a no-op. The stand-in addresses are never dereferenced."""
+    from vflorence_b200 import _native as N
+
+    A = 0x10000
+
+    def topk(scores=A, dtype=N.DTYPE_BF16, rows=4, vocab=1000, stride=1000, k=4, values=A, indices=A):
+        return native.vfl_row_topk(scores, dtype, rows, vocab, stride, 1, None, k, values, indices, None, 0, None)
+
+    assert topk(dtype=9) == N.VFL_ERR_UNSUPPORTED
+    assert topk(rows=-1) == N.VFL_ERR_INVALID_ARGUMENT
+    assert topk(vocab=0) == N.VFL_ERR_INVALID_ARGUMENT
+    assert topk(stride=999) == N.VFL_ERR_INVALID_ARGUMENT  # rows overlap
+    assert topk(k=0) == N.VFL_ERR_UNSUPPORTED
+    assert topk(k=65) == N.VFL_ERR_UNSUPPORTED             # beyond the largest supported k
+    assert topk(vocab=3, stride=3) == N.VFL_ERR_UNSUPPORTED  # k larger than the vocabulary
+    assert topk(rows=0, scores=None, values=None, indices=None) == N.VFL_OK
+    assert topk(values=None) == N.VFL_ERR_INVALID_ARGUMENT
+    assert topk(scores=A + 1) == N.VFL_ERR_INVALID_ARGUMENT  # bf16 scores at an odd address
+    # the merge workspace is needed only when few rows split each row across CTAs
+    assert native.vfl_row_topk_workspace_size(255, 51289, 6) == 0
+    assert native.vfl_row_topk_workspace_size(2, 51289, 6) > 0
+
+    def merge(values=A, indices=A, rows=6, k=4, groups=A, ranks=A, num_groups=2, keep=4, out=A):
+        return native.vfl_beam_merge(values, indices, rows, k, groups, ranks, num_groups, keep, out, None)
+
+    assert merge(k=0) == N.VFL_ERR_INVALID_ARGUMENT
+    assert merge(keep=0) == N.VFL_ERR_INVALID_ARGUMENT
+    assert merge(num_groups=-1) == N.VFL_ERR_INVALID_ARGUMENT
+    assert merge(num_groups=0, values=None, indices=None, groups=None, ranks=None, out=None) == N.VFL_OK
+    assert merge(ranks=None) == N.VFL_ERR_INVALID_ARGUMENT
+
+    def fork(tokens=A, stride=300, rows=8, width=257, born=A, num_born=3):
+        return native.vfl_fork_token_rows(tokens, stride, rows, width, born, num_born, None)
+
+    assert fork(width=0) == N.VFL_ERR_INVALID_ARGUMENT
+    assert fork(stride=256) == N.VFL_ERR_INVALID_ARGUMENT  # rows shorter than the width
+    assert fork(num_born=-1) == N.VFL_ERR_INVALID_ARGUMENT
+    assert fork(num_born=0, tokens=None, born=None) == N.VFL_OK
+    assert fork(born=None) == N.VFL_ERR_INVALID_ARGUMENT
