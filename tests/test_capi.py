@@ -350,3 +350,28 @@ def test_selection_ops_refuse_bad_arguments_before_the_device(native):
     assert fork(num_born=-1) == N.VFL_ERR_INVALID_ARGUMENT
     assert fork(num_born=0, tokens=None, born=None) == N.VFL_OK
     assert fork(born=None) == N.VFL_ERR_INVALID_ARGUMENT
+
+
+def test_kv_proj_paged_refuses_bad_arguments_before_the_device(native):
+    """The fused encoder K/V projection checks its GEMM shape (hidden a multiple of 64, head_dim
+    of 32, 2 x heads x head_dim of 128), pointers, alignment and the hidden row stride on the
+    host; no tokens is a no-op. The stand-in addresses are never dereferenced."""
+    from vflorence_b200 import _native as N
+
+    A = 0x10000
+
+    def proj(hidden=A, stride=1024, w=A, kc=A, vc=A, slots=A, tokens=590, hidden_dim=1024, heads=16, head_dim=64,
+             block_size=16, blocks=64):
+        return native.vfl_kv_proj_paged(hidden, stride, w, None, kc, vc, slots, tokens, hidden_dim, heads, head_dim,
+                                        block_size, blocks, None)
+
+    assert proj(hidden_dim=1000) == N.VFL_ERR_INVALID_ARGUMENT  # not a multiple of the 64-wide k-step
+    assert proj(head_dim=48) == N.VFL_ERR_INVALID_ARGUMENT      # head slices are 32-column chunks
+    assert proj(heads=1, head_dim=32) == N.VFL_ERR_UNSUPPORTED  # 2 x 1 x 32 = 64 features: not a 128 tile
+    assert proj(tokens=-1) == N.VFL_ERR_INVALID_ARGUMENT
+    assert proj(blocks=0) == N.VFL_ERR_INVALID_ARGUMENT
+    assert proj(tokens=0, hidden=None, w=None, kc=None, vc=None, slots=None) == N.VFL_OK
+    assert proj(slots=None) == N.VFL_ERR_INVALID_ARGUMENT
+    assert proj(w=A + 8) == N.VFL_ERR_INVALID_ARGUMENT          # TMA sources start on 16 bytes
+    assert proj(stride=1028) == N.VFL_ERR_INVALID_ARGUMENT      # 2056-byte rows: not a 16-byte multiple
+    assert proj(stride=512) == N.VFL_ERR_INVALID_ARGUMENT       # rows shorter than hidden_dim
