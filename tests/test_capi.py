@@ -375,3 +375,33 @@ def test_kv_proj_paged_refuses_bad_arguments_before_the_device(native):
     assert proj(w=A + 8) == N.VFL_ERR_INVALID_ARGUMENT          # TMA sources start on 16 bytes
     assert proj(stride=1028) == N.VFL_ERR_INVALID_ARGUMENT      # 2056-byte rows: not a 16-byte multiple
     assert proj(stride=512) == N.VFL_ERR_INVALID_ARGUMENT       # rows shorter than hidden_dim
+
+
+def test_copy_blocks_c_entry_refuses_bad_arguments_before_the_device(native):
+    """vfl_copy_blocks reads its per-layer pool pointers on the host and checks them (NULL,
+    16-byte alignment), the layer limit and the block size before any launch; no pairs or no
+    layers is a no-op. The stand-in pool addresses are never dereferenced."""
+    from vflorence_b200 import _native as N
+
+    A = 0x10000
+    pairs = (ctypes.c_int64 * 2)(0, 1)
+
+    def layers(*addrs):
+        return (ctypes.c_void_p * len(addrs))(*addrs)
+
+    def copy(k=None, v=None, num_layers=2, prs=pairs, num_pairs=1, blocks=8, block_bytes=32768):
+        k = layers(A, A) if k is None else k
+        v = layers(A, A) if v is None else v
+        return native.vfl_copy_blocks(k, v, num_layers, prs, num_pairs, blocks, block_bytes, None)
+
+    assert copy(num_pairs=-1) == N.VFL_ERR_INVALID_ARGUMENT
+    assert copy(blocks=0) == N.VFL_ERR_INVALID_ARGUMENT
+    assert copy(num_pairs=0, prs=None) == N.VFL_OK
+    assert copy(num_layers=0) == N.VFL_OK
+    big = layers(*([A] * (N.MAX_COPY_LAYERS + 1)))
+    assert copy(k=big, v=big, num_layers=N.MAX_COPY_LAYERS + 1) == N.VFL_ERR_UNSUPPORTED
+    assert copy(block_bytes=24) == N.VFL_ERR_INVALID_ARGUMENT
+    assert copy(prs=None) == N.VFL_ERR_INVALID_ARGUMENT
+    assert copy(k=layers(A, None)) == N.VFL_ERR_INVALID_ARGUMENT
+    assert copy(v=layers(A, A + 4)) == N.VFL_ERR_INVALID_ARGUMENT
+    assert b"layer 1" in native.vfl_last_error_message()
