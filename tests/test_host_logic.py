@@ -116,3 +116,24 @@ def test_bench_reference_arm_prints_one_line():
 def test_bench_reference_arm_other_ranks_exit_quietly():
     """Under torchrun only rank 0 runs the reference arm; the other ranks print nothing."""
     assert _bench_reference({"WORLD_SIZE": "2", "RANK": "1", "LOCAL_RANK": "1"}) == []
+
+
+def test_bench_clock_summary_reads_throttle_reasons(tmp_path, monkeypatch):
+    """bench.py's clock record: the median SM clock under load, the max clock, the peak power and
+    every throttle reason seen active in the nvidia-smi trace (a fake trace here, no GPU)."""
+    import bench
+
+    monkeypatch.setenv("VFL_CLOCKS_DIR", str(tmp_path))
+    cs = bench.ClockSampler(0)
+    with open(cs.path, "w") as f:
+        f.write("1965, 1965, 410.5, 0x0, Not Active, Not Active, Not Active, Not Active\n")
+        f.write("1770, 1965, 998.1, 0x4, Not Active, Not Active, Not Active, Active\n")
+        f.write("1755, 1965, 1001.0, 0x4, Not Active, Not Active, Not Active, Active\n")
+        f.write("garbled line\n")
+    cs.proc = object()  # as if nvidia-smi had run
+    s = cs.summary()
+    assert s["sm_mhz"] == 1770 and s["sm_max_mhz"] == 1965 and s["samples"] == 3
+    assert s["power_w_max"] == 1001.0 and s["reasons"] == ["sw_power_cap"]
+    with open(cs.path, "a") as f:
+        f.write("1500, 1965, 700.0, 0x40, Not Active, Active, Not Active, Not Active\n")
+    assert cs.summary()["reasons"] == ["hw_thermal_slowdown", "sw_power_cap"]
