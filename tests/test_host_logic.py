@@ -137,3 +137,29 @@ def test_bench_clock_summary_reads_throttle_reasons(tmp_path, monkeypatch):
     with open(cs.path, "a") as f:
         f.write("1500, 1965, 700.0, 0x40, Not Active, Active, Not Active, Not Active\n")
     assert cs.summary()["reasons"] == ["hw_thermal_slowdown", "sw_power_cap"]
+
+
+def test_bench_algorithmic_bytes_and_workload():
+    """The roofline numerator: the minimum HBM bytes of one bench step, by the formulas of the
+    measurement notes (K/V read once per token, q and out once per row, the table slice, lengths
+    and query offsets; the append reads and writes each new K/V row plus its slot; cross-attention
+    reads each encoder token once). And the workload's block tables are a permutation of the pool
+    whose slots land on each sequence's newest position."""
+    import bench
+
+    w = dict(batch=3, ctx=torch.tensor([1, 16, 17], dtype=torch.int32))
+    row = 16 * 64 * 2  # one token's K (or V) over 16 heads of 64, bf16
+    nb = bench.algorithmic_bytes(w)
+    assert nb["self"] == 2 * 34 * row + 2 * 3 * row + 4 * (1 + 1 + 2) + 4 * 3 + 4 * 4
+    assert nb["append"] == 4 * 3 * row + 8 * 3
+    assert nb["cross"] == 2 * 3 * 1024 * row + 2 * 3 * row + 4 * 3 * 64 + 4 * 3 + 4 * 4
+    assert nb["total"] == nb["self"] + nb["append"] + nb["cross"]
+
+    w = bench.make_workload(9, 2, None)
+    ctx, table, slots = w["ctx"], w["table"], w["slots"]
+    nblk = (ctx + 15) // 16
+    used = torch.cat([table[b, : nblk[b]] for b in range(9)])
+    assert sorted(used.tolist()) == list(range(w["n_self"]))
+    assert sorted(w["cross_table"].flatten().tolist()) == list(range(w["n_cross"]))
+    pos = (ctx - 1).long()
+    assert torch.equal(slots // 16, table[torch.arange(9), pos // 16].long()) and torch.equal(slots % 16, pos % 16)
