@@ -506,27 +506,22 @@ def run_split_sweep(args):
 
 def run_profile_step(args):
     """The workload of the decode-step launch list: the config's engine with CUDA graphs, one
-    wave of requests, 120 steps, then one step between torch.cuda.profiler.start() and stop()
-    (capture it with ncu --profile-from-start off)."""
+    wave of requests, 120 steps (half of max_tokens for shorter jobs), then one step between
+    torch.cuda.profiler.start() and stop() (capture it with ncu --profile-from-start off)."""
     from vflorence_b200.engine import Engine, SamplingParams
 
     device = torch.device("cuda", 0)
     torch.cuda.set_device(device)
-    cfg = decode_config(args.profile_step)
+    cfg, model, reqs = decode_setup(args.profile_step, device)
     params = SamplingParams.from_dict(cfg["params"])
-    cfg["num_requests"] = min(cfg["num_requests"], cfg["max_num_seqs"] // params.num_beams)
-    model = build_decode_model(cfg, device)
-    if cfg["kind"] == "florence2":
-        with torch.inference_mode():
-            px = torch.zeros(1, 3, 768, 768, device=device, dtype=cfg["dtype"])
-            cfg["image_tokens"] = model.model.get_image_features(px).pooler_output.shape[1]
+    reqs = reqs[: cfg["max_num_seqs"] // params.num_beams]
     eng = Engine(model, max_num_seqs=cfg["max_num_seqs"], max_decoder_len=cfg["max_decoder_len"],
                  max_encoder_len=cfg["max_encoder_len"], block_size=BS, cuda_graphs=True)
     eng.graphs.capture(cfg["max_num_seqs"], params.num_beams)
-    for r in decode_requests(cfg, device):
+    for r in reqs:
         eng.add_request(r, params)
     with torch.inference_mode():
-        for _ in range(120):
+        for _ in range(min(120, params.max_tokens // 2)):
             eng.step()
         torch.cuda.synchronize()
         torch.cuda.profiler.start()
@@ -602,11 +597,14 @@ def decode_config(name: str):
     raise ValueError(name)
 
 
-def build_decode_model(cfg, device):
+def build_decode_model(cfg, device, dtype=None):
+    """Random-init weights of the config's shape: drawn on the CPU from seed 0 (so every device,
+    and the reference engine's checkpoint of the same model, holds the same values), then moved
+    to ``device`` and cast to ``dtype`` (default: the config's)."""
     from transformers import BartConfig, BartForConditionalGeneration
 
     torch.manual_seed(0)
-    with torch.device(device):
+    with torch.device("cpu"):
         if cfg["kind"] == "bart":
             model = BartForConditionalGeneration(BartConfig(**cfg["text"]))
         else:
@@ -614,12 +612,28 @@ def build_decode_model(cfg, device):
 
             fc = Florence2Config(text_config=cfg["text"], vision_config=cfg["vision"], image_token_id=51289)
             model = Florence2ForConditionalGeneration(fc)
-    return model.to(cfg["dtype"]).eval()
+    return model.eval().to(device).to(dtype or cfg["dtype"])
 
 
-def decode_requests(cfg, device):
-    from vflorence_b200.engine import Request
+def decode_setup(name: str, device, dtype=None, request_cls=None):
+    """(config, model, requests) of a BASELINE decode config on ``device``; Florence-2 configs
+    learn their image-token count from the built vision tower."""
+    cfg = decode_config(name)
+    model = build_decode_model(cfg, device, dtype)
+    if cfg["kind"] == "florence2":
+        with torch.inference_mode():
+            px = torch.zeros(1, 3, 768, 768, device=device, dtype=dtype or cfg["dtype"])
+            cfg["image_tokens"] = model.model.get_image_features(px).pooler_output.shape[1]
+    return cfg, model, decode_requests(cfg, device, request_cls)
 
+
+def decode_requests(cfg, device, request_cls=None):
+    """The config's seeded requests as ``request_cls(input_ids, pixel_values)`` (default: the
+    engine's Request)."""
+    if request_cls is None:
+        from vflorence_b200.engine import Request as request_cls
+
+    Request = request_cls
     g = torch.Generator().manual_seed(cfg["id_seed"])
     reqs = []
     for i in range(cfg["num_requests"]):
@@ -634,27 +648,13 @@ def decode_requests(cfg, device):
     return reqs
 
 
-def decode_measure(name: str, world: int, rank: int, local: int, eager: bool = False) -> dict:
-    """End-to-end decode tokens/s of the engine around the paged path on one BASELINE config:
-    completion tokens of all requests / wall time of the whole job (max over ranks). The
-    requests are dealt to the ranks whole (strong scaling: the job is fixed). Synthetic:
-    random-init weights of the config's shape, seeded ids and N(0,1) images; EOS is disabled so
-    every request decodes exactly max_tokens tokens (random weights have no natural stop)."""
+def decode_generate(cfg, model, reqs, eager: bool = False, world: int = 1):
+    """The engine's job on ``reqs`` as the decode leg times it: start-up warm-up, then every
+    request encoded and decoded from scratch. Returns (generated tokens per request, seconds)."""
     from vflorence_b200.engine import Engine, SamplingParams
-    from vflorence_b200.sharding import assign_requests, max_over_ranks, sum_over_ranks
 
-    device = torch.device("cuda", local)
-    cfg = decode_config(name)
-    model = build_decode_model(cfg, device)
-    if cfg["kind"] == "florence2":
-        with torch.inference_mode():
-            px = torch.zeros(1, 3, 768, 768, device=device, dtype=cfg["dtype"])
-            cfg["image_tokens"] = model.model.get_image_features(px).pooler_output.shape[1]
-    reqs = decode_requests(cfg, device)
-    costs = [len(r.input_ids) + cfg["params"]["num_beams"] * cfg["params"]["max_tokens"] for r in reqs]
-    mine = [reqs[i] for i in assign_requests(costs, world)[rank]]
-    for r in mine:  # images wait in pinned host memory, as a pinned data loader hands them over
-        if r.pixel_values is not None:
+    for r in reqs:  # images wait in pinned host memory, as a pinned data loader hands them over
+        if r.pixel_values is not None and not r.pixel_values.is_pinned():
             r.pixel_values = r.pixel_values.pin_memory()
     params = SamplingParams.from_dict(cfg["params"])
     eng = Engine(model, max_num_seqs=cfg["max_num_seqs"], max_decoder_len=cfg["max_decoder_len"],
@@ -664,17 +664,33 @@ def decode_measure(name: str, world: int, rank: int, local: int, eager: bool = F
     # in the timed region and cost up to seconds), 4 tokens each; graphs for every batch size
     # this run can reach are captured up front. The timed run then encodes and decodes every
     # request from scratch.
-    wave = max(1, min(len(mine), cfg["max_num_seqs"] // params.num_beams))
-    eng.generate(mine[:wave], SamplingParams.from_dict(dict(cfg["params"], max_tokens=4)))
+    wave = max(1, min(len(reqs), cfg["max_num_seqs"] // params.num_beams))
+    eng.generate(reqs[:wave], SamplingParams.from_dict(dict(cfg["params"], max_tokens=4)))
     if eng.graphs is not None:
-        eng.graphs.capture(min(cfg["max_num_seqs"], len(mine) * params.num_beams), params.num_beams)
+        eng.graphs.capture(min(cfg["max_num_seqs"], len(reqs) * params.num_beams), params.num_beams)
     barrier(world)
     torch.cuda.synchronize()
     t0 = time.perf_counter()
-    outs = eng.generate(mine, params)
+    outs = eng.generate(reqs, params)
     torch.cuda.synchronize()
     elapsed = time.perf_counter() - t0
     barrier(world)
+    return outs, elapsed
+
+
+def decode_measure(name: str, world: int, rank: int, local: int, eager: bool = False) -> dict:
+    """End-to-end decode tokens/s of the engine around the paged path on one BASELINE config:
+    completion tokens of all requests / wall time of the whole job (max over ranks). The
+    requests are dealt to the ranks whole (strong scaling: the job is fixed). Synthetic:
+    random-init weights of the config's shape, seeded ids and N(0,1) images; EOS is disabled so
+    every request decodes exactly max_tokens tokens (random weights have no natural stop)."""
+    from vflorence_b200.sharding import assign_requests, max_over_ranks, sum_over_ranks
+
+    device = torch.device("cuda", local)
+    cfg, model, reqs = decode_setup(name, device)
+    costs = [len(r.input_ids) + cfg["params"]["num_beams"] * cfg["params"]["max_tokens"] for r in reqs]
+    mine = [reqs[i] for i in assign_requests(costs, world)[rank]]
+    outs, elapsed = decode_generate(cfg, model, mine, eager, world)
     tokens = sum(len(o) for o in outs)
     total_tokens = sum_over_ranks(float(tokens))
     wall = max_over_ranks(elapsed)

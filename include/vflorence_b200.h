@@ -99,6 +99,16 @@ const char* vfl_last_error_message(void);
 /* Read (and with clear != 0 reset) the current device's error word. Synchronises `stream`. */
 int vfl_read_device_errors(unsigned int* bits, int clear, void* stream);
 
+/* (new: failure detection, no reference counterpart - the reference's failure handling is
+ * host-side, vflorence/engine/llm_engine.py:68-80.) Exercises the bounded shared-memory wait
+ * every pipelined kernel uses: one CTA whose consumer warp waits on a barrier that the producer
+ * warp arrives on only when producer_arrives != 0. Otherwise the wait gives up after limit_ns
+ * (in (0, 2e9]; VFL_ERR_INVALID_ARGUMENT else), VFL_DEVERR_TIMEOUT is set in the device error
+ * word and the kernel exits; the context stays usable. Asynchronous on `stream`. Note: while
+ * VFL_DEVERR_TIMEOUT is set, attention launches exit at once - read and clear the word with
+ * vfl_read_device_errors before further work. */
+int vfl_check_bounded_wait(int producer_arrives, int64_t limit_ns, void* stream);
+
 /* ---- the four vllm_cpu_attn functions -------------------------------------------------------
  * replaces vllm_cpu_attn.get_isa(dtype, block_size, head_dim)
  *   (vflorence/engine/model_runner.py:38). Writes "sm100" into buf. Fails with

@@ -32,6 +32,13 @@ def test_library_exports_every_declared_symbol(native):
     assert native.vfl_abi_version() == _native.ABI_VERSION == 3
 
 
+def test_bounded_wait_check_refuses_limits_on_the_host(native):
+    """The wait limit must lie in (0, 2 s]; refused before any CUDA call."""
+    for limit in (0, -5, 2_000_000_001):
+        assert native.vfl_check_bounded_wait(0, limit, None) == 1
+        assert b"limit_ns" in native.vfl_last_error_message()
+
+
 def test_status_strings(native):
     assert native.vfl_status_string(0) == b"ok"
     assert b"workspace" in native.vfl_status_string(3)

@@ -1,0 +1,178 @@
+"""Token parity of the engine on BASELINE-shaped models against the reference engine's tokens
+(tests/golden/decode_tokens.json, made by tests/golden/make_decode_golden.py with the unmodified
+reference engine on the CPU).
+
+* tiny Florence-2 (DaViT tower, image-token splice, cross pages), fp32, greedy / 2 / 4 beams:
+  tokens identical to the reference engine's and to HuggingFace ``generate`` run here on the GPU
+  (the check of the reference's own test, vflorence tests/test_florence2.py:108-130);
+* BASELINE config 1 (BART-large shape, fp32, greedy) through bench.py's own decode job: ids
+  identical to the reference engine's for all 8 requests;
+* BASELINE configs 2-4 (bf16, beam search), first requests: bf16 arithmetic may flip near-tie
+  decisions (the reference itself accepts bf16 token drift, vflorence tests/verify_parity.py:59-67),
+  so the test measures each divergence against an fp32 re-score of both sequences with the same
+  weights: the position-wise matching fraction, and at the first divergence the fp32 log-prob
+  gap between the two tokens and the top-1/top-2 margin there. Set VFL_PARITY_REPORT to a path to
+  get these figures as JSON.
+
+Weights are rebuilt on the CPU from the seeds the fixture names and checked against its
+checksum before any comparison.
+"""
+
+from __future__ import annotations
+
+import copy
+import json
+import os
+import sys
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda", 0)
+HERE = os.path.dirname(os.path.abspath(__file__))
+REPO = os.path.dirname(HERE)
+sys.path.insert(0, REPO)
+sys.path.insert(0, os.path.join(HERE, "golden"))
+
+
+@pytest.fixture(scope="module")
+def golden():
+    with open(os.path.join(HERE, "golden", "decode_tokens.json")) as f:
+        return json.load(f)
+
+
+@pytest.fixture(autouse=True)
+def _exact_fp32():
+    """fp32 comparisons run with fp32 arithmetic (no TF32 in matmuls or the tower's convolutions)."""
+    old = torch.backends.cuda.matmul.allow_tf32, torch.backends.cudnn.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = torch.backends.cudnn.allow_tf32 = False
+    yield
+    torch.backends.cuda.matmul.allow_tf32, torch.backends.cudnn.allow_tf32 = old
+
+
+def _report(key: str, value) -> None:
+    path = os.environ.get("VFL_PARITY_REPORT")
+    if not path:
+        return
+    data = {}
+    if os.path.exists(path):
+        with open(path) as f:
+            data = json.load(f)
+    data[key] = value
+    with open(path, "w") as f:
+        json.dump(data, f, indent=1)
+
+
+# ------------------------------------------------------------------------------ tiny Florence-2
+
+@pytest.fixture(scope="module")
+def tiny(golden):
+    import make_decode_golden as mk
+
+    g = golden["florence2_tiny"]
+    model = mk.build_tiny_florence2()
+    assert mk.weights_checksum(model) == pytest.approx(g["weights_checksum"], rel=1e-12)
+    return model.to(DEV), mk.tiny_requests(g["num_image_tokens"]), g
+
+
+@pytest.mark.parametrize("graphs", [False, True], ids=["eager", "cuda_graphs"])
+@pytest.mark.parametrize("run_index", [0, 1, 2], ids=["greedy", "beam2_norepeat3", "beam4"])
+def test_florence2_tiny_tokens_match_reference_and_hf(tiny, run_index, graphs):
+    from vflorence_b200 import paged_ops
+    from vflorence_b200.engine import Engine, Request, SamplingParams
+
+    model, reqs, g = tiny
+    run = g["runs"][run_index]
+    eng = Engine(model, max_num_seqs=8, max_decoder_len=32, max_encoder_len=32, cuda_graphs=graphs)
+    tokens = eng.generate([Request(ids, px) for ids, px in reqs], SamplingParams.from_dict(run["sampling"]))
+    assert tokens == run["tokens"]
+    assert all(len(t) == run["params"]["max_tokens"] for t in tokens)
+    kw = {k: v for k, v in run["params"].items() if k != "max_tokens"}
+    for (ids, px), mine in zip(reqs, tokens):
+        with torch.no_grad():
+            hf = model.generate(input_ids=torch.tensor([ids], device=DEV), pixel_values=px[None].to(DEV),
+                                max_new_tokens=run["params"]["max_tokens"], do_sample=False, **kw)
+        assert hf[0].tolist()[1:] == mine
+    assert paged_ops.read_device_errors(DEV) == 0
+
+
+# ------------------------------------------------------------------------------ BASELINE cfg 1
+
+def test_cfg1_bench_decode_ids_match_reference_engine(golden):
+    """bench.py --decode cfg1's job (CUDA graphs, warm-up, all 8 requests) gives the reference
+    engine's greedy ids for every request."""
+    import bench
+    import make_decode_golden as mk
+    from vflorence_b200 import paged_ops
+
+    g = golden["cfg1"]
+    cfg, model, reqs = bench.decode_setup("cfg1", DEV)
+    assert mk.weights_checksum(model) == pytest.approx(g["weights_checksum"], rel=1e-12)
+    assert len(reqs) == g["requests"] == 8
+    outs, _ = bench.decode_generate(cfg, model, reqs)
+    margins = g["logit_margins"]
+    first = [next((i for i, (a, b) in enumerate(zip(o, t)) if a != b), None) for o, t in zip(outs, g["tokens"])]
+    _report("cfg1", {"identical": outs == g["tokens"], "first_divergence": first,
+                     "reference_min_margin": min(min(m) for m in margins),
+                     "margin_at_divergence": [None if p is None else margins[i][p] for i, p in enumerate(first)]})
+    assert outs == g["tokens"]
+    assert paged_ops.read_device_errors(DEV) == 0
+
+
+# ------------------------------------------------------------------------- BASELINE cfg 2-4 (bf16)
+
+def _decoder_logprobs(model, kind, enc_ids, px, dec_ids):
+    """fp32 log-probs [len(dec_ids), vocab] of every next token, teacher-forced."""
+    enc = torch.tensor([enc_ids], device=DEV)
+    dec = torch.tensor([dec_ids], device=DEV)
+    with torch.no_grad():
+        if kind == "florence2":
+            out = model(input_ids=enc, pixel_values=px[None].to(DEV, torch.float32), decoder_input_ids=dec)
+        else:
+            out = model(input_ids=enc, decoder_input_ids=dec)
+    return torch.log_softmax(out.logits[0].float(), dim=-1)
+
+
+@pytest.mark.parametrize("name", ["cfg2", "cfg3", "cfg4"])
+def test_bf16_config_tokens_against_reference(golden, name):
+    """bf16 beam search on the first requests of a BASELINE config: every request has its full
+    length, and every divergence from the reference engine's tokens is a near tie of the exact
+    (fp32) model - the fp32 score of our whole sequence is within 1 % of the reference's."""
+    import bench
+    import make_decode_golden as mk
+    from vflorence_b200 import paged_ops
+
+    g = golden[name]
+    cfg, model32, reqs = bench.decode_setup(name, DEV, dtype=torch.float32)
+    assert mk.weights_checksum(model32) == pytest.approx(g["weights_checksum"], rel=1e-12)
+    reqs = reqs[: g["requests"]]
+    model16 = copy.deepcopy(model32).to(torch.bfloat16)
+    outs, _ = bench.decode_generate(cfg, model16, reqs)
+    del model16
+    start = model32.config.get_text_config().decoder_start_token_id
+    rows = []
+    for r, mine, ref in zip(reqs, outs, g["tokens"]):
+        assert len(mine) == len(ref) == cfg["params"]["max_tokens"]
+        same = sum(a == b for a, b in zip(mine, ref))
+        p = next((i for i, (a, b) in enumerate(zip(mine, ref)) if a != b), None)
+        row = {"matching_fraction": same / len(ref), "first_divergence": p}
+        if p is not None:
+            lp_mine = _decoder_logprobs(model32, cfg["kind"], r.input_ids, r.pixel_values, [start] + mine)
+            lp_ref = _decoder_logprobs(model32, cfg["kind"], r.input_ids, r.pixel_values, [start] + ref)
+            at = lp_ref[p]
+            top2 = at.topk(2).values
+            cum_mine = float(lp_mine[torch.arange(len(mine)), torch.tensor(mine)].sum())
+            cum_ref = float(lp_ref[torch.arange(len(ref)), torch.tensor(ref)].sum())
+            row.update(fp32_logprob_gap_at_divergence=float(at[ref[p]] - at[mine[p]]),
+                       fp32_top1_top2_margin_at_divergence=float(top2[0] - top2[1]),
+                       fp32_cum_logprob_ours=cum_mine, fp32_cum_logprob_reference=cum_ref,
+                       fp32_score_rel_gap=(cum_ref - cum_mine) / abs(cum_ref))
+        rows.append(row)
+    total = sum(len(t) for t in g["tokens"])
+    frac = sum(r["matching_fraction"] * len(t) for r, t in zip(rows, g["tokens"])) / total
+    _report(name, {"requests": len(rows), "matching_fraction": frac, "per_request": rows})
+    for row in rows:
+        if row["first_divergence"] is not None:
+            assert row["fp32_score_rel_gap"] <= 0.01, row
+    assert paged_ops.read_device_errors(DEV) == 0

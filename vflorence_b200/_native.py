@@ -41,6 +41,7 @@ EXPORTS = (
     "vfl_status_string",
     "vfl_last_error_message",
     "vfl_read_device_errors",
+    "vfl_check_bounded_wait",
     "vfl_get_isa",
     "vfl_plan_attention",
     "vfl_plan_attention_row_tables",
@@ -162,6 +163,7 @@ def _declare(L):
         "vfl_status_string": (ctypes.c_char_p, [i32]),
         "vfl_last_error_message": (ctypes.c_char_p, []),
         "vfl_read_device_errors": (i32, [ctypes.POINTER(ctypes.c_uint), i32, vp]),
+        "vfl_check_bounded_wait": (i32, [i32, i64, vp]),
         "vfl_get_isa": (i32, [i32, i32, i32, ctypes.c_char_p, i32]),
         "vfl_plan_attention": (i32, [i32, i32, i32, i32, i32, i32, i32, vp, vp, plan_p]),
         "vfl_plan_attention_row_tables": (i32, [i32, i32, i32, i32, i32, i32, vp, vp, plan_p]),

@@ -99,9 +99,16 @@ def _(query, key, value, k_cache, v_cache, scale):
 
 @torch.library.custom_op("vflorence::cross_attention", mutates_args={})
 def decoder_cross_attention(query: torch.Tensor, layer_idx: int, scale: float) -> torch.Tensor:
-    """Cross-attention of decoder layer ``layer_idx`` over the staged encoder K/V pages."""
+    """Cross-attention of decoder layer ``layer_idx`` over the staged encoder K/V pages. Takes this
+    module's staging (6-tuples with the beams' grouped ``query_start_loc``) or the reference's
+    (5-tuples, one request per row, with the Context's ``query_start_loc``,
+    vflorence/layers/attention.py:97-109)."""
     ctx = get_context()
-    k_cache, v_cache, block_table, seq_lens, metadata, qsl = ctx.cross_staged[layer_idx]
+    staged = ctx.cross_staged[layer_idx]
+    if len(staged) == 5:
+        (k_cache, v_cache, block_table, seq_lens, metadata), qsl = staged, ctx.query_start_loc
+    else:
+        k_cache, v_cache, block_table, seq_lens, metadata, qsl = staged
     out = torch.empty_like(query)
     paged_ops.attention_with_kv_cache(query, k_cache, v_cache, out, qsl, seq_lens, scale=scale,
                                       causal=False, block_table=block_table, scheduler_metadata=metadata)

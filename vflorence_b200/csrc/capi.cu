@@ -18,6 +18,32 @@ __device__ unsigned int g_device_error_word = 0;
 std::atomic<unsigned int*> g_error_word_addr[vfl::kMaxDevices];
 std::mutex g_setup_mutex;
 
+// The bounded-wait path of the pipelined kernels, on its own: warp 0 waits (bounded) on a
+// shared-memory barrier that expects one arrival; warp 1 plays the producer and makes that
+// arrival only when `arrive` is set. Without it the wait gives up after `limit_ns`, warp 0
+// reports VFL_DEVERR_TIMEOUT and raises the CTA's abort flag, and both warps meet at the CTA
+// barrier and exit - the unwinding the attention kernels use.
+__global__ void __launch_bounds__(64) bounded_wait_check_kernel(int arrive, uint64_t limit_ns,
+                                                                unsigned int* err) {
+  __shared__ uint64_t full;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    vfl::mbar_init(&full, 1);
+    abort_flag = 0;
+    vfl::fence_barrier_init();
+  }
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (warp == 1) {
+    if (arrive && lane == 0) vfl::mbar_arrive(&full);
+  } else if (lane == 0 && !vfl::mbar_wait_bounded(&full, 0, limit_ns)) {
+    vfl::report(err, VFL_DEVERR_TIMEOUT);
+    abort_flag = 1;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0 && abort_flag == 0 && !arrive) vfl::report(err, VFL_DEVERR_QUERY);  // cannot happen
+}
+
 }  // namespace
 
 namespace vfl {
@@ -107,6 +133,18 @@ int vfl_read_device_errors(unsigned int* bits, int clear, void* stream) {
   if (st) return st;
   *bits = host;
   return VFL_OK;
+}
+
+int vfl_check_bounded_wait(int producer_arrives, int64_t limit_ns, void* stream) {
+  if (limit_ns <= 0 || limit_ns > static_cast<int64_t>(vfl::kWaitLimitNs))
+    return vfl::fail(VFL_ERR_INVALID_ARGUMENT, "limit_ns %lld: must be in (0, %llu]",
+                     static_cast<long long>(limit_ns), static_cast<unsigned long long>(vfl::kWaitLimitNs));
+  unsigned int* err = nullptr;
+  int st = vfl::device_error_word(&err);
+  if (st) return st;
+  bounded_wait_check_kernel<<<1, 64, 0, static_cast<cudaStream_t>(stream)>>>(
+      producer_arrives != 0, static_cast<uint64_t>(limit_ns), err);
+  return vfl::cuda_status(cudaGetLastError(), "bounded_wait_check_kernel launch");
 }
 
 int vfl_get_isa(int dtype, int block_size, int head_dim, char* buf, int buf_len) {

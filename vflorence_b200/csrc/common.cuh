@@ -151,10 +151,12 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return done != 0;
 }
 
-// Waits for phase `parity` of `bar` to complete; gives up after kWaitLimitNs of wall time and
-// returns false (the caller records VFL_DEVERR_TIMEOUT and unwinds without faulting).
+// Waits for phase `parity` of `bar` to complete; gives up after `limit_ns` of wall time
+// (kWaitLimitNs unless a caller passes a shorter one) and returns false (the caller records
+// VFL_DEVERR_TIMEOUT and unwinds without faulting).
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity,
+                                                  uint64_t limit_ns = kWaitLimitNs) {
 #pragma unroll 1
   for (int i = 0; i < 64; ++i)
     if (mbar_try_wait(bar, parity)) return true;
@@ -162,7 +164,7 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
 #pragma unroll 1
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (globaltimer_ns() - t0 > kWaitLimitNs) return false;
+    if (globaltimer_ns() - t0 > limit_ns) return false;
   }
 }
 

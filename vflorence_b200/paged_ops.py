@@ -13,9 +13,14 @@ meaning follow the call sites in vflorence (paths inside that project):
     paged_slots               replaces the encoder slot arithmetic of _encode, :240-242
 
 Differences a caller sees:
-  * tensors live on one CUDA device (caches, queries, outputs, block tables, lengths); a CPU
-    tensor is an error, never a silent copy. ``get_scheduler_metadata`` reads its lengths on the
-    host - pass host tensors (the engine has them), or it copies (and synchronises) once.
+  * caches, queries, keys, values and outputs live on one CUDA device; a CPU one is an error
+    (there is no CPU path). The small integer metadata may come from the host in the forms the
+    reference builds them (``slot_mapping``, ``seq_lens``, ``query_start_loc``, block tables made
+    by ``pad_sequence``; vflorence/layers/attention.py:9-39, model_runner.py:290-306): each such
+    tensor is uploaded inside the call, one copy on the current stream (pinned ones with a wait
+    for that copy, so the caller may reuse them at once). Device metadata costs no copy.
+    ``get_scheduler_metadata`` reads its lengths on the host - pass host tensors (the engine has
+    them), or it copies (and synchronises) once.
   * the metadata is a host int64 tensor holding a ``vfl_attention_plan``; pass the same device
     lengths to ``attention_with_kv_cache`` as were planned (longer ones are clamped and flagged).
   * several query rows of one request (``query_start_loc``) attend to the same pages, so beams
@@ -59,6 +64,16 @@ def _require_dense_rows(name: str, t: torch.Tensor) -> None:
     if t.dim() != 3 or t.stride(2) != 1 or t.stride(1) != t.shape[2]:
         raise ValueError(f"vflorence_b200: {name} must be [tokens, heads, head_dim] with dense "
                          f"heads (got shape {tuple(t.shape)}, strides {t.stride()})")
+
+
+def _on_device(name: str, t: torch.Tensor, device: torch.device) -> torch.Tensor:
+    """Integer metadata on ``device``: a host tensor (the reference's form) is uploaded on the
+    current stream - pageable memory is staged before the copy returns, pinned memory is waited
+    for - so the caller may change or free its tensor after the call."""
+    if t.device.type == "cpu":
+        return t.to(device, non_blocking=not t.is_pinned())
+    _require_cuda(name, t, device)
+    return t
 
 
 def _host_int32(t: torch.Tensor | None) -> torch.Tensor | None:
@@ -150,11 +165,12 @@ def plan_of(metadata: torch.Tensor) -> N.AttentionPlan:
 
 def reshape_and_cache(key: torch.Tensor, value: torch.Tensor, k_cache: torch.Tensor,
                       v_cache: torch.Tensor, slot_mapping: torch.Tensor, isa: str | None = None) -> None:
-    """``k_cache[s // bs, h, s % bs] = key[t, h]`` (same for value) for ``s = slot_mapping[t] >= 0``."""
+    """``k_cache[s // bs, h, s % bs] = key[t, h]`` (same for value) for ``s = slot_mapping[t] >= 0``.
+    ``slot_mapping`` may be a host tensor (uploaded inside the call)."""
     dev = k_cache.device
-    for name, t in (("key", key), ("value", value), ("k_cache", k_cache), ("v_cache", v_cache),
-                    ("slot_mapping", slot_mapping)):
+    for name, t in (("key", key), ("value", value), ("k_cache", k_cache), ("v_cache", v_cache)):
         _require_cuda(name, t, dev)
+    slot_mapping = _on_device("slot_mapping", slot_mapping, dev)
     _require_dense_rows("key", key)
     _require_dense_rows("value", value)
     if key.shape != value.shape or key.dtype != k_cache.dtype or value.dtype != v_cache.dtype:
@@ -177,11 +193,14 @@ def reshape_and_cache(key: torch.Tensor, value: torch.Tensor, k_cache: torch.Ten
 # ------------------------------------------------------------------- attention_with_kv_cache
 
 def _attention_checks(plan, query, k_cache, v_cache, output, query_start_loc, seq_lens, causal, block_table):
+    """Checks shared by the attention entry points. Returns (device, pool blocks, workspace,
+    query_start_loc, seq_lens, block_table) with the metadata on the device."""
     dev = k_cache.device
-    for name, t in (("query", query), ("k_cache", k_cache), ("v_cache", v_cache), ("output", output),
-                    ("query_start_loc", query_start_loc), ("seq_lens", seq_lens),
-                    ("block_table", block_table)):
+    for name, t in (("query", query), ("k_cache", k_cache), ("v_cache", v_cache), ("output", output)):
         _require_cuda(name, t, dev)
+    query_start_loc = _on_device("query_start_loc", query_start_loc, dev)
+    seq_lens = _on_device("seq_lens", seq_lens, dev)
+    block_table = _on_device("block_table", block_table, dev)
     _require_dense_rows("query", query)
     _require_dense_rows("output", output)
     n, h, bs, d = k_cache.shape
@@ -206,17 +225,19 @@ def _attention_checks(plan, query, k_cache, v_cache, output, query_start_loc, se
     ws = None
     if plan.workspace_bytes > 0:
         ws = torch.empty(plan.workspace_bytes, dtype=torch.uint8, device=dev)
-    return dev, n, ws
+    return dev, n, ws, query_start_loc, seq_lens, block_table
 
 
 def attention_with_kv_cache(query: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
                             output: torch.Tensor, query_start_loc: torch.Tensor,
                             seq_lens: torch.Tensor, scale: float, causal: bool,
                             block_table: torch.Tensor, scheduler_metadata: torch.Tensor) -> None:
-    """``output = softmax(scale * q K^T) V`` per request over its paged tokens (writes ``output``)."""
+    """``output = softmax(scale * q K^T) V`` per request over its paged tokens (writes ``output``).
+    ``query_start_loc``, ``seq_lens`` and ``block_table`` may be host tensors (uploaded inside the
+    call), as the reference passes them."""
     plan = plan_of(scheduler_metadata)
-    dev, n, ws = _attention_checks(plan, query, k_cache, v_cache, output, query_start_loc, seq_lens, causal,
-                                   block_table)
+    dev, n, ws, query_start_loc, seq_lens, block_table = _attention_checks(
+        plan, query, k_cache, v_cache, output, query_start_loc, seq_lens, causal, block_table)
     st = N.lib().vfl_attention_with_kv_cache(
         ctypes.byref(plan), query.data_ptr(), query.stride(0), k_cache.data_ptr(), v_cache.data_ptr(), n,
         output.data_ptr(), output.stride(0), query_start_loc.data_ptr(), seq_lens.data_ptr(),
@@ -245,10 +266,11 @@ def attention_with_kv_cache_append(query: torch.Tensor, key: torch.Tensor, value
     positions ending there, in a block no other row of the call holds. Plans for which
     ``attention_append_supported`` is False raise VflError."""
     plan = plan_of(scheduler_metadata)
-    dev, n, ws = _attention_checks(plan, query, k_cache, v_cache, output, query_start_loc, seq_lens, causal,
-                                   block_table)
-    for name, t in (("key", key), ("value", value), ("slot_mapping", slot_mapping)):
+    dev, n, ws, query_start_loc, seq_lens, block_table = _attention_checks(
+        plan, query, k_cache, v_cache, output, query_start_loc, seq_lens, causal, block_table)
+    for name, t in (("key", key), ("value", value)):
         _require_cuda(name, t, dev)
+    slot_mapping = _on_device("slot_mapping", slot_mapping, dev)
     _require_dense_rows("key", key)
     _require_dense_rows("value", value)
     if key.shape != value.shape or key.shape[1:] != query.shape[1:] or key.shape[0] < plan.total_q \
@@ -542,3 +564,16 @@ def read_device_errors(device: torch.device | int | None = None, clear: bool = T
         st = N.lib().vfl_read_device_errors(ctypes.byref(bits), int(bool(clear)), _stream(dev))
     N.check(st, "read_device_errors")
     return bits.value
+
+
+def check_bounded_wait(limit_ns: int, producer_arrives: bool = False,
+                       device: torch.device | int | None = None) -> None:
+    """Run the bounded shared-memory wait of the pipelined kernels on its own (one CTA) on the
+    current stream: without the producer's arrival it gives up after ``limit_ns`` and raises
+    VFL_DEVERR_TIMEOUT in the device error word (read it with ``read_device_errors``, which also
+    clears it; attention launches exit at once while the bit is set)."""
+    dev = torch.device("cuda", torch.cuda.current_device() if device is None else
+                       (device if isinstance(device, int) else device.index or 0))
+    with torch.cuda.device(dev):
+        st = N.lib().vfl_check_bounded_wait(int(bool(producer_arrives)), int(limit_ns), _stream(dev))
+    N.check(st, "check_bounded_wait")
