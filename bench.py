@@ -228,15 +228,17 @@ def cpu_baseline(batch: int, seconds: float = 10.0, sample: int = 32):
     n_self = int(nblk.sum())
     kc = torch.randn(n_self, H, BS, D, generator=g).to(DTYPE)
     vc = torch.randn(n_self, H, BS, D, generator=g).to(DTYPE)
+    # block tables: a random permutation of the sampled pool, as the GPU arm reads its pool
+    perm = torch.randperm(n_self, generator=g).to(torch.int32)
     table = torch.zeros(sample, int(nblk.max()), dtype=torch.int32)
     pos = 0
     for i in range(sample):
-        table[i, : nblk[i]] = torch.arange(pos, pos + int(nblk[i]), dtype=torch.int32)
+        table[i, : nblk[i]] = perm[pos: pos + int(nblk[i])]
         pos += int(nblk[i])
     cw = math.ceil(ENC_LEN / BS)
     ck = torch.randn(sample * cw, H, BS, D, generator=g).to(DTYPE)
     cv = torch.randn(sample * cw, H, BS, D, generator=g).to(DTYPE)
-    ctab = torch.arange(sample * cw, dtype=torch.int32).view(sample, cw)
+    ctab = torch.randperm(sample * cw, generator=g).to(torch.int32).view(sample, cw)
     q = torch.randn(sample, H, D, generator=g).to(DTYPE)
     kn, vn = torch.randn(sample, H, D, generator=g).to(DTYPE), torch.randn(sample, H, D, generator=g).to(DTYPE)
     p = ctx.long() - 1
@@ -259,9 +261,36 @@ def cpu_baseline(batch: int, seconds: float = 10.0, sample: int = 32):
     full = algorithmic_bytes(w)["total"]
     return {"value": nbytes * reps / el / 1e9, "unit": "GB/s", "cores": threads, "kind": "port",
             "seconds_per_full_step": el / reps * full / nbytes,
-            "sample": f"{sample} of the {batch} sequences (self ctx U[1,4096] + cross enc {ENC_LEN}), "
-                      f"{reps} repetitions in {el:.1f} s",
+            "sample": f"{sample} of the {batch} sequences (self ctx U[1,4096] + cross enc {ENC_LEN}; block "
+                      f"tables a random permutation of the sampled pools), {reps} repetitions in {el:.1f} s",
             "seconds_per_step": el / reps}
+
+
+def reference_engine_cpu(name: str, requests: int = 0, timeout: float = 1800.0) -> dict:
+    """The reference's own decode engine timed on this host's cores: the unmodified vflorence
+    installed under baseline/_ref, with the C restatement of vllm_cpu_attn standing in for the
+    library, on the bench's decode workload (same weights, requests and sampling; first
+    ``requests`` requests when > 0). A child process without the GPU: the reference registers
+    the same custom-op names as this package, and it is a CPU figure."""
+    root = os.path.join(REPO, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(root, "vflorence")):
+        return {"unavailable": "the reference is not installed under baseline/_ref"}
+    threads = host_threads()
+    cmd = [sys.executable, os.path.join(REPO, "oracle", "reference_engine_cpu.py"), "--reference-root", root,
+           "--configs", name, "--threads", str(threads)] + (["--requests", str(requests)] if requests else [])
+    env = dict(os.environ, CUDA_VISIBLE_DEVICES="", OMP_NUM_THREADS=str(threads))
+    try:
+        res = subprocess.run(cmd, capture_output=True, text=True, timeout=timeout, env=env, cwd=REPO)
+    except subprocess.TimeoutExpired:
+        return {"unavailable": f"reference CPU engine did not finish within {timeout:.0f} s"}
+    lines = [ln for ln in res.stdout.splitlines() if ln.startswith("{")]
+    if res.returncode != 0 or not lines:
+        return {"unavailable": f"reference CPU engine exited {res.returncode}: {res.stderr.strip()[-200:]}"}
+    r = json.loads(lines[-1])
+    return {"value": r["value"], "unit": "tokens/s", "cores": r["threads"], "kind": "reference",
+            "sample": f"{r['requests']} of the {r['of_requests']} requests, {r['completion_tokens']} tokens in "
+                      f"{r['wall_s']:.1f} s (unmodified vflorence, C restatement of vllm_cpu_attn, compile=False)",
+            "cpu": r.get("cpu")}
 
 
 # -------------------------------------------------------------------------------------- sweep
@@ -648,9 +677,43 @@ def decode_requests(cfg, device, request_cls=None):
     return reqs
 
 
-def decode_generate(cfg, model, reqs, eager: bool = False, world: int = 1):
+def poisson_arrivals(n: int, rate: float, seed: int = 7) -> list[float]:
+    """Arrival offsets (seconds) of ``n`` requests of a Poisson process with ``rate`` per second:
+    cumulative sums of seeded exponential gaps."""
+    g = torch.Generator().manual_seed(seed)
+    gaps = torch.empty(n, dtype=torch.float64).exponential_(rate, generator=g)
+    return torch.cumsum(gaps, 0).tolist()
+
+
+def serve_arrivals(eng, reqs, params, arrivals):
+    """Continuous batching with arrivals, as a server loop drives the reference's engine
+    (vflorence/engine/llm_engine.py:34-63): each request is added when its arrival time has
+    passed, a step runs whenever anything is admitted or waiting, and the loop idles only when
+    nothing is. Returns (outputs in request order, per-request latency in seconds from arrival
+    to the step that finished it)."""
+    t0 = time.perf_counter()
+    rid_of, arrived, latency = [], {}, {}
+    i = 0
+    while i < len(reqs) or not eng.is_finished():
+        now = time.perf_counter() - t0
+        while i < len(reqs) and arrivals[i] <= now:
+            rid = eng.add_request(reqs[i], params)
+            rid_of.append(rid)
+            arrived[rid] = arrivals[i]
+            i += 1
+        if eng.is_finished():
+            time.sleep(max(0.0, arrivals[i] - (time.perf_counter() - t0)))
+            continue
+        for rid in eng.step():
+            latency[rid] = time.perf_counter() - t0 - arrived[rid]
+    return [eng.outputs.pop(r) for r in rid_of], [latency[r] for r in rid_of]
+
+
+def decode_generate(cfg, model, reqs, eager: bool = False, world: int = 1, arrivals=None, timer=None):
     """The engine's job on ``reqs`` as the decode leg times it: start-up warm-up, then every
-    request encoded and decoded from scratch. Returns (generated tokens per request, seconds)."""
+    request encoded and decoded from scratch - all queued at the start, or added at their
+    ``arrivals`` (seconds from the start). ``timer``: a PhaseTimer bracketing the job's phases.
+    Returns (generated tokens per request, seconds, per-request latencies or None)."""
     from vflorence_b200.engine import Engine, SamplingParams
 
     for r in reqs:  # images wait in pinned host memory, as a pinned data loader hands them over
@@ -668,43 +731,93 @@ def decode_generate(cfg, model, reqs, eager: bool = False, world: int = 1):
     eng.generate(reqs[:wave], SamplingParams.from_dict(dict(cfg["params"], max_tokens=4)))
     if eng.graphs is not None:
         eng.graphs.capture(min(cfg["max_num_seqs"], len(reqs) * params.num_beams), params.num_beams)
+    eng.timer = timer
     barrier(world)
     torch.cuda.synchronize()
     t0 = time.perf_counter()
-    outs = eng.generate(reqs, params)
+    latency = None
+    with torch.inference_mode():
+        if arrivals is None:
+            outs = eng.generate(reqs, params)
+        else:
+            outs, latency = serve_arrivals(eng, reqs, params, arrivals)
     torch.cuda.synchronize()
     elapsed = time.perf_counter() - t0
     barrier(world)
-    return outs, elapsed
+    return outs, elapsed, latency
 
 
-def decode_measure(name: str, world: int, rank: int, local: int, eager: bool = False) -> dict:
+def decode_measure(name: str, world: int, rank: int, local: int, eager: bool = False,
+                   arrival_rate: float = 0.0, setup=None) -> dict:
     """End-to-end decode tokens/s of the engine around the paged path on one BASELINE config:
     completion tokens of all requests / wall time of the whole job (max over ranks). The
-    requests are dealt to the ranks whole (strong scaling: the job is fixed). Synthetic:
+    requests are dealt to the ranks whole (strong scaling: the job is fixed); with
+    ``arrival_rate`` > 0 they arrive as a seeded Poisson process instead of all at the start, and
+    the line adds per-request latency percentiles. ``per_rank`` splits each rank's job into the
+    vision tower, text encoder, encoder K/V paging and decode steps (CUDA-event time), plus its
+    start-up (weights, warm-up, graph capture). ``setup``: a ready (cfg, model, requests).
+    Synthetic:
     random-init weights of the config's shape, seeded ids and N(0,1) images; EOS is disabled so
     every request decodes exactly max_tokens tokens (random weights have no natural stop)."""
-    from vflorence_b200.sharding import assign_requests, max_over_ranks, sum_over_ranks
+    from vflorence_b200.engine.timing import PhaseTimer
+    from vflorence_b200.sharding import assign_requests, gather_to_rank0, max_over_ranks, sum_over_ranks
 
     device = torch.device("cuda", local)
-    cfg, model, reqs = decode_setup(name, device)
+    t_start = time.perf_counter()
+    cfg, model, reqs = setup if setup is not None else decode_setup(name, device)
     costs = [len(r.input_ids) + cfg["params"]["num_beams"] * cfg["params"]["max_tokens"] for r in reqs]
-    mine = [reqs[i] for i in assign_requests(costs, world)[rank]]
-    outs, elapsed = decode_generate(cfg, model, mine, eager, world)
+    shard = assign_requests(costs, world)[rank]
+    mine = [reqs[i] for i in shard]
+    arrivals = None
+    if arrival_rate > 0:  # the job's arrival times; each rank serves its own requests as they arrive
+        every = poisson_arrivals(len(reqs), arrival_rate)
+        arrivals = [every[i] for i in shard]
+    timer = PhaseTimer()
+    outs, elapsed, latency = decode_generate(cfg, model, mine, eager, world, arrivals, timer)
+    startup = time.perf_counter() - t_start - elapsed
     tokens = sum(len(o) for o in outs)
+    phases = {k: round(v / 1e3, 4) if k != "steps" else v for k, v in timer.summary().items()}
+    per_rank = gather_to_rank0({"rank": rank, "requests": len(mine), "tokens": tokens, "wall_s": round(elapsed, 4),
+                                "startup_s": round(startup, 2), "phases_s": phases})
     total_tokens = sum_over_ranks(float(tokens))
     wall = max_over_ranks(elapsed)
-    return {"metric": "decode tokens/s", "config": name, "value": total_tokens / wall, "unit": "tokens/s",
+    line = {"metric": "decode tokens/s", "config": name, "value": total_tokens / wall, "unit": "tokens/s",
             "n_gpus": world, "scaling": "strong", "requests": cfg["num_requests"],
             "completion_tokens": int(total_tokens), "wall_s": wall, "params": cfg["params"],
             "dtype": str(cfg["dtype"]).replace("torch.", ""), "max_num_seqs": cfg["max_num_seqs"],
-            "cuda_graphs": not eager, "data": "synthetic (random-init weights)"}
+            "cuda_graphs": not eager, "data": "synthetic (random-init weights)",
+            "arrivals": (f"Poisson, {arrival_rate:g} requests/s (seed 7), dealt to ranks by request"
+                         if arrivals is not None else "all queued at the start (offline)"),
+            "per_rank": per_rank}
+    if latency is not None:
+        lat = sorted(x for r in gather_to_rank0(latency) or [] for x in r) if world > 1 else sorted(latency)
+        if lat:
+            line["latency_s"] = {"p50": lat[len(lat) // 2], "p90": lat[int(0.9 * (len(lat) - 1))], "max": lat[-1]}
+    return line
+
+
+def decode_legs(name: str, world: int, rank: int, local: int, eager: bool = False, arrival_rate: float = 0.0):
+    """The offline job, then - with ``arrival_rate`` > 0 - the same requests arriving as a Poisson
+    process, on the same weights (built once). One line; the Poisson job under ``poisson``."""
+    if world > 1:  # ranks share the host's cores while they build their weights
+        torch.set_num_threads(max(1, (os.cpu_count() or 8) // world))
+    t0 = time.perf_counter()
+    setup = decode_setup(name, torch.device("cuda", local))
+    build_s = time.perf_counter() - t0
+    line = decode_measure(name, world, rank, local, eager, setup=setup)
+    if arrival_rate > 0:
+        p = decode_measure(name, world, rank, local, eager, arrival_rate, setup=setup)
+        line["poisson"] = {k: p[k] for k in ("value", "unit", "wall_s", "arrivals", "latency_s", "per_rank") if k in p}
+    line["weights_build_s"] = round(build_s, 2)
+    return line
 
 
 def run_decode(args):
     world, rank, local = dist_setup()
     torch.cuda.set_device(torch.device("cuda", local))
-    line = decode_measure(args.decode, world, rank, local, args.eager)
+    line = decode_legs(args.decode, world, rank, local, args.eager, args.arrival_rate or 0.0)
+    if rank == 0 and args.cpu_engine:
+        line["cpu_baseline"] = reference_engine_cpu(args.decode, args.cpu_engine_requests)
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -741,11 +854,13 @@ def run_reference(args, world, rank):
     if rank != 0:
         return
     cb = cpu_baseline(args.batch, seconds=max(1.0, 0.05 * (args.steps + args.warmup)), sample=args.cpu_sample)
+    # ms_per_step: the sample's time per step scaled by bytes to the full step (not a timed full step)
     line = {"impl": "reference", "metric": METRIC, "value": cb["value"], "unit": "GB/s", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": cb["seconds_per_full_step"] * 1e3,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic", "config": config_of(args, world),
-            "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
+            "cpu_baseline": dict({k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
+                                 ms_per_step="the sample's time per step scaled by bytes to the full step"),
             "e2e": {"value": cb["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -779,6 +894,14 @@ def main():
     ap.add_argument("--decode", choices=["cfg1", "cfg2", "cfg3", "cfg4"], default=None,
                     help="end-to-end decode tokens/s of the engine on a BASELINE config")
     ap.add_argument("--eager", action="store_true", help="decode without CUDA graphs")
+    ap.add_argument("--cpu-engine", action="store_true",
+                    help="--decode: also time the reference's own decode engine on the host cores")
+    ap.add_argument("--cpu-engine-requests", type=int, default=0,
+                    help="requests of the reference CPU engine timing (0: all with --cpu-engine; the "
+                         "default run's decode leg uses 3)")
+    ap.add_argument("--arrival-rate", type=float, default=None,
+                    help="decode: also serve the requests arriving as a Poisson process at this many per "
+                         "second (default run: 1000 for cfg4; --decode: off)")
     ap.add_argument("--decode-config", default="cfg4", choices=["cfg1", "cfg2", "cfg3", "cfg4", "none"],
                     help="engine config measured after the kernel leg of the default run ('none' skips it)")
     args = ap.parse_args()
@@ -936,11 +1059,15 @@ def main():
         del w, step, d, host_in, host_meta, host_all, dev_sets, dev_outs, host_outs
         torch.cuda.empty_cache()
         try:
-            decode = decode_measure(args.decode_config, world, rank, local)
+            rate = args.arrival_rate if args.arrival_rate is not None else (1000.0 if args.decode_config == "cfg4" else 0.0)
+            decode = decode_legs(args.decode_config, world, rank, local, arrival_rate=rate)
         except Exception as exc:  # the kernel line stands even if the engine leg fails
             decode = {"config": args.decode_config, "error": f"{type(exc).__name__}: {exc}"[:300]}
 
     cb = None
+    if (rank == 0 and world == 1 and not args.no_cpu_baseline and isinstance(decode, dict)
+            and "error" not in decode):  # the reference's own engine beside the decode figure, N=1 only
+        decode["cpu_baseline"] = reference_engine_cpu(args.decode_config, args.cpu_engine_requests or 3)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:  # reported at N=1 only
         cb = cpu_baseline(args.batch, seconds=args.cpu_seconds, sample=args.cpu_sample)
         cb.pop("seconds_per_step", None)

@@ -15,8 +15,9 @@ decode tokens/s = completion tokens of all requests / wall time of the whole job
 included), as the reference counts them (vflorence/engine/llm_engine.py:114-118), with the
 thread count. A short warm-up job (two requests, 4 tokens) runs first.
 
-The reference does not travel to the GPU boxes, so this runs where the reference is checked out;
-the figure it prints is a reported CPU baseline, not something the product calls.
+``bench.py`` runs this script as a child process (its cpu-baseline leg) with the reference
+installed under ``baseline/_ref``, which travels with the tree; the figure it prints is a
+reported CPU baseline, not something the product calls.
 """
 
 from __future__ import annotations
@@ -149,7 +150,9 @@ def main():
             llm = LLM(path, max_num_seqs=cfg["max_num_seqs"], dtype=cfg["dtype"], compile=False,
                       max_decoder_len=cfg["max_decoder_len"], max_encoder_len=cfg["max_encoder_len"])
             assert llm.config.block_size == 16
-            params = SamplingParams(**cfg["params"])
+            # no forced EOS (the bench workload's rules; [] is the reference's "none" form, where
+            # the checkpoint's generation config would force EOS at the last position)
+            params = SamplingParams(**dict(cfg["params"], forced_eos_token_id=[]))
             # warm-up images are blank, so no timed image is already in the engine's embedding cache
             warm = [Request(ids, None if px is None else torch.zeros_like(px)) for ids, px in reqs[:2]]
             llm.generate(warm, SamplingParams(**dict(cfg["params"], max_tokens=4)), use_tqdm=False)

@@ -2,7 +2,7 @@
 BASELINE-shaped decode workloads (run once, where the reference is checked out).
 
     python tests/golden/make_decode_golden.py --reference-root <vflorence checkout> \
-        [--only florence2_tiny,cfg1,cfg2,cfg3,cfg4] [--bf16-requests 4]
+        [--only florence2_tiny,cfg1,cfg2,cfg3,cfg4,cfg2_fp32,cfg3_fp32,cfg4_fp32] [--bf16-requests 4]
 
 The reference engine (``vflorence.LLM``, block size 16, ``compile=False``) runs on this machine's
 CPU with ``oracle/vllm_cpu_attn`` (the C restatement) standing in for the un-installable
@@ -19,6 +19,8 @@ the fixture keeps a checksum of the weights so a test can tell that it rebuilt t
   two best logits of every row (how far each greedy decision was from a tie).
 * ``cfg2``..``cfg4``: the first ``--bf16-requests`` requests of BASELINE configs 2-4 (bf16, beam
   search) as bench.py builds them.
+* ``cfg2_fp32``..``cfg4_fp32``: the same requests and weights with fp32 arithmetic, where token
+  identity is the bar (bf16 runs on two machines may take different beam paths).
 
 The bench configs disable EOS and carry no forced EOS, so the reference is given
 ``forced_eos_token_id=[]`` (its "none" form; the checkpoint's generation config would force EOS
@@ -137,8 +139,9 @@ def florence2_tiny(vf) -> dict:
     return {"model": TINY, "num_image_tokens": n_img, "weights_checksum": weights_checksum(model), "runs": runs}
 
 
-def bench_config(vf, name: str, num_requests: int | None) -> dict:
-    """The reference engine on a BASELINE config as bench.py --decode builds it."""
+def bench_config(vf, name: str, num_requests: int | None, dtype=None) -> dict:
+    """The reference engine on a BASELINE config as bench.py --decode builds it (in ``dtype``
+    instead of the config's when given)."""
     sys.path.insert(0, REPO)
     import bench
 
@@ -146,6 +149,8 @@ def bench_config(vf, name: str, num_requests: int | None) -> dict:
     # the reference's own Request type: the product package is never imported here (it registers
     # custom ops under the reference's op names)
     cfg, model, reqs = bench.decode_setup(name, torch.device("cpu"), dtype=torch.float32, request_cls=vf.Request)
+    if dtype is not None:
+        cfg["dtype"] = dtype
     assert "vflorence_b200" not in sys.modules
     checksum = weights_checksum(model)
     if num_requests:
@@ -188,7 +193,7 @@ def bench_config(vf, name: str, num_requests: int | None) -> dict:
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference-root", required=True, help="vflorence checkout")
-    ap.add_argument("--only", default="florence2_tiny,cfg1,cfg2,cfg3,cfg4")
+    ap.add_argument("--only", default="florence2_tiny,cfg1,cfg2,cfg3,cfg4,cfg2_fp32,cfg3_fp32,cfg4_fp32")
     ap.add_argument("--bf16-requests", type=int, default=4)
     args = ap.parse_args()
     vf = _reference(args.reference_root)
@@ -199,6 +204,8 @@ def main():
     for name in args.only.split(","):
         if name == "florence2_tiny":
             data[name] = florence2_tiny(vf)
+        elif name.endswith("_fp32"):  # a bf16 config's first requests with fp32 arithmetic
+            data[name] = bench_config(vf, name[: -len("_fp32")], args.bf16_requests, torch.float32)
         else:
             data[name] = bench_config(vf, name, None if name == "cfg1" else args.bf16_requests)
         with open(OUT, "w") as f:

@@ -40,12 +40,14 @@ def test_tiny_florence2_rebuilds_to_the_fixture_weights(golden):
             assert run["sampling"][k] == v
 
 
-@pytest.mark.parametrize("name", ["cfg1", "cfg2", "cfg3", "cfg4"])
+@pytest.mark.parametrize("name", ["cfg1", "cfg2", "cfg3", "cfg4", "cfg2_fp32", "cfg3_fp32", "cfg4_fp32"])
 def test_bench_entries_use_bench_sampling(golden, name):
     import bench
     from vflorence_b200.engine import SamplingParams
 
-    g, cfg = golden[name], bench.decode_config(name)
+    g, cfg = golden[name], bench.decode_config(name.split("_")[0])
+    if name.endswith("_fp32"):
+        cfg["dtype"] = torch.float32
     eff = SamplingParams.from_dict(g["sampling"])
     ours = SamplingParams.from_dict(cfg["params"])
     assert eff.forced_eos_token_id == [] and ours.forced_eos_token_id is None  # both: no forced EOS

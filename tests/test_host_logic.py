@@ -10,6 +10,7 @@ import json
 import os
 import subprocess
 import sys
+import time
 
 import torch
 
@@ -163,3 +164,52 @@ def test_bench_algorithmic_bytes_and_workload():
     assert sorted(w["cross_table"].flatten().tolist()) == list(range(w["n_cross"]))
     pos = (ctx - 1).long()
     assert torch.equal(slots // 16, table[torch.arange(9), pos // 16].long()) and torch.equal(slots % 16, pos % 16)
+
+
+class _FakeEngine:
+    """Engine stand-in for the arrival loop: each request finishes 3 steps after its admission."""
+
+    def __init__(self):
+        self.queue, self.outputs, self.added_at, self.step_count = [], {}, {}, 0
+        self.next = 0
+
+    def add_request(self, req, params):
+        rid = self.next
+        self.next += 1
+        self.queue.append([rid, 3])
+        self.added_at[rid] = time.perf_counter()
+        return rid
+
+    def is_finished(self):
+        return not self.queue
+
+    def step(self):
+        self.step_count += 1
+        done = []
+        for item in self.queue:
+            item[1] -= 1
+            if item[1] == 0:
+                done.append(item[0])
+                self.outputs[item[0]] = [item[0]] * 2
+        self.queue = [q for q in self.queue if q[1] > 0]
+        return done
+
+
+def test_poisson_arrivals_and_serving_loop():
+    """bench.py's arrival process is seeded and increasing with the stated mean gap; the serving
+    loop adds no request before its arrival time, returns outputs in request order and a
+    non-negative latency per request."""
+    import bench
+
+    a = bench.poisson_arrivals(2000, 500.0)
+    assert a == bench.poisson_arrivals(2000, 500.0)
+    assert all(x < y for x, y in zip(a, a[1:]))
+    assert abs(a[-1] / 2000 - 1 / 500) < 0.1 / 500
+    arrivals = [0.0, 0.0, 0.02, 0.05]
+    eng = _FakeEngine()
+    t0 = time.perf_counter()
+    outs, lat = bench.serve_arrivals(eng, ["r0", "r1", "r2", "r3"], None, arrivals)
+    assert outs == [[0, 0], [1, 1], [2, 2], [3, 3]]
+    assert all(x >= 0 for x in lat) and len(lat) == 4
+    for rid, t in eng.added_at.items():
+        assert t - t0 >= arrivals[rid] - 1e-3

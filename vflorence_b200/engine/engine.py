@@ -17,6 +17,7 @@ the host decode runtime (``vflorence_b200.runtime``, C++); Python handles whole 
 
 from __future__ import annotations
 
+import contextlib
 import math
 from collections import deque
 from dataclasses import dataclass
@@ -94,6 +95,8 @@ class Engine:
         self._next_id = 0
         self._rules: tuple[SamplingParams, LogitsRules, DecodeRules] | None = None
         self.record = [] if record_steps else None
+        # a PhaseTimer (engine.timing) to bracket the job's phases with CUDA events, or None
+        self.timer = None
         self.graphs = None
         if cuda_graphs:
             from .graphs import GraphedDecoder
@@ -160,6 +163,16 @@ class Engine:
     # ------------------------------------------------------------------------------------ step
     @torch.inference_mode()
     def step(self) -> list[int]:
+        """One decode step; returns the ids of the requests it finished."""
+        if self.timer is None:
+            return self._step()
+        with self.timer("step"):
+            return self._step()
+
+    def _phase(self, name: str):
+        return self.timer(name) if self.timer is not None else contextlib.nullcontext()
+
+    def _step(self) -> list[int]:
         params = self._admit()
         n = self.rt.num_running
         if n == 0:
@@ -258,14 +271,16 @@ class Engine:
                 pix = torch.empty((len(batch),) + px, dtype=batch[0].pixel_values.dtype, device=self.device)
                 for i, s in enumerate(batch):
                     pix[i].copy_(s.pixel_values, non_blocking=True)
-            hidden = self.model.encode(ids, pix, up(mask) if ragged else None)
-            for layer in range(len(self.model.layers)):
-                if self.fused_encoder_kv:
-                    L = self.model.layers[layer]
-                    self.kv.project_encoder_kv(layer, hidden.reshape(-1, self.model.d_model), L.w_kv, L.b_kv, slots)
-                else:
-                    k, v = self.model.cross_kv(layer, hidden)
-                    self.kv.write_encoder_kv(layer, k, v, slots)
+            hidden = self.model.encode(ids, pix, up(mask) if ragged else None, phase=self._phase)
+            with self._phase("encoder_kv_pages"):
+                for layer in range(len(self.model.layers)):
+                    if self.fused_encoder_kv:
+                        L = self.model.layers[layer]
+                        self.kv.project_encoder_kv(layer, hidden.reshape(-1, self.model.d_model), L.w_kv, L.b_kv,
+                                                   slots)
+                    else:
+                        k, v = self.model.cross_kv(layer, hidden)
+                        self.kv.write_encoder_kv(layer, k, v, slots)
 
     def _beam_groups(self, rows: StepRows) -> dict:
         """Self-attention groups of an eager beam step: runs of consecutive rows of one request

@@ -14,6 +14,7 @@ launch of ``paged_ops.add_layernorm`` where it is built for the model's width an
 
 from __future__ import annotations
 
+import contextlib
 from types import SimpleNamespace
 
 import torch
@@ -89,17 +90,22 @@ class PagedSeq2Seq:
     # ------------------------------------------------------------------------------- encoder
     @torch.inference_mode()
     def encode(self, input_ids: torch.Tensor, pixel_values: torch.Tensor | None = None,
-               attention_mask: torch.Tensor | None = None) -> torch.Tensor:
+               attention_mask: torch.Tensor | None = None, phase=None) -> torch.Tensor:
         """Encoder hidden states [G, S, d_model] for a batch of prompts (right-padded and masked
-        when their lengths differ; padded positions are never paged)."""
+        when their lengths differ; padded positions are never paged). ``phase(name)`` returns a
+        context manager bracketing the vision tower and the text encoder (timing), if given."""
+        phase = phase or (lambda name: contextlib.nullcontext())
         attention_mask = self._encoder_mask(attention_mask)
         if pixel_values is None:
-            return self.lm.encoder(input_ids=input_ids, attention_mask=attention_mask).last_hidden_state
-        feats = self.hf.model.get_image_features(pixel_values.to(self.dtype)).pooler_output
-        embeds = self.lm.get_input_embeddings()(input_ids)
-        mask = (input_ids == self.image_token_id).unsqueeze(-1).expand_as(embeds)
-        embeds = embeds.masked_scatter(mask, feats.to(embeds.dtype))
-        return self.lm.encoder(inputs_embeds=embeds, attention_mask=attention_mask).last_hidden_state
+            with phase("text_encoder"):
+                return self.lm.encoder(input_ids=input_ids, attention_mask=attention_mask).last_hidden_state
+        with phase("vision_tower"):
+            feats = self.hf.model.get_image_features(pixel_values.to(self.dtype)).pooler_output
+        with phase("text_encoder"):
+            embeds = self.lm.get_input_embeddings()(input_ids)
+            mask = (input_ids == self.image_token_id).unsqueeze(-1).expand_as(embeds)
+            embeds = embeds.masked_scatter(mask, feats.to(embeds.dtype))
+            return self.lm.encoder(inputs_embeds=embeds, attention_mask=attention_mask).last_hidden_state
 
     def _encoder_mask(self, mask: torch.Tensor | None):
         """The padding mask [G, S] as the prepared 4-D mask the encoder's attention takes (a 4-D

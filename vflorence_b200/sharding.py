@@ -55,3 +55,15 @@ def sum_over_ranks(value: float) -> float:
     import torch.distributed as dist
 
     return _reduce(value, dist.ReduceOp.SUM)
+
+
+def gather_to_rank0(obj):
+    """Every rank's ``obj`` as a list on rank 0 (None on the other ranks); ``[obj]`` without a
+    process group. Host-side reporting only, after the timed regions."""
+    import torch.distributed as dist
+
+    if not (dist.is_available() and dist.is_initialized()) or dist.get_world_size() == 1:
+        return [obj]
+    out = [None] * dist.get_world_size() if dist.get_rank() == 0 else None
+    dist.gather_object(obj, out, dst=0)
+    return out
