@@ -143,7 +143,14 @@ class Step:
 # ------------------------------------------------------------------------------------ clocks
 
 class ClockSampler:
-    """nvidia-smi samples of this GPU during the timed region."""
+    """Clock, power and throttle-reason samples of this GPU during a timed region: NVML read every
+    10 ms by a thread (read-only queries), else nvidia-smi every 100 ms; either writes rows of the
+    nvidia-smi trace format to one file, which ``summary`` reads."""
+
+    # NVML clocks-event reason bits: hw_slowdown, hw_thermal_slowdown, sw_thermal_slowdown, sw_power_cap
+    NVML_REASONS = (0x8, 0x40, 0x20, 0x4)
+    INTERVAL_S = 0.01
+    _count = 0
 
     FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -160,11 +167,41 @@ class ClockSampler:
         self.proc = None
         # the raw trace: VFL_CLOCKS_DIR when set (to keep it), else a temporary file
         out_dir = os.environ.get("VFL_CLOCKS_DIR") or tempfile.gettempdir()
-        self.path = os.path.join(out_dir, f"vfl_clocks_gpu{phys}_{os.getpid()}.csv")
+        ClockSampler._count += 1  # one trace file per sampler of the process
+        self.path = os.path.join(out_dir, f"vfl_clocks_gpu{phys}_{os.getpid()}_{ClockSampler._count}.csv")
+
+    def _nvml_loop(self, nvml, handle):
+        active = lambda bit: "Active" if self._reasons & bit else "Not Active"  # noqa: E731
+        while not self._stop.is_set():
+            try:
+                sm = nvml.nvmlDeviceGetClockInfo(handle, nvml.NVML_CLOCK_SM)
+                mx = nvml.nvmlDeviceGetMaxClockInfo(handle, nvml.NVML_CLOCK_SM)
+                pw = nvml.nvmlDeviceGetPowerUsage(handle) / 1000.0
+                self._reasons = nvml.nvmlDeviceGetCurrentClocksThrottleReasons(handle)
+            except Exception:  # a failed read drops the sample
+                self._stop.wait(self.INTERVAL_S)
+                continue
+            self.fh.write(f"{sm}, {mx}, {pw:.2f}, {self._reasons:#x}, "
+                          + ", ".join(active(b) for b in self.NVML_REASONS) + "\n")
+            self._stop.wait(self.INTERVAL_S)
 
     def __enter__(self):
+        import threading
+
+        self.fh = open(self.path, "w")
+        self._stop, self._thread, self._reasons = threading.Event(), None, 0
         try:
-            self.fh = open(self.path, "w")
+            import pynvml as nvml
+
+            nvml.nvmlInit()
+            handle = nvml.nvmlDeviceGetHandleByIndex(self.phys)
+            self._thread = threading.Thread(target=self._nvml_loop, args=(nvml, handle), daemon=True)
+            self._thread.start()
+            self.proc = self._thread
+            return self
+        except Exception:
+            self._thread = None
+        try:
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.phys), f"--query-gpu={self.FIELDS}",
                                           "--format=csv,noheader,nounits", "-lms", "100"],
                                          stdout=self.fh, stderr=subprocess.DEVNULL)
@@ -173,17 +210,20 @@ class ClockSampler:
         return self
 
     def __exit__(self, *exc):
-        if self.proc is not None:
+        if self._thread is not None:
+            self._stop.set()
+            self._thread.join(timeout=5)
+        elif self.proc is not None:
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
             except subprocess.TimeoutExpired:
                 self.proc.kill()
-            self.fh.close()
+        self.fh.close()
 
     def summary(self):
         if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["NVML and nvidia-smi unavailable"]}
         rows = []
         with open(self.path) as f:
             for line in f:
@@ -1037,8 +1077,9 @@ def main():
     barrier(world)
     torch.cuda.synchronize()
     s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e2e_run(e2e_steps, s2, e2)
-    torch.cuda.synchronize()
+    with ClockSampler(local) as clocks_e2e:
+        e2e_run(e2e_steps, s2, e2)
+        torch.cuda.synchronize()
     barrier(world)
     e2e_ms = max_over_ranks(s2.elapsed_time(e2))
     e2e_bytes = sum_over_ranks(float(nb["total"] * e2e_steps))
@@ -1080,7 +1121,7 @@ def main():
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": config_of(args, world),
             "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "ms_per_step": e2e_ms / e2e_steps, "steps": e2e_steps},
+                    "ms_per_step": e2e_ms / e2e_steps, "steps": e2e_steps, "clocks": clocks_e2e.summary()},
             "gpu_launches": launches,
             "roofline": {"bound": "hbm", "kernel": "self decode: paged_attention_tc_kernel (bf16, head_dim 64) + combine",
                          "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
