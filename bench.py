@@ -144,12 +144,12 @@ class Step:
 
 class ClockSampler:
     """Clock, power and throttle-reason samples of this GPU during a timed region: NVML read every
-    10 ms by a thread (read-only queries), else nvidia-smi every 100 ms; either writes rows of the
+    5 ms by a thread (read-only queries), else nvidia-smi every 100 ms; either writes rows of the
     nvidia-smi trace format to one file, which ``summary`` reads."""
 
     # NVML clocks-event reason bits: hw_slowdown, hw_thermal_slowdown, sw_thermal_slowdown, sw_power_cap
     NVML_REASONS = (0x8, 0x40, 0x20, 0x4)
-    INTERVAL_S = 0.01
+    INTERVAL_S = 0.005
     _count = 0
 
     FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"

@@ -39,6 +39,27 @@ def test_bounded_wait_check_refuses_limits_on_the_host(native):
         assert b"limit_ns" in native.vfl_last_error_message()
 
 
+def test_decode_linear_support_and_refusals(native):
+    """Shapes the skinny linear kernel takes, and host-side refusals before any launch."""
+    from vflorence_b200 import paged_ops as ops
+
+    assert ops.decode_linear_supported(torch.float32, 8, 1024, 4096)
+    assert ops.decode_linear_supported(torch.float32, 16, 50304, 1024)
+    assert ops.decode_linear_supported(torch.float32, 1, 96, 256)
+    for args in ((torch.bfloat16, 8, 1024, 1024), (torch.float32, 17, 1024, 1024), (torch.float32, 0, 1024, 1024),
+                 (torch.float32, 8, 1000, 1024), (torch.float32, 8, 1024, 1000)):
+        assert not ops.decode_linear_supported(*args)
+    ptr = 1 << 20  # never dereferenced: every call below is refused on the host
+    assert native.vfl_decode_linear(ptr, 1024, ptr, None, ptr, 1024, 8, 1024, 1024, 1, 0, None) == 2  # bf16
+    assert native.vfl_decode_linear(ptr, 1024, ptr, None, ptr, 1024, 8, 1024, 1024, 0, 7, None) == 1  # activation
+    assert native.vfl_decode_linear(None, 1024, ptr, None, ptr, 1024, 8, 1024, 1024, 0, 0, None) == 1
+    assert native.vfl_decode_linear(ptr + 4, 1024, ptr, None, ptr, 1024, 8, 1024, 1024, 0, 0, None) == 1
+    assert native.vfl_decode_linear(ptr, 1026, ptr, None, ptr, 1024, 8, 1024, 1024, 0, 0, None) == 1
+    assert native.vfl_decode_linear(ptr, 1024, ptr, None, ptr, 1000, 8, 1024, 1024, 0, 0, None) == 1
+    assert native.vfl_decode_linear(ptr, 1024, ptr, None, ptr, 1024, 20, 1024, 1024, 0, 0, None) == 2
+    assert native.vfl_decode_linear(ptr, 1024, ptr, None, ptr, 1024, 0, 1024, 1024, 0, 0, None) == 0  # no rows
+
+
 def test_status_strings(native):
     assert native.vfl_status_string(0) == b"ok"
     assert b"workspace" in native.vfl_status_string(3)

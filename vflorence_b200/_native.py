@@ -55,6 +55,8 @@ EXPORTS = (
     "vfl_kv_proj_paged",
     "vfl_add_layernorm",
     "vfl_add_layernorm_supported",
+    "vfl_decode_linear",
+    "vfl_decode_linear_supported",
     "vfl_paged_slots",
     "vfl_row_topk",
     "vfl_row_topk_workspace_size",
@@ -181,6 +183,8 @@ def _declare(L):
         "vfl_kv_proj_paged": (i32, [vp, i64, vp, vp, vp, vp, vp, i64, i32, i32, i32, i32, i64, vp]),
         "vfl_add_layernorm": (i32, [vp, i64, vp, i64, vp, vp, vp, i64, i32, i32, f32, i32, vp]),
         "vfl_add_layernorm_supported": (i32, [i32, i32]),
+        "vfl_decode_linear": (i32, [vp, i64, vp, vp, vp, i64, i32, i32, i32, i32, i32, vp]),
+        "vfl_decode_linear_supported": (i32, [i32, i32, i32, i32]),
         "vfl_row_topk": (i32, [vp, i32, i64, i64, i64, i32, vp, i32, vp, vp, vp, sz, vp]),
         "vfl_row_topk_workspace_size": (sz, [i64, i64, i32]),
         "vfl_beam_merge": (i32, [vp, vp, i64, i32, vp, vp, i32, i32, vp, vp]),

@@ -55,10 +55,11 @@ class Engine:
     def __init__(self, hf_model, *, max_num_seqs: int, max_decoder_len: int, max_encoder_len: int,
                  block_size: int = 16, num_blocks: int | None = None, decoder_start_token_id: int | None = None,
                  record_steps: bool = False, cuda_graphs: bool = False, group_beams: bool | str = True,
-                 fused_encoder_kv: bool = True, fused_layernorm: bool = True):
+                 fused_encoder_kv: bool = True, fused_layernorm: bool = True, skinny_linear: bool = True):
         # decoder post-norm residuals: LayerNorm(h + x) in one launch each where it is built for
         # the width (False: the add, then the torch module)
-        self.model = PagedSeq2Seq(hf_model, fused_layernorm=fused_layernorm)
+        # float32 steps of at most 16 rows: linear layers as weight-streaming launches (False: GEMMs)
+        self.model = PagedSeq2Seq(hf_model, fused_layernorm=fused_layernorm, skinny_linear=skinny_linear)
         # encoder K/V: one tensor-core launch per layer that projects and writes the pages (bf16);
         # False (or another dtype) runs the projection GEMM, then the append kernel
         self.fused_encoder_kv = fused_encoder_kv and paged_ops.kv_proj_supported(

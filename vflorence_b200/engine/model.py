@@ -9,7 +9,8 @@ ops the reference's decoder calls (vflorence/models/bart.py:106-146). The q/k/v 
 each decoder layer are fused into one GEMM and the encoder k/v projections into another, and the
 kernels take the strided q/k/v views of the fused outputs directly. Each post-norm residual,
 LayerNorm(h + sublayer(h)), and the embedding's LayerNorm(tokens + positions) run as one
-launch of ``paged_ops.add_layernorm`` where it is built for the model's width and dtype.
+launch of ``paged_ops.add_layernorm`` where it is built for the model's width and dtype. In
+float32 steps of at most 16 rows every linear layer is one ``paged_ops.decode_linear`` launch.
 """
 
 from __future__ import annotations
@@ -46,7 +47,7 @@ class _Layer:
 
 
 class PagedSeq2Seq:
-    def __init__(self, hf_model, fused_layernorm: bool = True):
+    def __init__(self, hf_model, fused_layernorm: bool = True, skinny_linear: bool = True):
         cfg = hf_model.config
         self.is_florence2 = cfg.model_type == "florence2"
         lm_cfg = cfg.get_text_config()
@@ -86,6 +87,11 @@ class PagedSeq2Seq:
                                 and all(isinstance(n, torch.nn.LayerNorm) and n.weight is not None
                                         and tuple(n.normalized_shape) == (self.d_model,) for n in norms)
                                 and paged_ops.add_layernorm_supported(self.dtype, self.d_model))
+        # float32 steps of at most 16 rows: the linear layers as weight-streaming launches
+        # (paged_ops.decode_linear) instead of library GEMMs; fc1's activation fused when it is
+        # the exact GELU
+        self.skinny_linear = skinny_linear and self.device.type == "cuda" and self.dtype == torch.float32
+        self.fuse_gelu = lm_cfg.activation_function == "gelu"
 
     # ------------------------------------------------------------------------------- encoder
     @torch.inference_mode()
@@ -132,6 +138,18 @@ class PagedSeq2Seq:
         return k.reshape(shape), v.reshape(shape)
 
     # ------------------------------------------------------------------------------- decoder
+    def _linear(self, x: torch.Tensor, w: torch.Tensor, b: torch.Tensor | None, act: bool = False) -> torch.Tensor:
+        """``x @ w.T + b`` (then the model's activation when ``act``): one decode_linear launch for a
+        few float32 rows, else the library GEMM."""
+        if self.skinny_linear and paged_ops.decode_linear_supported(x.dtype, x.shape[0], w.shape[0], w.shape[1]):
+            if not act:
+                return paged_ops.decode_linear(x, w, b)
+            if self.fuse_gelu:
+                return paged_ops.decode_linear(x, w, b, "gelu")
+            return self.act(paged_ops.decode_linear(x, w, b))
+        y = F.linear(x, w, b)
+        return self.act(y) if act else y
+
     def _add_norm(self, h: torch.Tensor, x: torch.Tensor, norm: torch.nn.LayerNorm) -> torch.Tensor:
         """``norm(h + x)``: one fused launch, or the add and the module."""
         if self.fused_layernorm:
@@ -146,14 +164,16 @@ class PagedSeq2Seq:
         h = self._add_norm(self.embed_tokens(input_ids), F.embedding(positions + self.pos_offset, self.pos_weight),
                            self.ln_embed)
         shape = (B, self.num_heads, self.head_dim)
+        lin = self._linear
         for i, L in enumerate(self.layers):
-            q, k, v = (t.reshape(shape) for t in F.linear(h, L.w_qkv, L.b_qkv).chunk(3, dim=-1))
+            q, k, v = (t.reshape(shape) for t in lin(h, L.w_qkv, L.b_qkv).chunk(3, dim=-1))
             a = decoder_self_attention(q, k, v, L.self_attn.k_cache, L.self_attn.v_cache, self.scale)
-            h = self._add_norm(h, L.self_out(a.reshape(B, self.d_model)), L.ln_self)
-            c = decoder_cross_attention(L.cross_q(h).reshape(shape), i, self.scale)
-            h = self._add_norm(h, L.cross_out(c.reshape(B, self.d_model)), L.ln_cross)
-            h = self._add_norm(h, L.fc2(self.act(L.fc1(h))), L.ln_final)
-        logits = F.linear(h, self.w_head, self.b_head)[:, : self.vocab_size]
+            h = self._add_norm(h, lin(a.reshape(B, self.d_model), L.self_out.weight, L.self_out.bias), L.ln_self)
+            c = decoder_cross_attention(lin(h, L.cross_q.weight, L.cross_q.bias).reshape(shape), i, self.scale)
+            h = self._add_norm(h, lin(c.reshape(B, self.d_model), L.cross_out.weight, L.cross_out.bias), L.ln_cross)
+            ff = lin(h, L.fc1.weight, L.fc1.bias, act=True)
+            h = self._add_norm(h, lin(ff, L.fc2.weight, L.fc2.bias), L.ln_final)
+        logits = lin(h, self.w_head, self.b_head)[:, : self.vocab_size]
         if self.final_logits_bias is not None:
             logits = logits + self.final_logits_bias
         return logits

@@ -577,3 +577,48 @@ def check_bounded_wait(limit_ns: int, producer_arrives: bool = False,
     with torch.cuda.device(dev):
         st = N.lib().vfl_check_bounded_wait(int(bool(producer_arrives)), int(limit_ns), _stream(dev))
     N.check(st, "check_bounded_wait")
+
+
+# ------------------------------------------------------------------------------ decode_linear
+
+_ACTS = {None: 0, "gelu": 1}
+
+
+def decode_linear_supported(dtype: torch.dtype, rows: int, n: int, k: int) -> bool:
+    """Whether ``decode_linear`` is built for this layer: float32, 1..16 rows, n a multiple of 32,
+    k a multiple of 128."""
+    if dtype != torch.float32:
+        return False
+    return bool(N.lib().vfl_decode_linear_supported(N.DTYPE_F32, int(rows), int(n), int(k)))
+
+
+def decode_linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = None,
+                  activation: str | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+    """``act(x @ weight.T + bias)`` for the few rows of a decode step (torch.nn.Linear's layout,
+    float32): one weight-streaming launch, bias and the exact GELU fused. Returns ``out`` (a new
+    [rows, n] tensor when None)."""
+    dev = weight.device
+    _require_cuda("x", x, dev)
+    _require_cuda("weight", weight, dev)
+    if activation not in _ACTS:
+        raise ValueError(f"vflorence_b200: decode_linear activation {activation!r} (None or 'gelu')")
+    if x.dim() != 2 or weight.dim() != 2 or x.shape[1] != weight.shape[1] or x.stride(1) != 1 \
+            or not weight.is_contiguous():
+        raise ValueError("vflorence_b200: decode_linear takes x [rows, k] (unit column stride) and a "
+                         "contiguous weight [n, k]")
+    if x.dtype != weight.dtype or (bias is not None and (bias.dtype != weight.dtype or bias.shape != (weight.shape[0],)
+                                                        or not bias.is_contiguous())):
+        raise ValueError("vflorence_b200: decode_linear x, weight and bias must share one dtype; bias [n]")
+    if bias is not None:
+        _require_cuda("bias", bias, dev)
+    rows, k = x.shape
+    n = weight.shape[0]
+    if out is None:
+        out = torch.empty(rows, n, dtype=x.dtype, device=dev)
+    elif out.shape != (rows, n) or out.dtype != x.dtype or out.stride(1) != 1:
+        raise ValueError("vflorence_b200: decode_linear out must be [rows, n] with unit column stride")
+    st = N.lib().vfl_decode_linear(x.data_ptr(), x.stride(0), weight.data_ptr(),
+                                   bias.data_ptr() if bias is not None else None, out.data_ptr(), out.stride(0),
+                                   rows, n, k, _dtype_code(x.dtype), _ACTS[activation], _stream(dev))
+    N.check(st, "decode_linear")
+    return out
