@@ -80,6 +80,17 @@ __global__ void __launch_bounds__(kWarps * 32) decode_linear_f32_kernel(DecodeLi
   const int S = gridDim.y;
   const int kslice = p.kslice, kq = kslice / 4;
   const int k0 = blockIdx.y * kslice;
+  const int n0 = blockIdx.x * kColsPerCta + warp * kColsPerWarp;
+  const float* wl = p.w + (size_t)n0 * p.k + k0 + lane * 4;
+  const int iters = kslice / kChunk;
+  // the first weight chunks go out before the rows are staged: their DRAM latency overlaps
+  // the staging (the weights do not depend on it)
+  float4 wv[U][kColsPerWarp];
+#pragma unroll
+  for (int u = 0; u < U; ++u)
+#pragma unroll
+    for (int c = 0; c < kColsPerWarp; ++c)
+      wv[u][c] = u < iters ? ldg_nc_f4(wl + (size_t)c * p.k + u * kChunk) : make_float4(0.f, 0.f, 0.f, 0.f);
   for (int i = threadIdx.x; i < MR * kq; i += kWarps * 32) {
     const int m = i / kq, c = i - m * kq;
     xs4[i] = m < p.rows ? *reinterpret_cast<const float4*>(p.x + m * p.x_stride + k0 + 4 * c)
@@ -87,20 +98,19 @@ __global__ void __launch_bounds__(kWarps * 32) decode_linear_f32_kernel(DecodeLi
   }
   __syncthreads();
 
-  const int n0 = blockIdx.x * kColsPerCta + warp * kColsPerWarp;
-  const float* wl = p.w + (size_t)n0 * p.k + k0 + lane * 4;
   float acc[NV];
 #pragma unroll
   for (int i = 0; i < NV; ++i) acc[i] = 0.f;
-  const int iters = kslice / kChunk;
 #pragma unroll 1
   for (int it0 = 0; it0 < iters; it0 += U) {
-    float4 wv[U][kColsPerWarp];
+    if (it0 > 0) {
 #pragma unroll
-    for (int u = 0; u < U; ++u)
+      for (int u = 0; u < U; ++u)
 #pragma unroll
-      for (int c = 0; c < kColsPerWarp; ++c)
-        wv[u][c] = it0 + u < iters ? ldg_nc_f4(wl + (size_t)c * p.k + (it0 + u) * kChunk) : make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int c = 0; c < kColsPerWarp; ++c)
+          wv[u][c] = it0 + u < iters ? ldg_nc_f4(wl + (size_t)c * p.k + (it0 + u) * kChunk)
+                                     : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       if (it0 + u >= iters) break;
@@ -162,13 +172,14 @@ __global__ void __launch_bounds__(kWarps * 32) decode_linear_f32_kernel(DecodeLi
   cluster.sync();  // no CTA leaves while another still reads its partials
 }
 
-// K splits for a layer: enough CTAs for two per SM where K allows, and the staged rows within
-// the shared-memory budget. 0 when no split fits.
+// K splits for a layer: the fewest that give every SM a CTA (where K allows), so the grid stays
+// within one wave of two CTAs per SM and each CTA streams several chunks per warp, with the
+// staged rows within the shared-memory budget. 0 when no split fits.
 int choose_splits(int mr, int n, int k) {
   const int tiles = n / kColsPerCta;
   int s = 1;
   auto fits = [&](int sp) { return k % (sp * kChunk) == 0 && (size_t)mr * (k / sp) * 4 <= (size_t)kMaxSmem; };
-  while (s < kMaxSplits && (tiles * s < 2 * kNumSMs || !fits(s)) && k % (2 * s * kChunk) == 0) s *= 2;
+  while (s < kMaxSplits && (tiles * s < kNumSMs || !fits(s)) && k % (2 * s * kChunk) == 0) s *= 2;
   return fits(s) ? s : 0;
 }
 
