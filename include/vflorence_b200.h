@@ -193,8 +193,11 @@ int vfl_attention_append_supported(const vfl_attention_plan* plan);
  * framework's pool already holds. Takes no workspace: the split-K scratch is a fixed array of
  * VFL_STATIC_WORKSPACE_BYTES inside the library, which every device that loads the library
  * keeps until exit. Plans needing more scratch fail with VFL_ERR_WORKSPACE. All calls on a
- * device share that array: calls that can overlap on the device race, so order them. The
- * first call on a device looks up the array's address; make it before any stream capture. */
+ * device share that array: calls that can overlap on the device race, so order them. Plans
+ * from vfl_plan_attention keep no state in it between calls; a caller-built plan with
+ * merge_in_kernel = 1 keeps arrival counters there, which such a call clears first. The first
+ * call on a device looks up the array's address (cached for the process; not valid after
+ * cudaDeviceReset); make it before any stream capture. */
 #define VFL_STATIC_WORKSPACE_BYTES (64u * 1024u * 1024u)
 int vfl_attention_with_kv_cache_no_alloc(const vfl_attention_plan* plan, const void* query,
                                          int64_t query_token_stride, const void* k_cache,

@@ -73,6 +73,35 @@ def test_no_alloc_matches_workspace_entry_point_twice(native):
     assert ops.read_device_errors(DEV) == 0
 
 
+def test_no_alloc_in_kernel_merge_counters_start_clean(native):
+    """A caller-built plan that merges split partials inside the launch keeps arrival counters in
+    the shared scratch; each call clears them first, so two calls in a row (the second finding
+    the first's counters) both equal the workspace entry point."""
+    from vflorence_b200 import _native
+    from vflorence_b200 import paged_ops as ops
+
+    for call, seed in enumerate((31, 32)):
+        q, kc, vc, qsl, lens, table = _case(seed, 4, 1500, 4096)
+        meta = ops.get_scheduler_metadata(4, H, H, D, lens, torch.bfloat16, qsl, False, "sm100", BS)
+        planned = ops.plan_of(meta)
+        plan = _native.AttentionPlan()
+        ctypes.memmove(ctypes.byref(plan), ctypes.byref(planned), ctypes.sizeof(plan))
+        assert plan.num_splits > 1 and plan.merge_in_kernel == 0
+        groups = H // plan.heads_per_cta
+        q_chunks = -(-plan.max_q_len // plan.queries_per_cta)
+        plan.merge_in_kernel = 1
+        plan.workspace_bytes += plan.num_reqs * groups * q_chunks * 4  # the arrival counters
+        d = dict(qsl=qsl.to(DEV), lens=lens.to(DEV), table=table.to(DEV))
+        ws = torch.empty(plan.workspace_bytes, dtype=torch.uint8, device=DEV)
+        want = _run(native, "vfl_attention_with_kv_cache", plan, q, kc, vc, d["qsl"], d["lens"], d["table"], ws)
+        got = _run(native, "vfl_attention_with_kv_cache_no_alloc", plan, q, kc, vc, d["qsl"], d["lens"],
+                   d["table"])
+        torch.cuda.synchronize()
+        assert torch.isfinite(got).all()
+        assert_attention_close(got, want, torch.bfloat16, f"in-kernel merge, no-alloc call {call + 1}")
+    assert ops.read_device_errors(DEV) == 0
+
+
 def test_no_alloc_rejects_plans_beyond_its_scratch(native):
     from vflorence_b200 import _native
     from vflorence_b200 import paged_ops as ops

@@ -12,14 +12,18 @@
 //     keeps that much memory until the process exits. A plan whose workspace_bytes is larger
 //     is rejected with VFL_ERR_WORKSPACE before anything is launched.
 //   * Every call on a device uses the same array, and it keeps whatever the last call left in
-//     it. The only part that must start at zero - the per-request arrival counters that pick
-//     the CTA which merges the split-K partials - is cleared by every call on its stream before
-//     its kernel runs; each partial the merge reads was written earlier in the same call. Calls
+//     it. The plans vfl_plan_attention builds merge the split-K partials in a separate combine
+//     launch and keep no state in the array between calls: every partial the combine reads was
+//     written earlier in the same call. Only a caller-built plan with merge_in_kernel = 1 puts
+//     per-request arrival counters in the array (they pick the CTA that merges); those must
+//     start at zero, and such a call clears them on its stream before its kernel runs. Calls
 //     whose kernels can overlap on one device (for example on two streams without an ordering
 //     between them) race on the array and give wrong results; order them on one stream or with
 //     events.
 //   * The first call on each device looks up the array's device address (cudaGetSymbolAddress,
-//     with that device current) and caches it; make that first call before any stream capture.
+//     with that device current) and caches it for the life of the process; make that first
+//     call before any stream capture. The cache does not survive cudaDeviceReset (the module
+//     reloads and the array may move): do not use this entry point after resetting a device.
 #include <atomic>
 #include <mutex>
 
