@@ -73,7 +73,9 @@ def test_get_isa(native):
         for d in sorted(ops.HEAD_DIMS):
             assert ops.get_isa(dt, 16, d) == "sm100"
     assert ops.get_isa(torch.bfloat16, 32, 64) == "sm100"
-    for args in ((torch.bfloat16, 16, 512), (torch.bfloat16, 8, 64), (torch.bfloat16, 24, 64)):
+    assert ops.get_isa(torch.float32, 16, 512) == "sm100"  # the reference's largest head_dim
+    for args in ((torch.bfloat16, 16, 1024), (torch.bfloat16, 16, 40), (torch.bfloat16, 8, 64),
+                 (torch.bfloat16, 24, 64)):
         with pytest.raises(ValueError):
             ops.get_isa(*args)
     with pytest.raises(ValueError):

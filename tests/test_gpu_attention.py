@@ -105,7 +105,7 @@ def test_fixture_cases_other_dtype(oracle_lib, case):
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16], ids=["f32", "bf16"])
-@pytest.mark.parametrize("head_dim", [32, 48, 64, 80, 96, 112, 128, 160, 192, 224, 256])
+@pytest.mark.parametrize("head_dim", [32, 48, 64, 80, 96, 112, 128, 160, 192, 224, 256, 512])
 @pytest.mark.parametrize("block_size", [16, 32])
 def test_head_dims_and_block_sizes(oracle_lib, dtype, head_dim, block_size):
     heads = 4 if head_dim <= 128 else 2

@@ -156,7 +156,7 @@ int vfl_get_isa(int dtype, int block_size, int head_dim, char* buf, int buf_len)
   if (!vfl::head_dim_supported(head_dim))
     return vfl::fail(VFL_ERR_UNSUPPORTED,
                      "head_dim %d: the sm100 kernels cover 32, 48, 64, 80, 96, 112, 128, 160, "
-                     "192, 224 and 256",
+                     "192, 224, 256 and 512",
                      head_dim);
   if (buf == nullptr || buf_len < 6) return vfl::fail(VFL_ERR_INVALID_ARGUMENT, "buffer too small");
   std::memcpy(buf, "sm100", 6);

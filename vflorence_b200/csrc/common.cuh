@@ -46,11 +46,12 @@ __host__ __device__ constexpr int next_pow2(int x) {
   return p;
 }
 
-// Head dims the attention kernels are built for (the reference accepts these and 512).
+// Head dims the attention kernels are built for (the reference's list,
+// vflorence/layers/attention.py:6).
 inline bool head_dim_supported(int d) {
   switch (d) {
     case 32: case 48: case 64: case 80: case 96: case 112: case 128:
-    case 160: case 192: case 224: case 256:
+    case 160: case 192: case 224: case 256: case 512:
       return true;
     default:
       return false;

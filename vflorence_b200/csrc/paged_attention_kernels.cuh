@@ -542,8 +542,9 @@ template <typename T, int D, int QPC>
 int launch_one(const AttnParams& p, dim3 grid, int threads, int smem_bytes, cudaStream_t stream) {
   static int smem_done[kMaxDevices];
   auto kernel = paged_attention_kernel<T, D, QPC>;
-  int st = ensure_smem_attribute(reinterpret_cast<const void*>(kernel), kHeaderBytes + kMaxStageBytes,
-                                 smem_done);
+  // the ring of most plans fits kMaxStageBytes; head_dim 512 needs two stages of up to 64 KiB
+  const int want = smem_bytes > kHeaderBytes + kMaxStageBytes ? smem_bytes : kHeaderBytes + kMaxStageBytes;
+  int st = ensure_smem_attribute(reinterpret_cast<const void*>(kernel), want, smem_done);
   if (st) return st;
   kernel<<<grid, threads, smem_bytes, stream>>>(p);
   st = cuda_status(cudaGetLastError(), "paged_attention launch");
@@ -574,6 +575,7 @@ int launch_dtype(const AttnParams& p, int head_dim, int qpc, dim3 grid, int thre
     case 192: return launch_qpc<T, 192>(p, qpc, grid, threads, smem_bytes, stream);
     case 224: return launch_qpc<T, 224>(p, qpc, grid, threads, smem_bytes, stream);
     case 256: return launch_qpc<T, 256>(p, qpc, grid, threads, smem_bytes, stream);
+    case 512: return launch_qpc<T, 512>(p, qpc, grid, threads, smem_bytes, stream);
     default: return fail(VFL_ERR_UNSUPPORTED, "head_dim %d not built", head_dim);
   }
 }

@@ -37,7 +37,7 @@ import torch
 
 from . import _native as N
 
-HEAD_DIMS = frozenset({32, 48, 64, 80, 96, 112, 128, 160, 192, 224, 256})
+HEAD_DIMS = frozenset({32, 48, 64, 80, 96, 112, 128, 160, 192, 224, 256, 512})
 _DTYPES = {torch.float32: N.DTYPE_F32, torch.bfloat16: N.DTYPE_BF16}
 
 
