@@ -267,23 +267,20 @@ int vfl_add_layernorm_supported(int dtype, int hidden_dim);
 #define VFL_ACT_NONE 0
 #define VFL_ACT_GELU 1 /* exact: 0.5 x (1 + erf(x / sqrt 2)), transformers' "gelu" */
 
-/* replaces, for decode steps of few rows, the decoder's linear layers
+/* replaces, for decode steps of at most 16 rows, the decoder's linear layers
  *   (vflorence/models/bart.py:106-146: q/k/v, out, cross q/out, fc1 + activation, fc2) and the
  *   vocabulary projection (bart.py:311-316), which the reference runs as torch GEMMs:
  *   y[m, n] = act(sum_k x[m, k] * weight[n, k] + bias[n]) for m < rows, n < n, with weight
- *   [n, k] row-major (torch.nn.Linear's layout). float32 (rows <= 16: weight streaming on CUDA
- *   cores; x_stride a multiple of 4) or bfloat16 (rows <= 256: tcgen05 tiles of 64 columns, fp32
- *   accumulate, one rounding; x_stride and y_stride multiples of 8). One launch; a K split runs in
- *   a thread-block cluster whose partial sums are added in a fixed order (results do not depend
- *   on timing). Strides in elements; x, weight (contiguous) and y 16-byte aligned; bias may be
- *   NULL. VFL_ERR_UNSUPPORTED unless vfl_decode_linear_supported. */
+ *   [n, k] row-major (torch.nn.Linear's layout). float32. One launch; a K split runs in a thread-
+ *   block cluster whose partial sums are added in a fixed order (results do not depend on
+ *   timing). Strides in elements; x, weight, y 16-byte aligned, x_stride a multiple of 4;
+ *   bias may be NULL. VFL_ERR_UNSUPPORTED unless vfl_decode_linear_supported. */
 int vfl_decode_linear(const void* x, int64_t x_stride, const void* weight, const void* bias, void* y,
                       int64_t y_stride, int32_t rows, int32_t n, int32_t k, int32_t dtype,
                       int32_t activation, void* stream);
 
-/* 1 when vfl_decode_linear is built for this shape: float32 with 1 <= rows <= 16, n a multiple
- * of 32, k a multiple of 128 (each K slice of the rows fitting 64 KiB of shared memory); or
- * bfloat16 with 1 <= rows <= 256, n and k multiples of 64. */
+/* 1 when vfl_decode_linear is built for this shape: float32, 1 <= rows <= 16, n a multiple of
+ * 32, k a multiple of 128 (with each K slice of the rows fitting 64 KiB of shared memory). */
 int vfl_decode_linear_supported(int dtype, int rows, int n, int k);
 
 /* replaces the encoder slot computation of ModelRunner._encode

@@ -58,54 +58,3 @@ def test_decode_linear_is_repeatable_and_takes_strided_rows():
     assert torch.equal(y1, y2) and torch.equal(y1, ops.decode_linear(x.contiguous(), w, b))
     assert bool((out[:, 1024:] == 0).all())
     assert_attention_close(y1, _reference(x, w, b, False), torch.float32, "strided")
-
-
-# bfloat16 (tensor cores, split K over a cluster): BART-large and Florence-2-base widths
-BF16_SHAPES = [(1024, 1024), (3072, 1024), (4096, 1024), (1024, 4096), (768, 768), (2304, 768), (3072, 768),
-               (768, 3072), (128, 256)]
-
-
-def _assert_bf16_close(got, want, what):
-    """One rounding of an fp32 sum to bf16 is off by at most half a bf16 ulp (2^-8 relative);
-    allow 2^-7 relative plus 1e-4 of the output's scale (erf and accumulation order)."""
-    got, want = got.double(), want.double()
-    tol = 2.0 ** -7 * want.abs() + 1e-4 * want.abs().max()
-    bad = (got - want).abs() > tol
-    assert not bool(bad.any()), f"{what}: {int(bad.sum())} entries off, max |diff| {(got - want).abs().max().item():.3e}"
-
-
-@pytest.mark.parametrize("rows", [1, 8, 100, 128, 129, 192, 255, 256])
-@pytest.mark.parametrize("n,k", BF16_SHAPES)
-def test_decode_linear_bf16_matches_float64(rows, n, k):
-    from vflorence_b200 import paged_ops as ops
-
-    assert ops.decode_linear_supported(torch.bfloat16, rows, n, k)
-    g = torch.Generator(device=DEV).manual_seed(n * 13 + k + rows)
-    x = torch.randn(rows, k, device=DEV, generator=g).to(torch.bfloat16)
-    w = (torch.randn(n, k, device=DEV, generator=g) * 0.02).to(torch.bfloat16)
-    b = torch.randn(n, device=DEV, generator=g).to(torch.bfloat16)
-    for bias, gelu in ((b, False), (None, False), (b, True)):
-        y = ops.decode_linear(x, w, bias, "gelu" if gelu else None)
-        assert y.dtype == torch.bfloat16
-        _assert_bf16_close(y, _reference(x, w, bias, gelu), f"bf16 rows {rows} n {n} k {k}")
-    assert ops.read_device_errors(DEV) == 0
-
-
-def test_decode_linear_bf16_repeatable_and_strided():
-    from vflorence_b200 import paged_ops as ops
-
-    g = torch.Generator(device=DEV).manual_seed(3)
-    wide = torch.randn(200, 1024 + 64, device=DEV, generator=g).to(torch.bfloat16)
-    x = wide[:, 64:]  # row stride 1088 elements, 128-byte aligned start
-    w = (torch.randn(3072, 1024, device=DEV, generator=g) * 0.02).to(torch.bfloat16)
-    b = torch.randn(3072, device=DEV, generator=g).to(torch.bfloat16)
-    out = torch.zeros(200, 3072 + 64, device=DEV, dtype=torch.bfloat16)
-    y1 = ops.decode_linear(x, w, b)
-    y2 = ops.decode_linear(x, w, b, out=out[:, :3072])
-    y3 = ops.decode_linear(x.contiguous(), w, b)
-    assert torch.equal(y1, y2) and torch.equal(y1, y3)
-    assert bool((out[:, 3072:] == 0).all())
-    _assert_bf16_close(y1, _reference(x, w, b, False), "bf16 strided")
-    # against the library GEMM: same operands, the same fp32-accumulate-then-round result within one ulp
-    ref = torch.nn.functional.linear(x, w, b)
-    assert float(((y1.float() - ref.float()).abs() > 2.0 ** -7 * ref.float().abs() + 1e-3).float().mean()) < 1e-3

@@ -206,18 +206,11 @@ int launch(const DecodeLinearParams& p, int splits, cudaStream_t stream) {
 }
 
 }  // namespace
-
-// bfloat16: the tensor-core kernel of decode_gemm.cu (up to 256 rows)
-bool decode_gemm_supported(int rows, int n, int k);
-int launch_decode_gemm(const void* x, int64_t x_stride, const void* w, const void* bias, void* y, int64_t y_stride,
-                       int rows, int n, int k, int act, cudaStream_t stream);
-
 }  // namespace vfl
 
 using namespace vfl;
 
 extern "C" int vfl_decode_linear_supported(int dtype, int rows, int n, int k) {
-  if (dtype == VFL_DTYPE_BF16) return decode_gemm_supported(rows, n, k) ? 1 : 0;
   if (dtype != VFL_DTYPE_F32 || rows < 1 || rows > kMaxRows || n <= 0 || k <= 0) return 0;
   if (n % kColsPerCta != 0 || k % kChunk != 0) return 0;
   return choose_splits(next_pow2(rows), n, k) > 0 ? 1 : 0;
@@ -226,25 +219,11 @@ extern "C" int vfl_decode_linear_supported(int dtype, int rows, int n, int k) {
 extern "C" int vfl_decode_linear(const void* x, int64_t x_stride, const void* weight, const void* bias, void* y,
                                  int64_t y_stride, int32_t rows, int32_t n, int32_t k, int32_t dtype,
                                  int32_t activation, void* stream) {
-  if (dtype != VFL_DTYPE_F32 && dtype != VFL_DTYPE_BF16)
-    return fail(VFL_ERR_UNSUPPORTED, "decode_linear: dtype %d (float32 or bfloat16)", dtype);
+  if (dtype != VFL_DTYPE_F32) return fail(VFL_ERR_UNSUPPORTED, "decode_linear: dtype %d (float32 only)", dtype);
   if (activation != VFL_ACT_NONE && activation != VFL_ACT_GELU)
     return fail(VFL_ERR_INVALID_ARGUMENT, "decode_linear: activation %d", activation);
   if (rows < 0 || n <= 0 || k <= 0) return fail(VFL_ERR_INVALID_ARGUMENT, "decode_linear: rows %d, n %d, k %d", rows, n, k);
   if (rows == 0) return VFL_OK;
-  if (dtype == VFL_DTYPE_BF16) {
-    if (!decode_gemm_supported(rows, n, k))
-      return fail(VFL_ERR_UNSUPPORTED, "decode_linear (bf16): rows %d (1..256), n %d and k %d (multiples of 64)", rows,
-                  n, k);
-    if (!x || !weight || !y) return fail(VFL_ERR_INVALID_ARGUMENT, "decode_linear: NULL pointer");
-    if (!aligned16(x) || !aligned16(weight) || !aligned16(y) || (bias && (reinterpret_cast<uintptr_t>(bias) & 1u)) ||
-        x_stride % 8 || x_stride < k || y_stride % 8 || y_stride < n)
-      return fail(VFL_ERR_INVALID_ARGUMENT,
-                  "decode_linear (bf16): x, weight and y must be 16-byte aligned, x_stride and y_stride multiples of "
-                  "8 with x_stride >= k and y_stride >= n");
-    return launch_decode_gemm(x, x_stride, weight, bias, y, y_stride, rows, n, k, activation,
-                              static_cast<cudaStream_t>(stream));
-  }
   if (!vfl_decode_linear_supported(dtype, rows, n, k))
     return fail(VFL_ERR_UNSUPPORTED,
                 "decode_linear: rows %d (1..16), n %d (a multiple of 32), k %d (a multiple of 128 whose "

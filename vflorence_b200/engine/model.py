@@ -10,8 +10,7 @@ each decoder layer are fused into one GEMM and the encoder k/v projections into 
 kernels take the strided q/k/v views of the fused outputs directly. Each post-norm residual,
 LayerNorm(h + sublayer(h)), and the embedding's LayerNorm(tokens + positions) run as one
 launch of ``paged_ops.add_layernorm`` where it is built for the model's width and dtype. In
-decode steps of few rows (float32: <= 16, bfloat16: <= 256) the linear layers are
-``paged_ops.decode_linear`` launches.
+float32 steps of at most 16 rows every linear layer is one ``paged_ops.decode_linear`` launch.
 """
 
 from __future__ import annotations
@@ -88,11 +87,10 @@ class PagedSeq2Seq:
                                 and all(isinstance(n, torch.nn.LayerNorm) and n.weight is not None
                                         and tuple(n.normalized_shape) == (self.d_model,) for n in norms)
                                 and paged_ops.add_layernorm_supported(self.dtype, self.d_model))
-        # decode steps of few rows (float32: at most 16, weight-streaming launches; bfloat16: at
-        # most 256, split-K tensor-core launches): the linear layers as paged_ops.decode_linear
-        # instead of library GEMMs; fc1's activation fused when it is the exact GELU
-        self.skinny_linear = (skinny_linear and self.device.type == "cuda"
-                              and self.dtype in (torch.float32, torch.bfloat16))
+        # float32 steps of at most 16 rows: the linear layers as weight-streaming launches
+        # (paged_ops.decode_linear) instead of library GEMMs; fc1's activation fused when it is
+        # the exact GELU
+        self.skinny_linear = skinny_linear and self.device.type == "cuda" and self.dtype == torch.float32
         self.fuse_gelu = lm_cfg.activation_function == "gelu"
 
     # ------------------------------------------------------------------------------- encoder
@@ -140,13 +138,10 @@ class PagedSeq2Seq:
         return k.reshape(shape), v.reshape(shape)
 
     # ------------------------------------------------------------------------------- decoder
-    def _linear(self, x: torch.Tensor, w: torch.Tensor, b: torch.Tensor | None, act: bool = False,
-                vocab: bool = False) -> torch.Tensor:
-        """``x @ w.T + b`` (then the model's activation when ``act``): one decode_linear launch for the
-        few rows of a decode step, else the library GEMM. The bfloat16 vocabulary projection
-        (``vocab``) stays a library GEMM: its 50k columns re-read every row many times."""
-        if (self.skinny_linear and not (vocab and x.dtype != torch.float32)
-                and paged_ops.decode_linear_supported(x.dtype, x.shape[0], w.shape[0], w.shape[1])):
+    def _linear(self, x: torch.Tensor, w: torch.Tensor, b: torch.Tensor | None, act: bool = False) -> torch.Tensor:
+        """``x @ w.T + b`` (then the model's activation when ``act``): one decode_linear launch for a
+        few float32 rows, else the library GEMM."""
+        if self.skinny_linear and paged_ops.decode_linear_supported(x.dtype, x.shape[0], w.shape[0], w.shape[1]):
             if not act:
                 return paged_ops.decode_linear(x, w, b)
             if self.fuse_gelu:
@@ -178,7 +173,7 @@ class PagedSeq2Seq:
             h = self._add_norm(h, lin(c.reshape(B, self.d_model), L.cross_out.weight, L.cross_out.bias), L.ln_cross)
             ff = lin(h, L.fc1.weight, L.fc1.bias, act=True)
             h = self._add_norm(h, lin(ff, L.fc2.weight, L.fc2.bias), L.ln_final)
-        logits = lin(h, self.w_head, self.b_head, vocab=True)[:, : self.vocab_size]
+        logits = lin(h, self.w_head, self.b_head)[:, : self.vocab_size]
         if self.final_logits_bias is not None:
             logits = logits + self.final_logits_bias
         return logits

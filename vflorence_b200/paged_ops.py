@@ -585,19 +585,17 @@ _ACTS = {None: 0, "gelu": 1}
 
 
 def decode_linear_supported(dtype: torch.dtype, rows: int, n: int, k: int) -> bool:
-    """Whether ``decode_linear`` is built for this layer: float32 with 1..16 rows, n a multiple of
-    32 and k of 128 (CUDA cores, weight streaming); bfloat16 with 1..256 rows, n and k multiples
-    of 64 (tensor cores, split K)."""
-    if dtype not in _DTYPES:
+    """Whether ``decode_linear`` is built for this layer: float32, 1..16 rows, n a multiple of 32,
+    k a multiple of 128."""
+    if dtype != torch.float32:
         return False
-    return bool(N.lib().vfl_decode_linear_supported(_DTYPES[dtype], int(rows), int(n), int(k)))
+    return bool(N.lib().vfl_decode_linear_supported(N.DTYPE_F32, int(rows), int(n), int(k)))
 
 
 def decode_linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = None,
                   activation: str | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
-    """``act(x @ weight.T + bias)`` for the few rows of a decode step (torch.nn.Linear's layout):
-    one launch with bias and the exact GELU fused - float32 (<= 16 rows) streams the weights on
-    CUDA cores, bfloat16 (<= 256 rows) runs split-K tensor-core tiles. Returns ``out`` (a new
+    """``act(x @ weight.T + bias)`` for the few rows of a decode step (torch.nn.Linear's layout,
+    float32): one weight-streaming launch, bias and the exact GELU fused. Returns ``out`` (a new
     [rows, n] tensor when None)."""
     dev = weight.device
     _require_cuda("x", x, dev)
