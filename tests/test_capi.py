@@ -193,7 +193,7 @@ def test_attention_rejects_foreign_metadata_without_touching_the_gpu(native):
     assert b"plan" in native.vfl_last_error_message()
 
 
-@pytest.mark.parametrize("field,value", [("blocks_per_split", 65), ("blocks_per_split", 0), ("stages", 5),
+@pytest.mark.parametrize("field,value", [("blocks_per_split", 65), ("blocks_per_split", 0), ("stages", 9),
                                          ("stages", 1), ("heads_per_cta", 3), ("num_splits", 1),
                                          ("workspace_bytes", 16), ("queries_per_cta", 2), ("merge_in_kernel", 2)])
 def test_attention_refuses_a_corrupted_plan_before_the_device(native, field, value):

@@ -122,8 +122,8 @@ int check_attention_plan(const vfl_attention_plan* plan) {
   const bool tc = qpc == kTcRows;
   if (tc ? !use_tensor_cores(plan->dtype, D) : !(qpc == 1 || qpc == 4))
     return fail(VFL_ERR_INVALID_ARGUMENT, "attention: plan queries_per_cta %d not built for this shape", qpc);
-  if (plan->stages < 2 || plan->stages > 4)
-    return fail(VFL_ERR_INVALID_ARGUMENT, "attention: plan stages %d outside [2, 4]", plan->stages);
+  if (plan->stages < 2 || plan->stages > kMaxStages)
+    return fail(VFL_ERR_INVALID_ARGUMENT, "attention: plan stages %d outside [2, %d]", plan->stages, kMaxStages);
   const int64_t stage_bytes = (int64_t)2 * hpc * 16 * D * (int64_t)dtype_size(plan->dtype);
   if ((tc ? kTcHeaderBytes : kHeaderBytes) + plan->stages * stage_bytes > 227 * 1024)
     return fail(VFL_ERR_INVALID_ARGUMENT, "attention: plan stages do not fit in shared memory");

@@ -11,8 +11,9 @@ int launch_paged_attention_bf16(const AttnParams& p, int head_dim, int qpc, dim3
 int launch_paged_attention_tc(const AttnParams& p, const CUtensorMap& kmap, const CUtensorMap& vmap, dim3 grid,
                               int threads, int smem_bytes, cudaStream_t stream) {
   static int smem_done[kMaxDevices];
-  int st = ensure_smem_attribute(reinterpret_cast<const void*>(paged_attention_tc_kernel),
-                                 kTcHeaderBytes + kMaxStageBytes, smem_done);
+  // plans ask for at most kMaxStageBytes of ring unless they set more stages (checked on the host)
+  const int want = smem_bytes > kTcHeaderBytes + kMaxStageBytes ? smem_bytes : kTcHeaderBytes + kMaxStageBytes;
+  int st = ensure_smem_attribute(reinterpret_cast<const void*>(paged_attention_tc_kernel), want, smem_done);
   if (st) return st;
   paged_attention_tc_kernel<<<grid, threads, smem_bytes, stream>>>(p, kmap, vmap);
   st = cuda_status(cudaGetLastError(), "paged_attention (tensor cores) launch");
