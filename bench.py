@@ -573,6 +573,50 @@ def run_split_sweep(args):
         del k, v
 
 
+def run_ring_sweep(args):
+    """Under-filled attention shapes (few requests, the decode engine's cross-attention shapes)
+    against the depth of the shared-memory ring: the planner's plan with 2, 4, 6 and 8 stages
+    (device time per call, L2 flushed). One JSON line per shape."""
+    from vflorence_b200 import paged_ops as ops
+
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    flush = torch.empty(192 * 1024 * 1024, dtype=torch.uint8, device=device)
+    g = torch.Generator().manual_seed(0)
+    peak, _ = load_peaks()
+    shapes = [("cross 32 requests x 4 beams x 1024", 32, 4, torch.full((32,), 1024, dtype=torch.int32)),
+              ("cross 64 x 3 x 587", 64, 3, torch.full((64,), 587, dtype=torch.int32)),
+              ("cross 85 x 3 x 592", 85, 3, torch.full((85,), 592, dtype=torch.int32)),
+              ("self 8 x U[1,4096]", 8, 1, torch.randint(1, MAX_CTX + 1, (8,), generator=g).to(torch.int32)),
+              ("self 32 x U[1,4096]", 32, 1, torch.randint(1, MAX_CTX + 1, (32,), generator=g).to(torch.int32)),
+              ("self 32 x 2048", 32, 1, torch.full((32,), 2048, dtype=torch.int32))]
+    for name, R, rpr, lens in shapes:
+        nb = -(-int(lens.max()) // BS)
+        k = torch.randn(R * nb, H, BS, D, device=device, dtype=DTYPE)
+        v = torch.randn_like(k)
+        table = torch.randperm(R * nb, generator=g).to(torch.int32).view(R, nb).to(device)
+        q = torch.randn(R * rpr, H, D, device=device, dtype=DTYPE)
+        out = torch.empty_like(q)
+        qsl = torch.arange(0, R * rpr + 1, rpr, dtype=torch.int32)
+        lens_d, qsl_d = lens.to(device), qsl.to(device)
+        plan = ops.plan_of(ops.get_scheduler_metadata(R, H, H, D, lens, DTYPE, qsl, False, "sm100", BS))
+        row = {"point": "ring_sweep", "shape": name, "plan": [plan.num_splits, plan.blocks_per_split, plan.stages]}
+        for stages in (2, 4, 6, 8):
+            meta = ops.get_scheduler_metadata(R, H, H, D, lens, DTYPE, qsl, False, "sm100", BS)
+            ops.plan_of(meta).stages = stages
+            call = lambda: ops.attention_with_kv_cache(q, k, v, out, qsl_d, lens_d, D ** -0.5,  # noqa: E731
+                                                       False, table, meta)
+            call()
+            row[f"stages_{stages}_us"] = round(_time_op(call, 10, flush) * 1e3, 2)
+        nbytes = int(lens.long().sum()) * H * D * ELEM * 2
+        best = min(v_ for k_, v_ in row.items() if k_.startswith("stages_"))
+        row["best_frac_of_hbm"] = round(nbytes / (best * 1e-6) / (peak * 1e9), 3)
+        if ops.read_device_errors(device):
+            raise RuntimeError(f"device error bits at {name}")
+        print(json.dumps(row), flush=True)
+        del k, v
+
+
 def run_profile_step(args):
     """The workload of the decode-step launch list: the config's engine with CUDA graphs, one
     wave of requests, 120 steps (half of max_tokens for shorter jobs), then one step between
@@ -927,6 +971,8 @@ def main():
     ap.add_argument("--split-sweep", action="store_true",
                     help="the planner's split rule against every fixed split, one line per shape")
     ap.add_argument("--sweep-batches", default="1,2,4,8,16,32,64,128,256,512,1024")
+    ap.add_argument("--ring-sweep", action="store_true",
+                    help="under-filled attention shapes against 2-8 ring stages, one line per shape")
     ap.add_argument("--profile-step", choices=["cfg1", "cfg2", "cfg3", "cfg4"], default=None,
                     help="one decode step of the config's engine inside a profiler range (for ncu)")
     ap.add_argument("--profile-kv-proj", type=int, default=0, metavar="TOKENS",
@@ -951,6 +997,9 @@ def main():
         return
     if args.split_sweep:
         run_split_sweep(args)
+        return
+    if args.ring_sweep:
+        run_ring_sweep(args)
         return
     if args.profile_step:
         run_profile_step(args)
