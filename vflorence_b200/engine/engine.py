@@ -6,8 +6,9 @@ One step (the same order as the reference engine, vflorence/engine/llm_engine.py
   3. encode the step's new requests (one padded batch per image shape) and page their
      encoder K/V into the cross pool, once per request (bf16: projection and page write in one
      tensor-core launch per layer);
-  4. copy-on-write copies (one launch), device-side step metadata (one upload, one kernel),
-     cross staging (memoised on the batch's request ids), then one decoder forward;
+  4. copy-on-write copies (one launch, issued before the host packs the rows), device-side step
+     metadata (one upload, one kernel), cross staging (memoised on the batch's request ids), then
+     one decoder forward;
   5. greedy argmax or beam candidates on the GPU, one small copy back, and the step's
      decisions (forks, finishes, frees) in the native runtime.
 
@@ -179,6 +180,9 @@ class Engine:
         if n == 0:
             return []
         copies = self.rt.prepare_step()
+        # copy-on-write first: the GPU copies the blocks while the host packs the step's rows
+        # (the copies touch only the self pools; nothing below reads or writes those blocks first)
+        self.kv.copy_blocks(copies, checked=True)
         g = self.graphs.graph_for(n, params.num_beams) if self.graphs is not None else None
         if g is not None:
             rows = self.rt.pack_step(*g.host_views())
@@ -189,7 +193,6 @@ class Engine:
         fresh = np.flatnonzero(rows.positions == 0)
         if len(fresh):
             self._encode([self.requests[int(r)] for r in rows.request_ids[fresh]])
-        self.kv.copy_blocks(copies, checked=True)
         if self.record is not None:
             tables = g.host_views()[0] if g is not None else host[: n * W].reshape(n, W)
             self.record.append({"request_ids": rows.request_ids.tolist(), "positions": rows.positions.tolist(),
