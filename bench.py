@@ -617,6 +617,37 @@ def run_ring_sweep(args):
         del k, v
 
 
+def run_profile_attn(args):
+    """The workload of the attention captures: three calls of paged attention for R requests x
+    ROWS query rows (beams sharing one request's pages, as the engine's cross-attention) over LEN
+    tokens each, the planner's plan (bf16, 16 heads x 64, block 16, block tables a random
+    permutation of the pool)."""
+    from vflorence_b200 import paged_ops as ops
+
+    R, rows, length = (int(x) for x in args.profile_attn.split(","))
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    g = torch.Generator().manual_seed(0)
+    nb = -(-length // BS)
+    k = torch.randn(R * nb, H, BS, D, device=device, dtype=DTYPE)
+    v = torch.randn_like(k)
+    table = torch.randperm(R * nb, generator=g).to(torch.int32).view(R, nb).to(device)
+    q = torch.randn(R * rows, H, D, device=device, dtype=DTYPE)
+    out = torch.empty_like(q)
+    lens = torch.full((R,), length, dtype=torch.int32)
+    qsl = torch.arange(0, R * rows + 1, rows, dtype=torch.int32)
+    meta = ops.get_scheduler_metadata(R, H, H, D, lens, DTYPE, qsl, False, "sm100", BS)
+    lens_d, qsl_d = lens.to(device), qsl.to(device)
+    for _ in range(3):
+        ops.attention_with_kv_cache(q, k, v, out, qsl_d, lens_d, D ** -0.5, False, table, meta)
+    torch.cuda.synchronize()
+    if ops.read_device_errors(device):
+        raise RuntimeError("attention raised device error bits")
+    p = ops.plan_of(meta)
+    print(json.dumps({"point": "profile_attn", "requests": R, "rows": rows, "len": length,
+                      "plan": [p.num_splits, p.blocks_per_split, p.stages, p.heads_per_cta]}))
+
+
 def run_profile_step(args):
     """The workload of the decode-step launch list: the config's engine with CUDA graphs, one
     wave of requests, 120 steps (half of max_tokens for shorter jobs), then one step between
@@ -975,6 +1006,8 @@ def main():
                     help="under-filled attention shapes against 2-8 ring stages, one line per shape")
     ap.add_argument("--profile-step", choices=["cfg1", "cfg2", "cfg3", "cfg4"], default=None,
                     help="one decode step of the config's engine inside a profiler range (for ncu)")
+    ap.add_argument("--profile-attn", default=None, metavar="R,ROWS,LEN",
+                    help="three paged-attention calls of R requests x ROWS rows over LEN tokens (for ncu)")
     ap.add_argument("--profile-kv-proj", type=int, default=0, metavar="TOKENS",
                     help="three encoder K/V projection calls at TOKENS tokens (for ncu)")
     ap.add_argument("--decode", choices=["cfg1", "cfg2", "cfg3", "cfg4"], default=None,
@@ -1006,6 +1039,9 @@ def main():
         return
     if args.profile_kv_proj:
         run_profile_kv_proj(args)
+        return
+    if args.profile_attn:
+        run_profile_attn(args)
         return
     if args.decode:
         run_decode(args)
