@@ -809,18 +809,22 @@ def serve_arrivals(eng, reqs, params, arrivals):
     t0 = time.perf_counter()
     rid_of, arrived, latency = [], {}, {}
     i = 0
-    while i < len(reqs) or not eng.is_finished():
-        now = time.perf_counter() - t0
-        while i < len(reqs) and arrivals[i] <= now:
-            rid = eng.add_request(reqs[i], params)
-            rid_of.append(rid)
-            arrived[rid] = arrivals[i]
-            i += 1
-        if eng.is_finished():
-            time.sleep(max(0.0, arrivals[i] - (time.perf_counter() - t0)))
-            continue
-        for rid in eng.step():
-            latency[rid] = time.perf_counter() - t0 - arrived[rid]
+    try:
+        while i < len(reqs) or not eng.is_finished():
+            now = time.perf_counter() - t0
+            while i < len(reqs) and arrivals[i] <= now:
+                rid = eng.add_request(reqs[i], params)
+                rid_of.append(rid)
+                arrived[rid] = arrivals[i]
+                i += 1
+            if eng.is_finished():
+                time.sleep(max(0.0, arrivals[i] - (time.perf_counter() - t0)))
+                continue
+            for rid in eng.step():
+                latency[rid] = time.perf_counter() - t0 - arrived[rid]
+    except BaseException:
+        eng.abort()  # as Engine.generate does: no request is left half-served
+        raise
     return [eng.outputs.pop(r) for r in rid_of], [latency[r] for r in rid_of]
 
 

@@ -12,6 +12,7 @@ import subprocess
 import sys
 import time
 
+import pytest
 import torch
 
 from vflorence_b200.attention import group_rows
@@ -183,6 +184,10 @@ class _FakeEngine:
     def is_finished(self):
         return not self.queue
 
+    def abort(self):
+        self.queue.clear()
+        self.aborted = True
+
     def step(self):
         self.step_count += 1
         done = []
@@ -213,3 +218,18 @@ def test_poisson_arrivals_and_serving_loop():
     assert all(x >= 0 for x in lat) and len(lat) == 4
     for rid, t in eng.added_at.items():
         assert t - t0 >= arrivals[rid] - 1e-3
+
+
+def test_serving_loop_aborts_the_engine_on_a_failed_step():
+    """A step that raises leaves no request half-served: the loop aborts the engine and re-raises."""
+    import bench
+
+    eng = _FakeEngine()
+
+    def failing_step():
+        raise RuntimeError("planted step failure")
+
+    eng.step = failing_step
+    with pytest.raises(RuntimeError, match="planted"):
+        bench.serve_arrivals(eng, ["r0", "r1"], None, [0.0, 0.0])
+    assert getattr(eng, "aborted", False) and eng.is_finished()
