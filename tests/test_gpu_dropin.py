@@ -65,7 +65,7 @@ def reference_cross_attention(query, layer_idx, scale, ctx):
     return out
 
 
-def _reference_context(step, run, isa, layers):
+def _reference_context(step, run, isa, layers, dtype=torch.float32):
     """The Context the reference's _prepare publishes for a recorded step: its own host tensors,
     the self metadata from model_runner.py:308-319, and the cross staging rebuilt from each row's
     pages (the recorded padded table's leading ceil(enc_len / bs) entries)."""
@@ -74,7 +74,7 @@ def _reference_context(step, run, isa, layers):
     bs, H, D = run["block_size"], run["num_heads"], run["head_dim"]
     lens = step["ctx_context_lens"]
     meta = vllm_cpu_attn.get_scheduler_metadata(
-        num_reqs=len(lens), num_heads=H, num_kv_heads=H, head_dim=D, seq_lens=lens, dtype=torch.float32,
+        num_reqs=len(lens), num_heads=H, num_kv_heads=H, head_dim=D, seq_lens=lens, dtype=dtype,
         query_start_loc=step["ctx_query_start_loc"], causal=False, isa=isa, block_size=bs)
     enc = step["cross_seq_lens"].tolist()
     pages = [step["cross_block_table"][i, : -(-n // bs)].clone() for i, n in enumerate(enc)]
@@ -84,30 +84,34 @@ def _reference_context(step, run, isa, layers):
                    query_start_loc=step["ctx_query_start_loc"], self_metadata=meta, isa=isa, cross_staged=staged)
 
 
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16], ids=["f32", "bf16"])
 @pytest.mark.parametrize("run_name", ["greedy", "beam2", "beam4"])
 @pytest.mark.parametrize("ops", ["reference_bodies", "product_ops"])
-def test_reference_call_forms_replay_trace(engine_trace, oracle_lib, run_name, ops):
+def test_reference_call_forms_replay_trace(engine_trace, oracle_lib, run_name, ops, dtype):
     """Every recorded step: append + self-attention and cross-attention of one layer, with the
-    reference's host metadata, on the GPU and on the oracle; outputs within the fp32 bar and the
-    pools bit-exact after every append."""
+    reference's host metadata, on the GPU and on the oracle; outputs within the bar of the dtype
+    and the pools bit-exact after every append. In bf16 (head_dim 64) the product's
+    self-attention op takes the tensor-core kernel with the KV append fused into it, here fed
+    the reference's host slot mapping, lengths and tables."""
     from vflorence_b200 import attention  # noqa: F401  (registers torch.ops.vflorence.*)
     from vflorence_b200.context import set_context
 
     run = next(r for r in engine_trace["runs"] if r["name"] == run_name)
     bs, H, D = run["block_size"], run["num_heads"], run["head_dim"]
-    isa = vllm_cpu_attn.get_isa(torch.float32, bs, D)
+    isa = vllm_cpu_attn.get_isa(dtype, bs, D)
     g = torch.Generator().manual_seed(3)
+    rnd = lambda *shape: torch.randn(*shape, generator=g).to(dtype)  # noqa: E731
     shape = (run["num_blocks"], H, bs, D)
-    k_host, v_host = torch.randn(shape, generator=g), torch.randn(shape, generator=g)
+    k_host, v_host = rnd(*shape), rnd(*shape)
     cross = (run["num_cross_blocks"], H, bs, D)
-    ck_host, cv_host = torch.randn(cross, generator=g), torch.randn(cross, generator=g)
+    ck_host, cv_host = rnd(*cross), rnd(*cross)
     k_dev, v_dev = k_host.to(DEV), v_host.to(DEV)
     layers = [_Layer(_Attn(ck_host.to(DEV), cv_host.to(DEV), H, D))]
     scale = D ** -0.5
     for n, step in enumerate(run["steps"]):
         B = len(step["ctx_context_lens"])
-        q, k, v, qc = (torch.randn(B, H, D, generator=g) for _ in range(4))
-        ctx = _reference_context(step, run, isa, layers)
+        q, k, v, qc = (rnd(B, H, D) for _ in range(4))
+        ctx = _reference_context(step, run, isa, layers, dtype)
         if ops == "reference_bodies":
             out = reference_self_attention(q.to(DEV), k.to(DEV), v.to(DEV), k_dev, v_dev, scale, ctx)
             out_c = reference_cross_attention(qc.to(DEV), 0, scale, ctx)
@@ -126,8 +130,8 @@ def test_reference_call_forms_replay_trace(engine_trace, oracle_lib, run_name, o
         want_c = torch.empty_like(qc)
         oracle_lib.attention(qc, ck_host, cv_host, want_c, torch.arange(B + 1, dtype=torch.int32),
                              step["cross_seq_lens"], scale, False, step["cross_block_table"])
-        assert_attention_close(out, want, torch.float32, f"{run_name} step {n} self")
-        assert_attention_close(out_c, want_c, torch.float32, f"{run_name} step {n} cross")
+        assert_attention_close(out, want, dtype, f"{run_name} step {n} self")
+        assert_attention_close(out_c, want_c, dtype, f"{run_name} step {n} cross")
         assert torch.equal(k_dev.cpu(), k_host) and torch.equal(v_dev.cpu(), v_host), f"step {n} pools"
     assert vllm_cpu_attn.read_device_errors(DEV) == 0
 
