@@ -617,6 +617,75 @@ def run_ring_sweep(args):
         del k, v
 
 
+def run_schedule_sweep(args):
+    """The measurements behind the planner's choice of schedule: for 8-512 requests x 1, 3 or 4
+    query rows x 128-4096 tokens (near-uniform U[3/4 ctx, ctx] and skewed U[1, ctx] lengths),
+    the item grid of the planner's split rule against the balanced schedule at 2 and 4 stages x
+    4-32 tiles per CTA at least. Device time per call with L2 flushed, bf16, 16 heads x 64,
+    block 16, block tables a random permutation of the pool. One JSON line per shape."""
+    from vflorence_b200 import paged_ops as ops
+
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    flush = torch.empty(192 * 1024 * 1024, dtype=torch.uint8, device=device)
+    g = torch.Generator().manual_seed(0)
+    peak, _ = load_peaks()
+    shapes = []
+    for rpr in (1, 3, 4):
+        for R in (8, 32, 85, 128, 256, 512):
+            if rpr > 1 and R > 256:
+                continue
+            for ctx in (128, 592, 1024, 2048, 4096):
+                for skew in (False, True):
+                    if not (skew and ctx < 1024) and R * ctx <= 512 * 2048:
+                        shapes.append((rpr, R, ctx, skew))
+    if args.sweep_shapes:
+        keep = {tuple(int(x) for x in s.split("x")) for s in args.sweep_shapes.split(",")}
+        shapes = [s for s in shapes if (s[0], s[1], s[2]) in keep]
+    for rpr, R, ctx, skew in shapes:
+        nb = -(-ctx // BS)
+        lens = torch.randint(1 if skew else max(1, ctx * 3 // 4), ctx + 1, (R,), generator=g).to(torch.int32)
+        k = torch.randn(R * nb, H, BS, D, device=device, dtype=DTYPE)
+        v = torch.randn_like(k)
+        table = torch.randperm(R * nb, generator=g).to(torch.int32).view(R, nb).to(device)
+        q = torch.randn(R * rpr, H, D, device=device, dtype=DTYPE)
+        out = torch.empty_like(q)
+        qsl = torch.arange(0, R * rpr + 1, rpr, dtype=torch.int32)
+        lens_d, qsl_d = lens.to(device), qsl.to(device)
+
+        def us(meta):
+            call = lambda: ops.attention_with_kv_cache(q, k, v, out, qsl_d, lens_d, D ** -0.5,  # noqa: E731
+                                                       False, table, meta)
+            call()
+            return round(_time_op(call, 10, flush) * 1e3, 2)
+
+        mk = lambda: ops.get_scheduler_metadata(R, H, H, D, lens, DTYPE, qsl, False, "sm100", BS)  # noqa: E731
+        base = mk()
+        bp = ops.plan_of(base)
+        nbytes = int(lens.long().sum()) * H * D * ELEM * 2
+        row = {"point": "schedule_sweep", "rows_per_request": rpr, "requests": R, "ctx": ctx,
+               "lengths": "U[1,ctx]" if skew else "U[3/4 ctx,ctx]", "bytes": nbytes,
+               "plan": [bp.schedule, bp.num_splits, bp.blocks_per_split, bp.stages, bp.min_tiles],
+               "plan_us": us(base)}
+        items = ops.set_schedule(mk(), ops.SCHEDULE_ITEMS)
+        row["items_us"] = us(items)
+        var = {}
+        for stages in (2, 4):
+            for min_tiles in (4, 8, 16, 32):
+                m = mk()
+                ops.plan_of(m).stages = stages
+                ops.set_schedule(m, ops.SCHEDULE_BALANCED, min_tiles)
+                var[f"{stages}/{min_tiles}"] = us(m)
+        best = min(var, key=var.get)
+        row.update(balanced_best=[best, var[best]], items_over_best_balanced=round(row["items_us"] / var[best], 3),
+                   plan_frac_of_hbm=round(nbytes / (row["plan_us"] * 1e-6) / (peak * 1e9), 3),
+                   balanced_stages_min_tiles=var)
+        if ops.read_device_errors(device):
+            raise RuntimeError(f"device error bits at {row}")
+        print(json.dumps(row), flush=True)
+        del k, v
+
+
 def run_profile_attn(args):
     """The workload of the attention captures: three calls of paged attention for R requests x
     ROWS query rows (beams sharing one request's pages, as the engine's cross-attention) over LEN
@@ -1008,6 +1077,10 @@ def main():
     ap.add_argument("--sweep-batches", default="1,2,4,8,16,32,64,128,256,512,1024")
     ap.add_argument("--ring-sweep", action="store_true",
                     help="under-filled attention shapes against 2-8 ring stages, one line per shape")
+    ap.add_argument("--schedule-sweep", action="store_true",
+                    help="item grid against the balanced schedule (attention), one line per shape")
+    ap.add_argument("--sweep-shapes", default="",
+                    help="--schedule-sweep: only these ROWSxREQUESTSxCTX shapes (comma-separated)")
     ap.add_argument("--profile-step", choices=["cfg1", "cfg2", "cfg3", "cfg4"], default=None,
                     help="one decode step of the config's engine inside a profiler range (for ncu)")
     ap.add_argument("--profile-attn", default=None, metavar="R,ROWS,LEN",
@@ -1037,6 +1110,9 @@ def main():
         return
     if args.ring_sweep:
         run_ring_sweep(args)
+        return
+    if args.schedule_sweep:
+        run_schedule_sweep(args)
         return
     if args.profile_step:
         run_profile_step(args)

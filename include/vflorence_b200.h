@@ -33,7 +33,7 @@
 extern "C" {
 #endif
 
-#define VFL_ABI_VERSION 3
+#define VFL_ABI_VERSION 4
 
 typedef enum vfl_status {
   VFL_OK = 0,
@@ -57,6 +57,18 @@ typedef enum vfl_dtype {
 #define VFL_DEVERR_TIMEOUT 0x8u   /* a bounded wait on a shared-memory barrier gave up      */
 #define VFL_DEVERR_QUERY 0x10u    /* query_start_loc not non-decreasing / beyond num_tokens  */
 
+/* How a plan spreads the work over CTAs.
+ * VFL_SCHEDULE_ITEMS: one CTA per (request, head group, query chunk, split-K range).
+ * VFL_SCHEDULE_BALANCED (tensor-core kernel, at most 8 query rows per request, no row tables):
+ *   one persistent wave of num_splits CTAs; the (request, head group) items' 16-token tiles
+ *   are laid end to end and each CTA takes an equal run of them, cutting items where the runs
+ *   end; a second launch merges the pieces of cut items. Chosen for calls that would fill the
+ *   GPU's CTA slots unevenly. */
+typedef enum vfl_attention_schedule {
+  VFL_SCHEDULE_ITEMS = 0,
+  VFL_SCHEDULE_BALANCED = 1
+} vfl_attention_schedule;
+
 /* Launch plan for vfl_attention_with_kv_cache. Built on the host from host-side lengths;
  * plays the role of vllm_cpu_attn's opaque scheduler metadata. */
 typedef struct vfl_attention_plan {
@@ -73,14 +85,16 @@ typedef struct vfl_attention_plan {
   int32_t heads_per_cta;    /* heads handled by one CTA (one warp each)                  */
   int32_t queries_per_cta;  /* query rows of one request handled together: 1 or 4 (CUDA-core
                                kernel), 8 (tensor-core kernel: bf16, head_dim 64)          */
-  int32_t blocks_per_split; /* KV blocks per split-K work item                           */
+  int32_t blocks_per_split; /* KV blocks per split-K work item (VFL_SCHEDULE_ITEMS)      */
   int32_t num_splits;       /* split-K partitions of the longest request                 */
   int32_t stages;           /* shared-memory pipeline depth (16-token K/V tiles)         */
   int32_t merge_in_kernel;  /* split partials merged by the last split CTA (1) or by a
                                separate combine launch (0)                              */
   int64_t workspace_bytes;  /* scratch the caller must pass (0 = none)                   */
   int32_t row_tables;       /* 1: block_table rows are query rows (vfl_plan_attention_row_tables) */
-  int32_t reserved;
+  int32_t schedule;         /* vfl_attention_schedule                                    */
+  int32_t min_tiles;        /* VFL_SCHEDULE_BALANCED: fewest 16-token tiles per CTA      */
+  int32_t balanced_ctas;    /* VFL_SCHEDULE_BALANCED: CTAs of the persistent grid        */
 } vfl_attention_plan;
 
 #define VFL_PLAN_MAGIC 0x31504c4656LL /* "VFLP1" */
@@ -135,6 +149,13 @@ int vfl_plan_attention(int num_reqs, int num_heads, int num_kv_heads, int head_d
 int vfl_plan_attention_row_tables(int num_reqs, int num_heads, int num_kv_heads, int head_dim,
                                   int block_size, int dtype, const int32_t* seq_lens_host,
                                   const int32_t* query_start_loc_host, vfl_attention_plan* plan);
+
+/* (new: no reference counterpart - vllm_cpu_attn's metadata is opaque.) Re-plans `plan` (from
+ * vfl_plan_attention) for the given vfl_attention_schedule: VFL_SCHEDULE_ITEMS, or
+ * VFL_SCHEDULE_BALANCED with at least min_tiles 16-token tiles per CTA (0: the default).
+ * Updates workspace_bytes. VFL_ERR_UNSUPPORTED when the plan cannot be balanced (not the
+ * tensor-core kernel, row tables, more than 8 query rows per request or 512 requests). */
+int vfl_plan_attention_schedule(vfl_attention_plan* plan, int schedule, int min_tiles);
 
 /* replaces vllm_cpu_attn.reshape_and_cache(key, value, k_cache, v_cache, slot_mapping, isa=)
  *   (vflorence/layers/attention.py:55-57, vflorence/engine/model_runner.py:252-259).

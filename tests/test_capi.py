@@ -29,7 +29,7 @@ def test_library_exports_every_declared_symbol(native):
     assert sorted(declared) == sorted(_native.EXPORTS)
     for name in declared:
         assert hasattr(native, name), name
-    assert native.vfl_abi_version() == _native.ABI_VERSION == 3
+    assert native.vfl_abi_version() == _native.ABI_VERSION == 4
 
 
 def test_bounded_wait_check_refuses_limits_on_the_host(native):
@@ -181,6 +181,72 @@ def test_plan_rejects_bad_input(native):
         _plan([3, 4], qsl=[0, 2, 1])
     with pytest.raises(ValueError):
         _plan([3, 4], qsl=[0, 1])
+
+
+def _r256(x):
+    return -(-x // 256) * 256
+
+
+def test_plan_balanced_schedule(native):
+    """vfl_plan_attention_schedule re-plans a call for one persistent wave: 148 SMs x 3 CTAs,
+    at least 8 tiles per CTA by default, a workspace of partial records (2 per CTA, head and
+    row) and the item directory; back to the item grid restores the grid's workspace."""
+    from vflorence_b200 import paged_ops as ops
+
+    lens = torch.full((85,), 592, dtype=torch.int32)
+    qsl = torch.arange(0, 256, 3, dtype=torch.int32)
+    meta = ops.get_scheduler_metadata(85, 16, 16, 64, lens, torch.bfloat16, qsl, False, "sm100", 16)
+    ops.set_schedule(meta, ops.SCHEDULE_ITEMS)
+    items_ws = ops.plan_of(meta).workspace_bytes
+    ops.set_schedule(meta, ops.SCHEDULE_BALANCED)
+    p = ops.plan_of(meta)
+    assert (p.schedule, p.balanced_ctas, p.min_tiles) == (ops.SCHEDULE_BALANCED, 148 * 3, 8)
+    recs = 148 * 3 * 2 * 4 * 8
+    assert p.workspace_bytes == _r256(recs * 64 * 4) + _r256(recs * 2 * 4) + _r256(85 * 4 * 16)
+    ops.set_schedule(meta, ops.SCHEDULE_BALANCED, 3)
+    assert ops.plan_of(meta).min_tiles == 3
+    ops.set_schedule(meta, ops.SCHEDULE_ITEMS)
+    p = ops.plan_of(meta)
+    assert (p.schedule, p.min_tiles, p.balanced_ctas, p.workspace_bytes) == (ops.SCHEDULE_ITEMS, 0, 0, items_ws)
+
+
+def test_plan_balanced_schedule_refused_where_not_built(native):
+    from vflorence_b200 import paged_ops as ops
+
+    def meta(n=4, rows=1, d=64, dtype=torch.bfloat16, row_tables=False):
+        lens = torch.full((n,), 300, dtype=torch.int32)
+        qsl = torch.arange(0, n * rows + 1, rows, dtype=torch.int32)
+        return ops.get_scheduler_metadata(n, 16, 16, d, lens, dtype, qsl, False, "sm100", 16, row_tables=row_tables)
+
+    for m in (meta(dtype=torch.float32), meta(d=128), meta(rows=9), meta(n=513), meta(rows=2, row_tables=True)):
+        with pytest.raises(ValueError, match="balanced"):
+            ops.set_schedule(m, ops.SCHEDULE_BALANCED)
+        assert ops.plan_of(m).schedule == ops.SCHEDULE_ITEMS
+    with pytest.raises(ValueError, match="schedule"):
+        ops.set_schedule(meta(), 2)
+    with pytest.raises(ValueError, match="min_tiles"):
+        ops.set_schedule(meta(), ops.SCHEDULE_BALANCED, -1)
+    assert ops.plan_of(meta(n=512)).num_reqs == 512
+    ops.set_schedule(meta(n=512), ops.SCHEDULE_BALANCED)  # the most requests it takes
+
+
+@pytest.mark.parametrize("field,value", [("schedule", 2), ("min_tiles", 0), ("balanced_ctas", 0),
+                                         ("balanced_ctas", 148 * 3 + 1), ("workspace_bytes", 4096),
+                                         ("row_tables", 1), ("max_q_len", 9)])
+def test_attention_refuses_a_corrupted_balanced_plan_before_the_device(native, field, value):
+    from vflorence_b200 import _native
+    from vflorence_b200 import paged_ops as ops
+
+    lens = torch.tensor([2048, 1000, 37], dtype=torch.int32)
+    meta = ops.get_scheduler_metadata(3, 16, 16, 64, lens, torch.bfloat16, None, False, "sm100", 16)
+    ops.set_schedule(meta, ops.SCHEDULE_BALANCED)
+    plan = ops.plan_of(meta)
+    setattr(plan, field, value)
+    fake = 1 << 20  # never dereferenced: the call must fail before touching memory
+    st = native.vfl_attention_with_kv_cache(ctypes.byref(plan), fake, 16 * 64, fake, fake, 1000, fake, 16 * 64,
+                                            fake, fake, fake, 128, 128, 1.0, fake, 1 << 30, None)
+    assert st == _native.VFL_ERR_INVALID_ARGUMENT, native.vfl_last_error_message()
+    assert b"plan" in native.vfl_last_error_message()
 
 
 def test_attention_rejects_foreign_metadata_without_touching_the_gpu(native):

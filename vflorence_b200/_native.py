@@ -20,7 +20,7 @@ VFL_ERR_UNSUPPORTED = 2
 VFL_ERR_WORKSPACE = 3
 VFL_ERR_CUDA = 4
 VFL_ERR_CAPACITY = 5
-ABI_VERSION = 3
+ABI_VERSION = 4
 
 DTYPE_F32 = 0
 DTYPE_BF16 = 1
@@ -45,6 +45,7 @@ EXPORTS = (
     "vfl_get_isa",
     "vfl_plan_attention",
     "vfl_plan_attention_row_tables",
+    "vfl_plan_attention_schedule",
     "vfl_reshape_and_cache",
     "vfl_attention_with_kv_cache",
     "vfl_attention_with_kv_cache_append",
@@ -107,7 +108,9 @@ class AttentionPlan(ctypes.Structure):
         ("merge_in_kernel", ctypes.c_int32),
         ("workspace_bytes", ctypes.c_int64),
         ("row_tables", ctypes.c_int32),
-        ("reserved", ctypes.c_int32),
+        ("schedule", ctypes.c_int32),
+        ("min_tiles", ctypes.c_int32),
+        ("balanced_ctas", ctypes.c_int32),
     ]
 
 
@@ -169,6 +172,7 @@ def _declare(L):
         "vfl_get_isa": (i32, [i32, i32, i32, ctypes.c_char_p, i32]),
         "vfl_plan_attention": (i32, [i32, i32, i32, i32, i32, i32, i32, vp, vp, plan_p]),
         "vfl_plan_attention_row_tables": (i32, [i32, i32, i32, i32, i32, i32, vp, vp, plan_p]),
+        "vfl_plan_attention_schedule": (i32, [plan_p, i32, i32]),
         "vfl_reshape_and_cache": (i32, [vp, vp, vp, vp, vp, i64, i32, i32, i32, i64, i64, i64, i32, vp]),
         "vfl_attention_with_kv_cache": (i32, [vp, vp, i64, vp, vp, i64, vp, i64, vp, vp, vp, i64, i32,
                                               f32, vp, sz, vp]),

@@ -107,6 +107,65 @@ int make_tensor_map_2d_bf16(const void* base, uint64_t inner, uint64_t outer, ui
   return VFL_OK;
 }
 
+// The balanced schedule's shapes: the tensor-core kernel, one query chunk per request, one
+// block table per request, lengths and rows that fit its shared-memory arrays.
+bool balanced_supported(const vfl_attention_plan* plan) {
+  return plan->queries_per_cta == kTcRows && use_tensor_cores(plan->dtype, plan->head_dim) && plan->row_tables == 0 &&
+         plan->max_q_len <= kTcRows && plan->num_reqs >= 1 && plan->num_reqs <= kBalancedMaxReqs &&
+         plan->max_seq_len < kBalancedMaxLen;
+}
+
+// Workspace of an item-schedule plan: acc partials | (m, l) partials | arrival counters.
+int64_t items_workspace(const vfl_attention_plan* plan) {
+  if (plan->num_splits <= 1) return 0;
+  const int64_t items = (int64_t)plan->total_q * plan->num_heads * plan->num_splits;
+  const int64_t q_chunks =
+      ceil_div((int64_t)(plan->max_q_len < 1 ? 1 : plan->max_q_len), (int64_t)plan->queries_per_cta);
+  return ceil_div(items * plan->head_dim * 4, (int64_t)256) * 256 + ceil_div(items * 2 * 4, (int64_t)256) * 256 +
+         (plan->merge_in_kernel
+              ? (int64_t)plan->num_reqs * (plan->num_heads / plan->heads_per_cta) * q_chunks * 4
+              : 0);
+}
+
+// Sets a plan's schedule and the fields and workspace it implies (the plan is otherwise filled).
+int set_schedule(vfl_attention_plan* plan, int schedule, int min_tiles) {
+  if (schedule == VFL_SCHEDULE_ITEMS) {
+    plan->schedule = VFL_SCHEDULE_ITEMS;
+    plan->min_tiles = 0;
+    plan->balanced_ctas = 0;
+    plan->workspace_bytes = items_workspace(plan);
+    return VFL_OK;
+  }
+  if (schedule != VFL_SCHEDULE_BALANCED)
+    return fail(VFL_ERR_INVALID_ARGUMENT, "attention: schedule %d", schedule);
+  if (!balanced_supported(plan))
+    return fail(VFL_ERR_UNSUPPORTED,
+                "attention: the balanced schedule needs bf16 with head_dim 64, one block table per request, "
+                "at most %d query rows per request and %d requests",
+                kTcRows, kBalancedMaxReqs);
+  if (min_tiles < 0) return fail(VFL_ERR_INVALID_ARGUMENT, "attention: min_tiles %d < 0", min_tiles);
+  const int hpc = plan->heads_per_cta;
+  const int stage_bytes = 2 * hpc * 16 * plan->head_dim * 2;
+  const int smem = kTcHeaderBytes + plan->stages * stage_bytes + balanced_sched_bytes(plan->num_reqs);
+  int per_sm = kSmemPerSM / (smem + 1024);
+  per_sm = per_sm > kBalancedCtasPerSM ? kBalancedCtasPerSM : per_sm;
+  if (per_sm < 1) return fail(VFL_ERR_UNSUPPORTED, "attention: balanced ring of %d stages too large", plan->stages);
+  plan->schedule = VFL_SCHEDULE_BALANCED;
+  plan->min_tiles = min_tiles > 0 ? min_tiles : kBalancedMinTiles;
+  plan->balanced_ctas = kNumSMs * per_sm;
+  plan->workspace_bytes = BalancedWorkspace(plan->balanced_ctas, hpc, plan->num_reqs, plan->num_heads).total();
+  return VFL_OK;
+}
+
+// Whether the balanced schedule beats the item grid for a plan (rule fitted below).
+bool balanced_pays_off(const vfl_attention_plan* plan, int64_t base_items, int64_t slots, bool skewed) {
+  (void)plan;
+  (void)base_items;
+  (void)slots;
+  (void)skewed;
+  return false;
+}
+
 // A plan is caller memory: every constraint the kernels rely on (shared-memory table slice,
 // stage ring, CTA shape, workspace size) is re-derived here before anything touches the device.
 int check_attention_plan(const vfl_attention_plan* plan) {
@@ -138,6 +197,22 @@ int check_attention_plan(const vfl_attention_plan* plan) {
     return fail(VFL_ERR_INVALID_ARGUMENT, "attention: plan merge mode %d", plan->merge_in_kernel);
   if (plan->row_tables != 0 && (plan->row_tables != 1 || !tc || plan->causal))
     return fail(VFL_ERR_INVALID_ARGUMENT, "attention: plan row_tables needs the tensor-core kernel, not causal");
+  if (plan->schedule != VFL_SCHEDULE_ITEMS && plan->schedule != VFL_SCHEDULE_BALANCED)
+    return fail(VFL_ERR_INVALID_ARGUMENT, "attention: plan schedule %d", plan->schedule);
+  if (plan->schedule == VFL_SCHEDULE_BALANCED) {
+    if (!balanced_supported(plan))
+      return fail(VFL_ERR_INVALID_ARGUMENT, "attention: balanced plan outside the balanced kernel's shapes");
+    if (plan->min_tiles < 1 || plan->balanced_ctas < 1 || plan->balanced_ctas > kNumSMs * kBalancedCtasPerSM)
+      return fail(VFL_ERR_INVALID_ARGUMENT, "attention: balanced plan min_tiles %d / %d CTAs", plan->min_tiles,
+                  plan->balanced_ctas);
+    if (kTcHeaderBytes + plan->stages * stage_bytes + balanced_sched_bytes(plan->num_reqs) > 227 * 1024)
+      return fail(VFL_ERR_INVALID_ARGUMENT, "attention: balanced plan does not fit in shared memory");
+    const int64_t need = BalancedWorkspace(plan->balanced_ctas, hpc, plan->num_reqs, H).total();
+    if (plan->workspace_bytes < need)
+      return fail(VFL_ERR_INVALID_ARGUMENT, "attention: plan workspace_bytes %lld < the %lld its schedule needs",
+                  (long long)plan->workspace_bytes, (long long)need);
+    return VFL_OK;
+  }
   const int64_t q_chunks = ceil_div((int64_t)(plan->max_q_len < 1 ? 1 : plan->max_q_len), (int64_t)qpc);
   if (q_chunks > 65535 || (int64_t)plan->num_reqs * (H / hpc) > INT32_MAX)
     return fail(VFL_ERR_INVALID_ARGUMENT, "attention: plan launch grid too large");
@@ -299,14 +374,6 @@ int vfl_plan_attention(int num_reqs, int num_heads, int num_kv_heads, int head_d
   // call: the counters' memset and the merge on the tail's critical path).
   const int merge_in_kernel = 0;
 
-  // workspace: acc partials | (m, l) partials | arrival counters (in-kernel merge only)
-  int64_t ws = 0;
-  if (splits > 1) {
-    const int64_t items = total_q * num_heads * splits;
-    ws = ceil_div(items * head_dim * 4, (int64_t)256) * 256 + ceil_div(items * 2 * 4, (int64_t)256) * 256 +
-         (merge_in_kernel ? (int64_t)num_reqs * groups * q_chunks * 4 : 0);
-  }
-
   plan->magic = VFL_PLAN_MAGIC;
   plan->num_reqs = num_reqs;
   plan->num_heads = num_heads;
@@ -323,9 +390,10 @@ int vfl_plan_attention(int num_reqs, int num_heads, int num_kv_heads, int head_d
   plan->num_splits = static_cast<int32_t>(splits);
   plan->stages = stages;
   plan->merge_in_kernel = merge_in_kernel;
-  plan->workspace_bytes = ws;
   plan->row_tables = 0;
-  plan->reserved = 0;
+  set_schedule(plan, VFL_SCHEDULE_ITEMS, 0);  // sets workspace_bytes
+  if (balanced_pays_off(plan, base_items, slots, skewed) && set_schedule(plan, VFL_SCHEDULE_BALANCED, 0) != VFL_OK)
+    set_schedule(plan, VFL_SCHEDULE_ITEMS, 0);
   return VFL_OK;
 }
 
@@ -340,7 +408,15 @@ int vfl_plan_attention_row_tables(int num_reqs, int num_heads, int num_kv_heads,
                                     query_start_loc_host, plan);
   if (st) return st;
   plan->row_tables = 1;
-  return VFL_OK;
+  return set_schedule(plan, VFL_SCHEDULE_ITEMS, 0);
+}
+
+int vfl_plan_attention_schedule(vfl_attention_plan* plan, int schedule, int min_tiles) {
+  if (plan == nullptr || plan->magic != VFL_PLAN_MAGIC)
+    return fail(VFL_ERR_INVALID_ARGUMENT, "plan_attention_schedule: plan missing or not built by vfl_plan_attention");
+  const int st = check_attention_plan(plan);
+  if (st) return st;
+  return set_schedule(plan, schedule, min_tiles);
 }
 
 }  // extern "C"
@@ -410,6 +486,9 @@ int attention_run(const vfl_attention_plan* plan, const void* query, int64_t que
   p.stages = plan->stages;
   p.max_seq_len = plan->max_seq_len;
   p.row_tables = plan->row_tables;
+  p.schedule = plan->schedule;
+  p.min_tiles = plan->min_tiles;
+  p.balanced_ctas = plan->balanced_ctas;
   p.scale_log2 = scale * 1.4426950408889634f;
   if (append != nullptr) {
     p.new_k = append->key;
@@ -424,7 +503,14 @@ int attention_run(const vfl_attention_plan* plan, const void* query, int64_t que
   const int qpc = plan->queries_per_cta;
   const int q_chunks = static_cast<int>(ceil_div(plan->max_q_len < 1 ? 1 : plan->max_q_len, qpc));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (plan->num_splits > 1) {
+  const bool balanced = plan->schedule == VFL_SCHEDULE_BALANCED;
+  if (balanced) {
+    const BalancedWorkspace w(plan->balanced_ctas, hpc, plan->num_reqs, H);
+    char* base = static_cast<char*>(workspace);
+    p.ws_acc = reinterpret_cast<float*>(base);
+    p.ws_ml = reinterpret_cast<float*>(base + w.acc_bytes);
+    p.ws_desc = reinterpret_cast<int4*>(base + w.acc_bytes + w.ml_bytes);
+  } else if (plan->num_splits > 1) {
     const int64_t items = (int64_t)plan->total_q * H * plan->num_splits;
     const int64_t acc_bytes = ceil_div(items * D * 4, (int64_t)256) * 256;
     const int64_t ml_bytes = ceil_div(items * 2 * 4, (int64_t)256) * 256;
@@ -438,10 +524,11 @@ int attention_run(const vfl_attention_plan* plan, const void* query, int64_t que
       if (st) return st;
     }
   }
-  dim3 grid(plan->num_reqs * (H / hpc), plan->num_splits, q_chunks);
+  const dim3 grid = balanced ? dim3(plan->balanced_ctas) : dim3(plan->num_reqs * (H / hpc), plan->num_splits, q_chunks);
   const int threads = (hpc + 1) * 32;  // hpc consumer warps + one producer warp
   const bool tc = plan->queries_per_cta == kTcRows;
-  const int smem = (tc ? kTcHeaderBytes : kHeaderBytes) + plan->stages * 2 * hpc * 16 * D * es;
+  const int smem = (tc ? kTcHeaderBytes : kHeaderBytes) + plan->stages * 2 * hpc * 16 * D * es +
+                   (balanced ? balanced_sched_bytes(plan->num_reqs) : 0);
   if (tc) {
     const uint64_t rows = (uint64_t)num_blocks * H * plan->block_size;
     const uint32_t box_rows = plan->block_size == 16 ? 16u * hpc : 16u;

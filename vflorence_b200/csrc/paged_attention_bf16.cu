@@ -1,6 +1,6 @@
 // bfloat16 instantiations of the paged attention kernels (split from f32 to compile in parallel),
-// including the tensor-core variant for head_dim 64.
-#include "paged_attention_tc.cuh"
+// including the tensor-core variant for head_dim 64 and its balanced schedule.
+#include "paged_attention_balanced.cuh"
 
 namespace vfl {
 int launch_paged_attention_bf16(const AttnParams& p, int head_dim, int qpc, dim3 grid, int threads,
@@ -13,6 +13,30 @@ int launch_paged_attention_tc(const AttnParams& p, const CUtensorMap& kmap, cons
   static int smem_done[kMaxDevices];
   // plans ask for at most kMaxStageBytes of ring unless they set more stages (checked on the host)
   const int want = smem_bytes > kTcHeaderBytes + kMaxStageBytes ? smem_bytes : kTcHeaderBytes + kMaxStageBytes;
+  if (p.schedule == VFL_SCHEDULE_BALANCED) {
+    static int smem_done_balanced[kMaxDevices];
+    const int want_b = kTcHeaderBytes + kMaxStageBytes + balanced_sched_bytes(kBalancedMaxReqs);
+    int st = ensure_smem_attribute(reinterpret_cast<const void*>(paged_attention_tc_balanced_kernel),
+                                   smem_bytes > want_b ? smem_bytes : want_b, smem_done_balanced);
+    if (st) return st;
+    paged_attention_tc_balanced_kernel<<<grid, threads, smem_bytes, stream>>>(p, kmap, vmap);
+    st = cuda_status(cudaGetLastError(), "paged_attention (balanced) launch");
+    if (st) return st;
+    // the merge of cut items as a programmatic dependent launch: its CTAs start while the
+    // attention grid drains and wait for it (griddepcontrol.wait) before reading the pieces
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(static_cast<unsigned>(p.num_reqs * (p.num_heads / p.heads_per_cta)));
+    cfg.blockDim = dim3(static_cast<unsigned>(32 * p.heads_per_cta));
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cuda_status(cudaLaunchKernelEx(&cfg, paged_attention_tc_balanced_combine_kernel, p),
+                       "paged_attention (balanced) merge launch");
+  }
   int st = ensure_smem_attribute(reinterpret_cast<const void*>(paged_attention_tc_kernel), want, smem_done);
   if (st) return st;
   paged_attention_tc_kernel<<<grid, threads, smem_bytes, stream>>>(p, kmap, vmap);

@@ -53,11 +53,15 @@ struct AttnParams {
   int32_t stages;
   int32_t max_seq_len;  // planned maximum; longer device lengths are clamped and reported
   int32_t row_tables;   // 1: one block table per query row (tensor-core kernel only)
+  int32_t schedule;     // VFL_SCHEDULE_ITEMS or VFL_SCHEDULE_BALANCED (tensor-core kernel only)
+  int32_t min_tiles;    // balanced: fewest 16-token tiles a CTA takes
+  int32_t balanced_ctas;  // balanced: CTAs of the grid (partial records in the workspace)
   float scale_log2;  // softmax scale * log2(e)
   float* ws_acc;     // [total_q, H, num_splits, D]
   float* ws_ml;      // [total_q, H, num_splits, 2]
   int* ws_arrivals;  // [num_reqs, H / heads_per_cta, q_chunks], zero at launch; null: the
                      // combine kernel merges the partials instead
+  int4* ws_desc;     // balanced: [num_reqs, H / heads_per_cta] where each item's pieces went
   // fused KV append (tensor-core kernel only; null: the caches already hold every token): query
   // row t's new key / value, [H, D] dense at new_k + t * new_k_stride, go to slot slots[t] (< 0:
   // none) before the item reads the block that holds them
@@ -529,6 +533,31 @@ __global__ void __launch_bounds__(128) paged_attention_combine_kernel(const Attn
 // Tensor-core variant (paged_attention_tc.cuh): bf16, head_dim 64, up to kTcRows rows per CTA.
 constexpr int kTcHeaderBytes = 4096;  // SmemHeader | one 8x16 bf16 P tile per consumer warp | row tables
 constexpr int kTcRows = 8;            // query rows per CTA (the mma N dimension)
+
+// Balanced schedule (paged_attention_balanced.cuh).
+constexpr int kBalancedMaxReqs = 512;   // requests whose lengths and rows fit in shared memory
+constexpr int kBalancedMaxLen = 1 << 27;  // lengths packed with the row count into 32 bits
+constexpr int kBalancedCtasPerSM = 3;   // the kernel's launch bounds (registers)
+constexpr int kBalancedMinTiles = 8;    // default fewest 16-token tiles per CTA
+
+// Shared-memory bytes of its per-request arrays: tile prefix [R + 1], packed length and rows
+// [R], first query row [R].
+inline __host__ __device__ int balanced_sched_bytes(int num_reqs) {
+  return ((3 * num_reqs + 1) * 4 + 15) / 16 * 16;
+}
+
+// Its workspace: partial records acc [ctas, 2, hpc, kTcRows, 64] f32 | (m, l) [.., 2] f32 |
+// item directory [num_reqs, H / hpc] int4; each part 256-byte aligned.
+struct BalancedWorkspace {
+  int64_t acc_bytes, ml_bytes, desc_bytes;
+  __host__ __device__ BalancedWorkspace(int64_t ctas, int hpc, int64_t num_reqs, int num_heads) {
+    const int64_t recs = ctas * 2 * hpc * kTcRows;
+    acc_bytes = (recs * 64 * 4 + 255) / 256 * 256;
+    ml_bytes = (recs * 2 * 4 + 255) / 256 * 256;
+    desc_bytes = (num_reqs * (num_heads / hpc) * 16 + 255) / 256 * 256;
+  }
+  __host__ __device__ int64_t total() const { return acc_bytes + ml_bytes + desc_bytes; }
+};
 int launch_paged_attention_tc(const AttnParams& p, const CUtensorMap& kmap, const CUtensorMap& vmap, dim3 grid,
                               int threads, int smem_bytes, cudaStream_t stream);
 

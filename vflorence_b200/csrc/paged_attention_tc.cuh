@@ -92,6 +92,175 @@ __device__ __forceinline__ uint32_t pack_bf16x2_bits(__nv_bfloat16 lo, __nv_bflo
   return (uint32_t)__bfloat16_as_ushort(lo) | ((uint32_t)__bfloat16_as_ushort(hi) << 16);
 }
 
+// A consumer lane's place in the mma fragments and its ldmatrix rows / 16-byte chunks.
+struct TcLane {
+  int g, tq;                 // mma row group, thread in group
+  int k_row, k_chunk_hi;     // K tile rows (A = K through ldmatrix)
+  int v_row, v_chunk_hi;     // V tile rows (A = V^T through ldmatrix.trans)
+  __device__ __forceinline__ explicit TcLane(int lane) {
+    g = lane >> 2;
+    tq = lane & 3;
+    const int mat = lane >> 3;
+    k_row = (lane & 7) + (mat & 1) * 8;
+    k_chunk_hi = mat >> 1;
+    v_row = (lane & 7) + (mat >> 1) * 8;
+    v_chunk_hi = mat & 1;
+  }
+};
+
+// A consumer warp's running state for its head and this lane's query columns 2tq, 2tq+1:
+// max m and sum l per column (exp2 domain), and the O^T m-tiles [dim 16mt + g (+8)][column].
+struct TcAccum {
+  float m[2], l[2];
+  float o[4][4];
+  __device__ __forceinline__ void reset() {
+    m[0] = m[1] = -INFINITY;
+    l[0] = l[1] = 0.f;
+#pragma unroll
+    for (int mt = 0; mt < 4; ++mt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) o[mt][e] = 0.f;
+  }
+  // the l partial sums over the 8 row-group lanes that share each query column
+  __device__ __forceinline__ void reduce_l() {
+#pragma unroll
+    for (int e = 0; e < 2; ++e)
+#pragma unroll
+      for (int off = 4; off < 32; off <<= 1) l[e] += __shfl_xor_sync(0xffffffffu, l[e], off);
+  }
+  // column e normalised into the head's 64 outputs at dst (after reduce_l)
+  __device__ __forceinline__ void store_output(int e, __nv_bfloat16* dst, const TcLane& ln) const {
+    const float inv = l[e] > 0.f ? 1.f / l[e] : 0.f;
+#pragma unroll
+    for (int mt = 0; mt < 4; ++mt) {
+      dst[16 * mt + ln.g] = __float2bfloat16_rn(o[mt][e] * inv);
+      dst[16 * mt + ln.g + 8] = __float2bfloat16_rn(o[mt][e + 2] * inv);
+    }
+  }
+  // column e's (m, l, acc[64]) partial (after reduce_l)
+  __device__ __forceinline__ void store_partial(int e, float* acc, float* ml, const TcLane& ln) const {
+#pragma unroll
+    for (int mt = 0; mt < 4; ++mt) {
+      acc[16 * mt + ln.g] = o[mt][e];
+      acc[16 * mt + ln.g + 8] = o[mt][e + 2];
+    }
+    if (ln.g == 0) *reinterpret_cast<float2*>(ml) = make_float2(m[e], l[e]);
+  }
+};
+
+// One 16-token tile of one head, in its consumer warp:
+//   S[token g, g+8][query 2tq, 2tq+1] = K_tile . Q^T (K through ldmatrix, Q fragments bq);
+//   online softmax per query column (exp2 domain, lazy rescaling as in the CUDA-core kernel),
+//   masked to the rows the tile's block belongs to (row_on) and to each column's visible tokens;
+//   P rounded to bf16 through the warp's shared P tile; O^T += V^T . P^T.
+// kt / vt: shared addresses of the head's swizzled K and V tiles. The caller syncs the warp
+// before the stage or the P tile is reused.
+__device__ __forceinline__ void tc_consume_tile(uint32_t kt, uint32_t vt, const uint32_t (&bq)[4][2],
+                                                const bool (&row_on)[2], int tok0, const int (&vis_c)[2],
+                                                float scale_log2, __nv_bfloat16* p_tile, uint32_t p_tile_u32,
+                                                const TcLane& ln, TcAccum& acc) {
+  const int g = ln.g, tq = ln.tq;
+  float sc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int kk = 0; kk < 4; ++kk) {
+    uint32_t a[4];
+    ldsm_x4(swz(kt, ln.k_row, 2 * kk + ln.k_chunk_hi), a);
+    mma_bf16_16x8x16(sc, a, bq[kk][0], bq[kk][1]);
+  }
+  constexpr float kRescaleSlack = 8.f;
+  __nv_bfloat16 pb[4];
+#pragma unroll
+  for (int e = 0; e < 2; ++e) {
+    const bool v0 = row_on[e] && tok0 + g < vis_c[e];
+    const bool v1 = row_on[e] && tok0 + g + 8 < vis_c[e];
+    const float s0 = v0 ? sc[e] * scale_log2 : -INFINITY;
+    const float s1 = v1 ? sc[e + 2] * scale_log2 : -INFINITY;
+    float mx = fmaxf(s0, s1);
+#pragma unroll
+    for (int off = 4; off < 32; off <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+    if (mx > acc.m[e] + kRescaleSlack) {
+      const float alpha = acc.m[e] == -INFINITY ? 0.f : exp2_approx(acc.m[e] - mx);
+      acc.m[e] = mx;
+      acc.l[e] *= alpha;
+#pragma unroll
+      for (int mt = 0; mt < 4; ++mt) {
+        acc.o[mt][e] *= alpha;
+        acc.o[mt][e + 2] *= alpha;
+      }
+    }
+    const bool none = acc.m[e] == -INFINITY;
+    pb[e] = __float2bfloat16_rn(none ? 0.f : exp2_approx(s0 - acc.m[e]));
+    pb[e + 2] = __float2bfloat16_rn(none ? 0.f : exp2_approx(s1 - acc.m[e]));
+    acc.l[e] += __bfloat162float(pb[e]) + __bfloat162float(pb[e + 2]);
+  }
+  // P -> shared [query][token], then the PV B fragments: query g, tokens 2tq (+1), 2tq+8 (+9)
+  p_tile[(2 * tq) * 16 + g] = pb[0];
+  p_tile[(2 * tq + 1) * 16 + g] = pb[1];
+  p_tile[(2 * tq) * 16 + g + 8] = pb[2];
+  p_tile[(2 * tq + 1) * 16 + g + 8] = pb[3];
+  __syncwarp();
+  uint32_t bp0, bp1;
+  asm volatile("ld.shared.b32 %0, [%1];" : "=r"(bp0) : "r"(p_tile_u32 + (g * 16 + 2 * tq) * 2));
+  asm volatile("ld.shared.b32 %0, [%1];" : "=r"(bp1) : "r"(p_tile_u32 + (g * 16 + 2 * tq + 8) * 2));
+  // O^T += V^T . P^T over the tile's 16 tokens, four 16-dim m-tiles
+#pragma unroll
+  for (int mt = 0; mt < 4; ++mt) {
+    uint32_t a[4];
+    ldsm_x4_trans(swz(vt, ln.v_row, 2 * mt + ln.v_chunk_hi), a);
+    mma_bf16_16x8x16(acc.o[mt], a, bp0, bp1);
+  }
+}
+
+// The B operand of S = K.Q^T for query row `row` (g < nq) of head h: dims 16kk + 2tq (+1) and
+// 16kk + 8 + 2tq (+1); zeros for columns without a row.
+__device__ __forceinline__ void tc_load_query(const AttnParams& p, int64_t row, bool on, int h, const TcLane& ln,
+                                              uint32_t (&bq)[4][2]) {
+#pragma unroll
+  for (int kk = 0; kk < 4; ++kk) {
+    bq[kk][0] = bq[kk][1] = 0u;
+    if (on) {
+      const __nv_bfloat16* src =
+          static_cast<const __nv_bfloat16*>(p.q) + row * p.q_stride + h * 64 + kk * 16 + 2 * ln.tq;
+      bq[kk][0] = __ldg(reinterpret_cast<const unsigned int*>(src));
+      bq[kk][1] = __ldg(reinterpret_cast<const unsigned int*>(src + 8));
+    }
+  }
+}
+
+// Fused KV append, in the consumer warp of head h: the new key and value of each query row
+// q0 + j (j < nq) whose new position lies in [pos_lo, pos_hi) go to the row's slot, 16-byte
+// pieces (lanes 0-7 the key, 8-15 the value), then a proxy fence orders the stores before the
+// producer's TMA (async proxy) reads of the same block. Padding rows (slot < 0) store nothing.
+__device__ __forceinline__ void tc_append_rows(const AttnParams& p, int q0, int nq, int q_end, int L, int h,
+                                               int pos_lo, int pos_hi, int warp, int lane) {
+  using T = __nv_bfloat16;
+  constexpr int D = 64;
+  const int bs = p.block_size;
+  const int64_t capacity = p.num_blocks * (int64_t)bs;
+  for (int j = 0; j < nq; ++j) {
+    const int t = q0 + j;
+    const int pos = p.causal ? L - (q_end - t) : L - 1;
+    if (pos < pos_lo || pos >= pos_hi) continue;
+    const int64_t slot = __ldg(p.slots + t);
+    if (slot < 0) continue;  // padding row
+    if (slot >= capacity) {
+      if (warp == 0 && lane == 0) report(p.err, VFL_DEVERR_SLOT);
+      continue;
+    }
+    if (lane < 2 * (D / 8)) {
+      const int kv = lane >> 3, c = lane & 7;
+      const int64_t blk = slot / bs, off = slot - blk * bs;
+      const T* src =
+          static_cast<const T*>(kv ? p.new_v : p.new_k) + t * (kv ? p.new_v_stride : p.new_k_stride) + h * D + c * 8;
+      T* dst = static_cast<T*>(const_cast<void*>(kv ? p.v_cache : p.k_cache)) +
+               ((blk * p.num_heads + h) * bs + off) * D + c * 8;
+      *reinterpret_cast<uint4*>(dst) = ldg_nc_v4(src);
+    }
+  }
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+  __syncwarp();
+}
+
 // kmap / vmap: the K and V pools as 2-D [num_blocks * H * block_size rows, 64 columns] bf16 with
 // the 128-byte swizzle; box = 64 columns x (16 * heads_per_cta rows if block_size == 16, else 16).
 __global__ void __launch_bounds__(160, 3) paged_attention_tc_kernel(const AttnParams p,
@@ -262,44 +431,12 @@ __global__ void __launch_bounds__(160, 3) paged_attention_tc_kernel(const AttnPa
 
   // ================= consumers: one warp per head, mma fragments ==========================
   const int h = h0 + warp;
-  const int g = lane >> 2;   // mma row group
-  const int tq = lane & 3;   // mma thread-in-group
-  // B operand of S = K.Q^T: query row g, dims 16kk + 2tq (+1) and 16kk + 8 + 2tq (+1)
+  const TcLane ln(lane);
+  const int tq = ln.tq;
   uint32_t bq[4][2];
-#pragma unroll
-  for (int kk = 0; kk < 4; ++kk) {
-    bq[kk][0] = bq[kk][1] = 0u;
-    if (g < nq) {
-      const T* src = static_cast<const T*>(p.q) + (int64_t)(q0 + g) * p.q_stride + h * D + kk * 16 + 2 * tq;
-      bq[kk][0] = __ldg(reinterpret_cast<const unsigned int*>(src));
-      bq[kk][1] = __ldg(reinterpret_cast<const unsigned int*>(src + 8));
-    }
-  }
+  tc_load_query(p, q0 + ln.g, ln.g < nq, h, ln, bq);
   if (appends) {  // this warp's head of each row whose new position this split holds
-    const int64_t capacity = p.num_blocks * (int64_t)bs;
-    for (int j = 0; j < nq; ++j) {
-      const int t = q0 + j;
-      const int pos = p.causal ? L - (q_end - t) : L - 1;
-      if (pos < split_lo || pos >= split_hi) continue;
-      const int64_t slot = __ldg(p.slots + t);
-      if (slot < 0) continue;  // padding row
-      if (slot >= capacity) {
-        if (warp == 0 && lane == 0) report(p.err, VFL_DEVERR_SLOT);
-        continue;
-      }
-      if (lane < 2 * (D / 8)) {  // 16-byte pieces: lanes 0-7 the key, 8-15 the value
-        const int kv = lane >> 3, c = lane & 7;
-        const int64_t blk = slot / bs, off = slot - blk * bs;
-        const T* src = static_cast<const T*>(kv ? p.new_v : p.new_k) + t * (kv ? p.new_v_stride : p.new_k_stride) +
-                       h * D + c * 8;
-        T* dst = static_cast<T*>(const_cast<void*>(kv ? p.v_cache : p.k_cache)) +
-                 ((blk * p.num_heads + h) * bs + off) * D + c * 8;
-        *reinterpret_cast<uint4*>(dst) = ldg_nc_v4(src);
-      }
-    }
-    // the stores above, before the producer's TMA (async proxy) reads of the same block
-    asm volatile("fence.proxy.async.global;" ::: "memory");
-    __syncwarp();
+    tc_append_rows(p, q0, nq, q_end, L, h, split_lo, split_hi, warp, lane);
     if (lane == 0) mbar_arrive(&hdr.appended);
   }
   // this thread's two query columns 2tq, 2tq+1
@@ -307,19 +444,11 @@ __global__ void __launch_bounds__(160, 3) paged_attention_tc_kernel(const AttnPa
   vis_c[0] = visible(2 * tq);
   vis_c[1] = visible(2 * tq + 1);
   const bool col_on[2] = {2 * tq < nq, 2 * tq + 1 < nq};
-  float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
-  float o[4][4];  // O^T m-tiles: [dim 16mt + g (+8)][query 2tq (+1)]
-#pragma unroll
-  for (int mt = 0; mt < 4; ++mt)
-#pragma unroll
-    for (int e = 0; e < 4; ++e) o[mt][e] = 0.f;
+  TcAccum acc;
+  acc.reset();
   // this warp's P tile: [8 query rows][16 tokens] bf16
   T* p_tile = reinterpret_cast<T*>(smem + kTcPTileOffset) + warp * (kTcRows * 16);
   const uint32_t p_tile_u32 = smem_u32(p_tile);
-  // ldmatrix row/chunk of this lane: K (A = K rows) and V^T (A = V^T via .trans)
-  const int mat = lane >> 3;
-  const int k_row = (lane & 7) + (mat & 1) * 8, k_chunk_hi = mat >> 1;
-  const int v_row = (lane & 7) + (mat >> 1) * 8, v_chunk_hi = mat & 1;
 
   bool aborted = false;
   int u = 0;
@@ -333,114 +462,44 @@ __global__ void __launch_bounds__(160, 3) paged_attention_tc_kernel(const AttnPa
 #pragma unroll 1
     for (int j = tiles.count_and_get(bi, 0, done, &phys_unused, &mask); j < nq;
          j = tiles.count_and_get(bi, j + 1, done, &phys_unused, &mask)) {
-    done |= mask;
-    const int s = u % stages;
-    if (!mbar_wait_bounded(&hdr.full[s], (u / stages) & 1)) {
-      report(p.err, VFL_DEVERR_TIMEOUT);
-      if (lane == 0) {
-        hdr.abort = 1;
-        atomicMax(&hdr.consumed, u);
-      }
-      aborted = true;
-      break;
-    }
-    const uint32_t kt = smem_u32(s_kv + (size_t)s * stage_elems + warp * TILE);
-    const uint32_t vt = kt + hpc * TILE * sizeof(T);
-    // the rows this unit's block belongs to (every row without row tables)
-    const bool row_on[2] = {col_on[0] && ((mask >> (2 * tq)) & 1u), col_on[1] && ((mask >> (2 * tq + 1)) & 1u)};
-
-    // S[token g, g+8][query 2tq, 2tq+1]
-    float sc[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-    for (int kk = 0; kk < 4; ++kk) {
-      uint32_t a[4];
-      ldsm_x4(swz(kt, k_row, 2 * kk + k_chunk_hi), a);
-      mma_bf16_16x8x16(sc, a, bq[kk][0], bq[kk][1]);
-    }
-    // online softmax per query column (exp2 domain, lazy rescale as in the CUDA-core kernel)
-    constexpr float kRescaleSlack = 8.f;
-    __nv_bfloat16 pb[4];
-#pragma unroll
-    for (int e = 0; e < 2; ++e) {
-      const bool v0 = row_on[e] && tok0 + g < vis_c[e];
-      const bool v1 = row_on[e] && tok0 + g + 8 < vis_c[e];
-      const float s0 = v0 ? sc[e] * p.scale_log2 : -INFINITY;
-      const float s1 = v1 ? sc[e + 2] * p.scale_log2 : -INFINITY;
-      float mx = fmaxf(s0, s1);
-#pragma unroll
-      for (int off = 4; off < 32; off <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-      if (mx > m[e] + kRescaleSlack) {
-        const float alpha = m[e] == -INFINITY ? 0.f : exp2_approx(m[e] - mx);
-        m[e] = mx;
-        l[e] *= alpha;
-#pragma unroll
-        for (int mt = 0; mt < 4; ++mt) {
-          o[mt][e] *= alpha;
-          o[mt][e + 2] *= alpha;
+      done |= mask;
+      const int s = u % stages;
+      if (!mbar_wait_bounded(&hdr.full[s], (u / stages) & 1)) {
+        report(p.err, VFL_DEVERR_TIMEOUT);
+        if (lane == 0) {
+          hdr.abort = 1;
+          atomicMax(&hdr.consumed, u);
         }
+        aborted = true;
+        break;
       }
-      const bool none = m[e] == -INFINITY;
-      pb[e] = __float2bfloat16_rn(none ? 0.f : exp2_approx(s0 - m[e]));
-      pb[e + 2] = __float2bfloat16_rn(none ? 0.f : exp2_approx(s1 - m[e]));
-      l[e] += __bfloat162float(pb[e]) + __bfloat162float(pb[e + 2]);
-    }
-    // P -> shared [query][token], then the PV B fragments: query g, tokens 2tq (+1), 2tq+8 (+9)
-    p_tile[(2 * tq) * 16 + g] = pb[0];
-    p_tile[(2 * tq + 1) * 16 + g] = pb[1];
-    p_tile[(2 * tq) * 16 + g + 8] = pb[2];
-    p_tile[(2 * tq + 1) * 16 + g + 8] = pb[3];
-    __syncwarp();
-    uint32_t bp0, bp1;
-    asm volatile("ld.shared.b32 %0, [%1];" : "=r"(bp0) : "r"(p_tile_u32 + (g * 16 + 2 * tq) * 2));
-    asm volatile("ld.shared.b32 %0, [%1];" : "=r"(bp1) : "r"(p_tile_u32 + (g * 16 + 2 * tq + 8) * 2));
-    // O^T += V^T . P^T over the tile's 16 tokens, four 16-dim m-tiles
-#pragma unroll
-    for (int mt = 0; mt < 4; ++mt) {
-      uint32_t a[4];
-      ldsm_x4_trans(swz(vt, v_row, 2 * mt + v_chunk_hi), a);
-      mma_bf16_16x8x16(o[mt], a, bp0, bp1);
-    }
-    __syncwarp();  // P tile and K/V stage reads done before the next tile reuses them
-    if (lane == 0) mbar_arrive(&hdr.empty[s]);
-    ++u;
+      const uint32_t kt = smem_u32(s_kv + (size_t)s * stage_elems + warp * TILE);
+      const uint32_t vt = kt + hpc * TILE * sizeof(T);
+      // the rows this unit's block belongs to (every row without row tables)
+      const bool row_on[2] = {col_on[0] && ((mask >> (2 * tq)) & 1u), col_on[1] && ((mask >> (2 * tq + 1)) & 1u)};
+      tc_consume_tile(kt, vt, bq, row_on, tok0, vis_c, p.scale_log2, p_tile, p_tile_u32, ln, acc);
+      __syncwarp();  // P tile and K/V stage reads done before the next tile reuses them
+      if (lane == 0) mbar_arrive(&hdr.empty[s]);
+      ++u;
     }
   }
   __syncthreads();
   if (aborted || *reinterpret_cast<volatile int*>(&hdr.abort)) return;
-
-  // l partial sums over the 8 row-group lanes that share each query column
-#pragma unroll
-  for (int e = 0; e < 2; ++e)
-#pragma unroll
-    for (int off = 4; off < 32; off <<= 1) l[e] += __shfl_xor_sync(0xffffffffu, l[e], off);
+  acc.reduce_l();
 
   const int S = p.num_splits;
   if (n_splits <= 1) {
 #pragma unroll
-    for (int e = 0; e < 2; ++e) {
-      if (!col_on[e]) continue;
-      const int row = q0 + 2 * tq + e;
-      const float inv = l[e] > 0.f ? 1.f / l[e] : 0.f;
-      T* dst = static_cast<T*>(p.out) + (int64_t)row * p.out_stride + h * D;
-#pragma unroll
-      for (int mt = 0; mt < 4; ++mt) {
-        dst[16 * mt + g] = __float2bfloat16_rn(o[mt][e] * inv);
-        dst[16 * mt + g + 8] = __float2bfloat16_rn(o[mt][e + 2] * inv);
-      }
-    }
+    for (int e = 0; e < 2; ++e)
+      if (col_on[e])
+        acc.store_output(e, static_cast<T*>(p.out) + (int64_t)(q0 + 2 * tq + e) * p.out_stride + h * D, ln);
     return;
   }
 #pragma unroll
   for (int e = 0; e < 2; ++e) {
     if (!col_on[e]) continue;
     const int64_t item = ((int64_t)(q0 + 2 * tq + e) * p.num_heads + h) * S + split;
-    float* dst = p.ws_acc + item * D;
-#pragma unroll
-    for (int mt = 0; mt < 4; ++mt) {
-      dst[16 * mt + g] = o[mt][e];
-      dst[16 * mt + g + 8] = o[mt][e + 2];
-    }
-    if (g == 0) *reinterpret_cast<float2*>(p.ws_ml + item * 2) = make_float2(m[e], l[e]);
+    acc.store_partial(e, p.ws_acc + item * D, p.ws_ml + item * 2, ln);
   }
   if (p.ws_arrivals == nullptr) return;  // the combine launch merges
   consumer_barrier(hpc);

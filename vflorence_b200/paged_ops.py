@@ -149,6 +149,21 @@ def get_scheduler_metadata(num_reqs: int, num_heads: int, num_kv_heads: int, hea
     return meta
 
 
+SCHEDULE_ITEMS = 0     # one CTA per (request, head group, query chunk, split)
+SCHEDULE_BALANCED = 1  # one persistent wave; equal runs of 16-token tiles per CTA
+
+
+def set_schedule(metadata: torch.Tensor, schedule: int, min_tiles: int = 0) -> torch.Tensor:
+    """Re-plan ``metadata`` (in place) for ``SCHEDULE_ITEMS`` or ``SCHEDULE_BALANCED`` (at least
+    ``min_tiles`` 16-token tiles per CTA; 0: the default); returns it. ``ValueError`` when the
+    plan cannot take that schedule."""
+    plan = plan_of(metadata)
+    st = N.lib().vfl_plan_attention_schedule(ctypes.byref(plan), int(schedule), int(min_tiles))
+    if st != N.VFL_OK:
+        raise ValueError(f"vflorence_b200: {N.last_error()}")
+    return metadata
+
+
 def plan_of(metadata: torch.Tensor) -> N.AttentionPlan:
     """View the plan struct stored in a metadata tensor (no copy; the view keeps the tensor's
     memory alive, so ``plan_of(get_scheduler_metadata(...))`` is safe)."""
