@@ -64,6 +64,17 @@ __device__ __forceinline__ void report(unsigned int* err, unsigned int bits) {
   if (err != nullptr) atomicOr(err, bits);
 }
 
+// Programmatic dependent launch. The grid launched next on the stream as this grid's
+// programmatic dependent may start once every CTA here has called launch_dependents (or
+// exited); griddepcontrol.wait in the dependent blocks until this grid has completed and its
+// memory operations are visible. A grid launched without the attribute waits as usual, and
+// griddepcontrol.wait then returns at once.
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 __device__ __forceinline__ unsigned int load_volatile(const unsigned int* p) {
   unsigned int v;
   asm volatile("ld.volatile.global.u32 %0, [%1];" : "=r"(v) : "l"(p));

@@ -85,12 +85,6 @@ __device__ __forceinline__ bool balanced_piece_appends(const AttnParams& p, int 
   return p.new_k != nullptr && hi >= 0 && hi >= pc.t_lo * 16 && lo < pc.t_hi * 16;
 }
 
-__device__ __forceinline__ void griddep_launch_dependents() {
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-}
-
-__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-
 __global__ void __launch_bounds__(160, 3) paged_attention_tc_balanced_kernel(const AttnParams p,
                                                                               const __grid_constant__ CUtensorMap kmap,
                                                                               const __grid_constant__ CUtensorMap vmap) {

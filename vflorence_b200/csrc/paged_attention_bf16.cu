@@ -24,18 +24,10 @@ int launch_paged_attention_tc(const AttnParams& p, const CUtensorMap& kmap, cons
     if (st) return st;
     // the merge of cut items as a programmatic dependent launch: its CTAs start while the
     // attention grid drains and wait for it (griddepcontrol.wait) before reading the pieces
-    cudaLaunchConfig_t cfg{};
-    cfg.gridDim = dim3(static_cast<unsigned>(p.num_reqs * (p.num_heads / p.heads_per_cta)));
-    cfg.blockDim = dim3(static_cast<unsigned>(32 * p.heads_per_cta));
-    cfg.dynamicSmemBytes = 0;
-    cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    return cuda_status(cudaLaunchKernelEx(&cfg, paged_attention_tc_balanced_combine_kernel, p),
-                       "paged_attention (balanced) merge launch");
+    return launch_dependent(paged_attention_tc_balanced_combine_kernel,
+                            dim3(static_cast<unsigned>(p.num_reqs * (p.num_heads / p.heads_per_cta))),
+                            dim3(static_cast<unsigned>(32 * p.heads_per_cta)), stream,
+                            "paged_attention (balanced) merge launch", p);
   }
   int st = ensure_smem_attribute(reinterpret_cast<const void*>(paged_attention_tc_kernel), want, smem_done);
   if (st) return st;
@@ -43,8 +35,8 @@ int launch_paged_attention_tc(const AttnParams& p, const CUtensorMap& kmap, cons
   st = cuda_status(cudaGetLastError(), "paged_attention (tensor cores) launch");
   if (st || p.num_splits <= 1 || p.ws_arrivals != nullptr) return st;
   const int64_t warps = (int64_t)p.total_q * p.num_heads;
-  paged_attention_combine_kernel<__nv_bfloat16, 64>
-      <<<static_cast<int>(ceil_div(warps, (int64_t)4)), 128, 0, stream>>>(p);
-  return cuda_status(cudaGetLastError(), "paged_attention combine launch");
+  return launch_dependent(paged_attention_combine_kernel<__nv_bfloat16, 64>,
+                          dim3(static_cast<unsigned>(ceil_div(warps, (int64_t)4))), dim3(128), stream,
+                          "paged_attention combine launch", p);
 }
 }  // namespace vfl

@@ -299,6 +299,7 @@ __global__ void __launch_bounds__(160, QPC == 1 ? 3 : 2) paged_attention_kernel(
         }
         issued = i + 1;
       }
+      griddep_launch_dependents();  // the combine launch may start; it waits for the grid
     }
     __syncwarp();
     __syncthreads();  // pairs with the consumers' barrier below
@@ -527,7 +528,26 @@ __global__ void __launch_bounds__(128) paged_attention_combine_kernel(const Attn
   L = max(L, 0);
   const int n_splits = ceil_div(ceil_div(L, p.block_size), p.blocks_per_split);
   if (n_splits <= 1) return;  // written directly by the main kernel
+  griddep_wait();             // launched as the attention grid's programmatic dependent
   merge_splits<T, D>(p, row, h, n_splits, lane);
+}
+
+// Launches `kernel` as the programmatic dependent of the grid launched before it on `stream`:
+// its CTAs may start while that grid drains, and wait for it with griddepcontrol.wait.
+template <typename... Params, typename... Args>
+int launch_dependent(void (*kernel)(Params...), dim3 grid, dim3 block, cudaStream_t stream, const char* what,
+                     Args... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cuda_status(cudaLaunchKernelEx(&cfg, kernel, args...), what);
 }
 
 // Tensor-core variant (paged_attention_tc.cuh): bf16, head_dim 64, up to kTcRows rows per CTA.
@@ -579,8 +599,8 @@ int launch_one(const AttnParams& p, dim3 grid, int threads, int smem_bytes, cuda
   st = cuda_status(cudaGetLastError(), "paged_attention launch");
   if (st || p.num_splits <= 1 || p.ws_arrivals != nullptr) return st;
   const int64_t warps = (int64_t)p.total_q * p.num_heads;
-  paged_attention_combine_kernel<T, D><<<static_cast<int>(ceil_div(warps, (int64_t)4)), 128, 0, stream>>>(p);
-  return cuda_status(cudaGetLastError(), "paged_attention combine launch");
+  return launch_dependent(paged_attention_combine_kernel<T, D>, dim3(static_cast<unsigned>(ceil_div(warps, (int64_t)4))),
+                          dim3(128), stream, "paged_attention combine launch", p);
 }
 
 template <typename T, int D>

@@ -419,6 +419,7 @@ __global__ void __launch_bounds__(160, 3) paged_attention_tc_kernel(const AttnPa
           issued = ++u;
         }
       }
+      griddep_launch_dependents();  // the combine launch may start; it waits for the grid
     }
     __syncwarp();
     __syncthreads();
