@@ -632,12 +632,12 @@ def run_schedule_sweep(args):
     peak, _ = load_peaks()
     shapes = []
     for rpr in (1, 3, 4):
-        for R in (8, 32, 85, 128, 256, 512):
+        for R in (8, 32, 85, 128, 256, 512, 1024):
             if rpr > 1 and R > 256:
                 continue
             for ctx in (128, 592, 1024, 2048, 4096):
                 for skew in (False, True):
-                    if not (skew and ctx < 1024) and R * ctx <= 512 * 2048:
+                    if not (skew and ctx < 1024) and (R * ctx <= 512 * 2048 or (R == 1024 and skew)):
                         shapes.append((rpr, R, ctx, skew))
     if args.sweep_shapes:
         keep = {tuple(int(x) for x in s.split("x")) for s in args.sweep_shapes.split(",")}

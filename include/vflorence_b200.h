@@ -59,7 +59,8 @@ typedef enum vfl_dtype {
 
 /* How a plan spreads the work over CTAs.
  * VFL_SCHEDULE_ITEMS: one CTA per (request, head group, query chunk, split-K range).
- * VFL_SCHEDULE_BALANCED (tensor-core kernel, at most 8 query rows per request, no row tables):
+ * VFL_SCHEDULE_BALANCED (tensor-core kernel, at most 8 query rows per request and 2048
+ *   requests, no row tables):
  *   one persistent wave of num_splits CTAs; the (request, head group) items' 16-token tiles
  *   are laid end to end and each CTA takes an equal run of them, cutting items where the runs
  *   end; a second launch merges the pieces of cut items. Chosen for calls that would fill the
@@ -153,8 +154,9 @@ int vfl_plan_attention_row_tables(int num_reqs, int num_heads, int num_kv_heads,
 /* (new: no reference counterpart - vllm_cpu_attn's metadata is opaque.) Re-plans `plan` (from
  * vfl_plan_attention) for the given vfl_attention_schedule: VFL_SCHEDULE_ITEMS, or
  * VFL_SCHEDULE_BALANCED with at least min_tiles 16-token tiles per CTA (0: the default).
- * Updates workspace_bytes. VFL_ERR_UNSUPPORTED when the plan cannot be balanced (not the
- * tensor-core kernel, row tables, more than 8 query rows per request or 512 requests). */
+ * Updates workspace_bytes; keeps the plan's stage count (the planner gives balanced plans two).
+ * VFL_ERR_UNSUPPORTED when the plan cannot be balanced (not the
+ * tensor-core kernel, row tables, more than 8 query rows per request or 2048 requests). */
 int vfl_plan_attention_schedule(vfl_attention_plan* plan, int schedule, int min_tiles);
 
 /* replaces vllm_cpu_attn.reshape_and_cache(key, value, k_cache, v_cache, slot_mapping, isa=)

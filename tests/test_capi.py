@@ -92,24 +92,57 @@ def _plan(lens, qsl=None, heads=16, d=64, bs=16, dtype=torch.bfloat16, causal=Fa
 
 
 def test_plan_large_batch_splits_long_requests(native):
+    from vflorence_b200 import paged_ops as ops
+
     g = torch.Generator().manual_seed(2)
     lens = torch.randint(1, 4097, (1024,), generator=g).tolist()
     p = _plan(lens)
-    assert (p.heads_per_cta, p.queries_per_cta, p.stages) == (4, 8, 4)   # bf16 x 64: tensor cores
-    assert p.blocks_per_split == 64                # only the table slice (64 blocks) splits them
+    assert (p.heads_per_cta, p.queries_per_cta) == (4, 8)   # bf16 x 64: tensor cores
+    assert p.blocks_per_split == 64                # only the table slice (64 blocks) splits the grid
     assert p.num_splits == -(-max(lens) // 1024)
-    assert p.workspace_bytes >= 1024 * 16 * p.num_splits * (64 + 2) * 4
     assert p.total_q == 1024 and p.max_seq_len == max(lens)
     assert p.merge_in_kernel == 0          # bandwidth-bound: separate combine launch
+    # skewed lengths over many waves of that grid: the balanced wave, with two stages
+    assert (p.schedule, p.stages, p.balanced_ctas, p.min_tiles) == (ops.SCHEDULE_BALANCED, 2, 148 * 3, 8)
+    recs = 148 * 3 * 2 * 4 * 8
+    assert p.workspace_bytes == _r256(recs * 64 * 4) + _r256(recs * 2 * 4) + _r256(1024 * 4 * 16)
+
+
+def test_plan_schedule_rule(native):
+    """The item grid where it runs in at most one wave, where items are short, and for
+    near-uniform lengths it runs unsplit over four waves or more; the balanced wave otherwise."""
+    from vflorence_b200 import paged_ops as ops
+
+    g = torch.Generator().manual_seed(3)
+    beams = lambda n, k: [min(k * r, k * n) for r in range(n + 1)]  # noqa: E731
+    items = ops.SCHEDULE_ITEMS
+    bal = ops.SCHEDULE_BALANCED
+    cases = [
+        (_plan([592] * 85, qsl=beams(85, 3)), items),          # the cfg-4 cross-attention wave: 0.77 waves
+        (_plan([1024] * 32, qsl=beams(32, 4)), items),         # cfg 2: split 3 ways, 0.86 waves
+        (_plan([128] * 256), items),                           # short items
+        (_plan([592] * 1024), items),                          # near-uniform, unsplit, 9 waves
+        (_plan([592] * 128), bal),                             # 2.3 waves
+        (_plan(torch.randint(1, 2049, (32,), generator=g).tolist()), bal),  # skewed, split grid
+        (_plan(torch.randint(1, 1025, (1024,), generator=g).tolist()), bal),  # skewed, 9 waves
+        (_plan([577] * 200, heads=16, dtype=torch.float32), items),  # CUDA-core kernel: grid only
+        (_plan([4096] * 32, d=128), items),
+    ]
+    for i, (p, want) in enumerate(cases):
+        assert p.schedule == want, i
 
 
 def test_plan_merges_splits_in_a_separate_launch(native):
     """Split partials always merge in a separate combine launch (measured faster than the
     in-kernel last-arriver merge in 1214 of 1220 swept cases); the workspace holds only the
     partials, no arrival counters."""
+    from vflorence_b200 import paged_ops as ops
+
     g = torch.Generator().manual_seed(2)
     for n in (8, 256):
-        p = _plan(torch.randint(1, 4097, (n,), generator=g).tolist())
+        lens = torch.randint(1, 4097, (n,), generator=g).to(torch.int32)
+        meta = ops.get_scheduler_metadata(n, 16, 16, 64, lens, torch.bfloat16, None, False, "sm100", 16)
+        p = ops.plan_of(ops.set_schedule(meta, ops.SCHEDULE_ITEMS))  # the item grid of the same call
         assert p.num_splits > 1 and p.merge_in_kernel == 0
         items = p.total_q * 16 * p.num_splits
         r256 = lambda x: -(-x // 256) * 256  # noqa: E731
@@ -218,7 +251,7 @@ def test_plan_balanced_schedule_refused_where_not_built(native):
         qsl = torch.arange(0, n * rows + 1, rows, dtype=torch.int32)
         return ops.get_scheduler_metadata(n, 16, 16, d, lens, dtype, qsl, False, "sm100", 16, row_tables=row_tables)
 
-    for m in (meta(dtype=torch.float32), meta(d=128), meta(rows=9), meta(n=513), meta(rows=2, row_tables=True)):
+    for m in (meta(dtype=torch.float32), meta(d=128), meta(rows=9), meta(n=2049), meta(rows=2, row_tables=True)):
         with pytest.raises(ValueError, match="balanced"):
             ops.set_schedule(m, ops.SCHEDULE_BALANCED)
         assert ops.plan_of(m).schedule == ops.SCHEDULE_ITEMS
@@ -226,8 +259,8 @@ def test_plan_balanced_schedule_refused_where_not_built(native):
         ops.set_schedule(meta(), 2)
     with pytest.raises(ValueError, match="min_tiles"):
         ops.set_schedule(meta(), ops.SCHEDULE_BALANCED, -1)
-    assert ops.plan_of(meta(n=512)).num_reqs == 512
-    ops.set_schedule(meta(n=512), ops.SCHEDULE_BALANCED)  # the most requests it takes
+    big = ops.set_schedule(meta(n=2048), ops.SCHEDULE_BALANCED)  # the most requests it takes
+    assert ops.plan_of(big).num_reqs == 2048 and ops.plan_of(big).balanced_ctas >= 148
 
 
 @pytest.mark.parametrize("field,value", [("schedule", 2), ("min_tiles", 0), ("balanced_ctas", 0),

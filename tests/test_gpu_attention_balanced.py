@@ -50,7 +50,7 @@ def balanced_meta(lens, qsl, heads, block_size, causal=False, min_tiles=0):
     (16, 1, 16, 16, 1000, 2000, 1, False, 8),   # one-tile runs allowed: every CTA of the wave
     (16, 4, 16, 16, 1000, 2000, 64, False, 9),  # long runs: fewer CTAs, whole items
     (12, 8, 16, 16, 8, 600, 0, True, 10),       # causal rows, up to 8 per request
-    (512, 1, 16, 16, 1, 200, 0, False, 11),     # the most requests the schedule takes
+    (2048, 1, 16, 16, 1, 200, 0, False, 11),    # the most requests the schedule takes
     (1, 1, 16, 16, 3000, 3000, 0, False, 12),   # one request over the whole wave
 ])
 def test_balanced_matches_oracle(oracle_lib, requests, rows, heads, block_size, min_len, max_len, min_tiles,

@@ -158,12 +158,26 @@ int set_schedule(vfl_attention_plan* plan, int schedule, int min_tiles) {
 }
 
 // Whether the balanced schedule beats the item grid for a plan (rule fitted below).
-bool balanced_pays_off(const vfl_attention_plan* plan, int64_t base_items, int64_t slots, bool skewed) {
-  (void)plan;
-  (void)base_items;
-  (void)slots;
-  (void)skewed;
-  return false;
+// Whether the balanced schedule beats the item grid: `work` 16-token tiles over `items`
+// (request, head group) items, which the grid runs as `grid_ctas` CTAs (`splits` split-K
+// pieces of the longest request). Fitted to device time on B200 with L2 flushed (bf16, 16 heads
+// x 64, block 16; 8-1024 requests x 1, 3 or 4 rows x 128-4096 tokens, near-uniform U[3/4 ctx,
+// ctx] and skewed U[1, ctx] lengths; 132 shapes):
+//   * a grid of at most one wave (148 SMs x 3 CTAs) runs all its CTAs at once and pays no
+//     pieces to merge: the grid wins or ties (the balanced wave: 0.65-1.06 x);
+//   * items of fewer than 16 tiles on average: the balanced wave's fixed cost (the length scan,
+//     the merge launch) outweighs its gain (0.89-1.05 x);
+//   * near-uniform lengths that the grid runs unsplit in four waves or more are already even
+//     (0.986-1.0 x);
+//   * otherwise the balanced wave wins, by 0.997-1.38 x (1.04 x at 1024 requests of U[1, 4096]
+//     tokens; most where lengths are skewed, or a split grid lands between whole waves).
+bool balanced_pays_off(const vfl_attention_plan* plan, int64_t work, int64_t items, int64_t grid_ctas, int64_t splits,
+                       bool skewed) {
+  if (!balanced_supported(plan) || items <= 0) return false;
+  const int64_t wave = (int64_t)kNumSMs * kBalancedCtasPerSM;
+  if (grid_ctas <= wave || work < 16 * items) return false;
+  if (!skewed && splits == 1 && grid_ctas >= 4 * wave) return false;
+  return true;
 }
 
 // A plan is caller memory: every constraint the kernels rely on (shared-memory table slice,
@@ -392,8 +406,19 @@ int vfl_plan_attention(int num_reqs, int num_heads, int num_kv_heads, int head_d
   plan->merge_in_kernel = merge_in_kernel;
   plan->row_tables = 0;
   set_schedule(plan, VFL_SCHEDULE_ITEMS, 0);  // sets workspace_bytes
-  if (balanced_pays_off(plan, base_items, slots, skewed) && set_schedule(plan, VFL_SCHEDULE_BALANCED, 0) != VFL_OK)
-    set_schedule(plan, VFL_SCHEDULE_ITEMS, 0);
+  int64_t work = 0;  // 16-token tiles of all (request, head group) items
+  for (int r = 0; r < num_reqs; ++r) {
+    const int64_t ql = query_start_loc_host ? (int64_t)query_start_loc_host[r + 1] - query_start_loc_host[r] : 1;
+    if (ql > 0) work += ceil_div((int64_t)seq_lens_host[r], (int64_t)16) * groups;
+  }
+  if (balanced_pays_off(plan, work, base_items, split_items_of(bps), splits, skewed)) {
+    const int item_stages = plan->stages;
+    plan->stages = 2;  // measured: two stages beat four in the balanced wave at every winning shape
+    if (set_schedule(plan, VFL_SCHEDULE_BALANCED, 0) != VFL_OK) {
+      plan->stages = item_stages;
+      set_schedule(plan, VFL_SCHEDULE_ITEMS, 0);
+    }
+  }
   return VFL_OK;
 }
 
@@ -489,6 +514,7 @@ int attention_run(const vfl_attention_plan* plan, const void* query, int64_t que
   p.schedule = plan->schedule;
   p.min_tiles = plan->min_tiles;
   p.balanced_ctas = plan->balanced_ctas;
+  p.max_q_len = plan->max_q_len;
   p.scale_log2 = scale * 1.4426950408889634f;
   if (append != nullptr) {
     p.new_k = append->key;

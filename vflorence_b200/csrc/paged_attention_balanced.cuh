@@ -414,18 +414,20 @@ __global__ void __launch_bounds__(160, 3) paged_attention_tc_balanced_kernel(con
   __syncthreads();  // pairs with the producer's barrier (abort bookkeeping)
 }
 
-// Merges the pieces of the items the balanced kernel cut: one CTA per item (request, head
-// group), one warp per head. Pieces in run order, fixed-order sums. Waits for the attention
-// grid with griddepcontrol.wait (launched as its programmatic dependent).
+// Merges the pieces of the items the balanced kernel cut: CTA (item, query row j), one warp per
+// head of the item's head group. Each piece's (m, l) and the first kPre pieces' partial outputs
+// load in one round, then fixed-order sums. Waits for the attention grid with
+// griddepcontrol.wait (launched as its programmatic dependent).
 __global__ void __launch_bounds__(128) paged_attention_tc_balanced_combine_kernel(const AttnParams p) {
   constexpr int D = 64;
+  constexpr int kPre = 8;
   const int hpc = p.heads_per_cta;
   const int G = p.num_heads / hpc;
-  const int r = blockIdx.x / G, g = blockIdx.x - r * G;
+  const int r = blockIdx.x / G, g = blockIdx.x - r * G, j = blockIdx.y;
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int qb = __ldg(p.qsl + r), qe = __ldg(p.qsl + r + 1);  // inputs: read before the wait
   griddep_wait();
-  if (w >= hpc || qb < 0 || qe < qb || qe > p.total_q || qe - qb > kTcRows) return;
+  if (w >= hpc || qb < 0 || qe < qb || qe > p.total_q || qe - qb > kTcRows || j >= qe - qb) return;
   // An attention grid that gave up (a timeout in the error word) wrote no directory, or part of
   // one: nothing to merge. No entry may send the reads outside the records of the grid's CTAs.
   if (load_volatile(p.err) & VFL_DEVERR_TIMEOUT) return;
@@ -437,46 +439,64 @@ __global__ void __launch_bounds__(128) paged_attention_tc_balanced_combine_kerne
     return;
   }
   const int h = g * hpc + w;
-  // piece i's record of row j: CTA d.x + i, slot d.y for the first piece and 0 after it
-  const int64_t first = balanced_record(d.x, d.y, w, 0, hpc);
+  // piece i's record: CTA d.x + i, slot d.y for the first piece and 0 after it
+  const int64_t first = balanced_record(d.x, d.y, w, j, hpc);
+  const int64_t second = balanced_record((int64_t)d.x + 1, 0, w, j, hpc);
   const int64_t stride = balanced_record(1, 0, 0, 0, hpc);  // one CTA further, slot 0
-  const int64_t second = balanced_record((int64_t)d.x + 1, 0, w, 0, hpc);
-  for (int j = 0; j < qe - qb; ++j) {
-    float M = -INFINITY;
-    for (int i = lane; i < pieces; i += 32) {
-      const int64_t rec = (i == 0 ? first : second + (i - 1) * stride) + j;
-      M = fmaxf(M, __ldcg(p.ws_ml + rec * 2));
-    }
+  auto rec = [&](int i) { return i == 0 ? first : second + (i - 1) * stride; };
+  const float2* ml = reinterpret_cast<const float2*>(p.ws_ml);
+  float2 own = make_float2(-INFINITY, 0.f);  // piece `lane`
+  if (lane < pieces) own = __ldcg(ml + rec(lane));
+  float pre0[kPre], pre1[kPre];
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-    float a0 = 0.f, a1 = 0.f, lsum = 0.f;
-    if (M != -INFINITY) {
-      for (int i0 = 0; i0 < pieces; i0 += 32) {
-        float wt = 0.f;
-        if (i0 + lane < pieces) {
-          const int i = i0 + lane;
-          const int64_t rec = (i == 0 ? first : second + (i - 1) * stride) + j;
-          const float2 ml = __ldcg(reinterpret_cast<const float2*>(p.ws_ml) + rec);
-          wt = exp2f(ml.x - M);
-          lsum = fmaf(wt, ml.y, lsum);
-        }
-        const int n = min(32, pieces - i0);
-        for (int k = 0; k < n; ++k) {
+  for (int k = 0; k < kPre; ++k) {
+    pre0[k] = pre1[k] = 0.f;
+    if (k < pieces) {
+      const float* src = p.ws_acc + rec(k) * D;
+      pre0[k] = __ldcg(src + lane);
+      pre1[k] = __ldcg(src + lane + 32);
+    }
+  }
+  float M = own.x;
+  for (int i = lane + 32; i < pieces; i += 32) M = fmaxf(M, __ldcg(ml + rec(i)).x);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+  float o0 = 0.f, o1 = 0.f, lsum = 0.f;
+  if (M != -INFINITY) {
+    for (int i0 = 0; i0 < pieces; i0 += 32) {
+      float wt = 0.f;
+      if (i0 + lane < pieces) {
+        const float2 v = i0 == 0 ? own : __ldcg(ml + rec(i0 + lane));
+        wt = exp2f(v.x - M);
+        lsum = fmaf(wt, v.y, lsum);
+      }
+      const int n = min(32, pieces - i0);
+      int k0 = 0;
+      if (i0 == 0) {
+#pragma unroll
+        for (int k = 0; k < kPre; ++k) {
           const float wk = __shfl_sync(0xffffffffu, wt, k);
-          const int i = i0 + k;
-          const float* src = p.ws_acc + ((i == 0 ? first : second + (i - 1) * stride) + j) * D;
-          a0 = fmaf(wk, __ldcg(src + lane), a0);
-          a1 = fmaf(wk, __ldcg(src + lane + 32), a1);
+          if (k < n) {
+            o0 = fmaf(wk, pre0[k], o0);
+            o1 = fmaf(wk, pre1[k], o1);
+          }
         }
+        k0 = kPre;
+      }
+      for (int k = k0; k < n; ++k) {
+        const float wk = __shfl_sync(0xffffffffu, wt, k);
+        const float* src = p.ws_acc + rec(i0 + k) * D;
+        o0 = fmaf(wk, __ldcg(src + lane), o0);
+        o1 = fmaf(wk, __ldcg(src + lane + 32), o1);
       }
     }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) lsum += __shfl_xor_sync(0xffffffffu, lsum, o);
-    const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
-    __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.out) + (int64_t)(qb + j) * p.out_stride + h * D;
-    out[lane] = __float2bfloat16_rn(a0 * inv);
-    out[lane + 32] = __float2bfloat16_rn(a1 * inv);
   }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) lsum += __shfl_xor_sync(0xffffffffu, lsum, o);
+  const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
+  __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.out) + (int64_t)(qb + j) * p.out_stride + h * D;
+  out[lane] = __float2bfloat16_rn(o0 * inv);
+  out[lane + 32] = __float2bfloat16_rn(o1 * inv);
 }
 
 }  // namespace vfl

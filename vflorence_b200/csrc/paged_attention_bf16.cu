@@ -25,7 +25,8 @@ int launch_paged_attention_tc(const AttnParams& p, const CUtensorMap& kmap, cons
     // the merge of cut items as a programmatic dependent launch: its CTAs start while the
     // attention grid drains and wait for it (griddepcontrol.wait) before reading the pieces
     return launch_dependent(paged_attention_tc_balanced_combine_kernel,
-                            dim3(static_cast<unsigned>(p.num_reqs * (p.num_heads / p.heads_per_cta))),
+                            dim3(static_cast<unsigned>(p.num_reqs * (p.num_heads / p.heads_per_cta)),
+                                 static_cast<unsigned>(p.max_q_len < 1 ? 1 : p.max_q_len)),
                             dim3(static_cast<unsigned>(32 * p.heads_per_cta)), stream,
                             "paged_attention (balanced) merge launch", p);
   }

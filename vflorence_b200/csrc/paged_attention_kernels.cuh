@@ -56,6 +56,7 @@ struct AttnParams {
   int32_t schedule;     // VFL_SCHEDULE_ITEMS or VFL_SCHEDULE_BALANCED (tensor-core kernel only)
   int32_t min_tiles;    // balanced: fewest 16-token tiles a CTA takes
   int32_t balanced_ctas;  // balanced: CTAs of the grid (partial records in the workspace)
+  int32_t max_q_len;      // balanced: most query rows of a request (rows of the merge grid)
   float scale_log2;  // softmax scale * log2(e)
   float* ws_acc;     // [total_q, H, num_splits, D]
   float* ws_ml;      // [total_q, H, num_splits, 2]
@@ -555,7 +556,7 @@ constexpr int kTcHeaderBytes = 4096;  // SmemHeader | one 8x16 bf16 P tile per c
 constexpr int kTcRows = 8;            // query rows per CTA (the mma N dimension)
 
 // Balanced schedule (paged_attention_balanced.cuh).
-constexpr int kBalancedMaxReqs = 512;   // requests whose lengths and rows fit in shared memory
+constexpr int kBalancedMaxReqs = 2048;  // requests whose lengths and rows fit in shared memory
 constexpr int kBalancedMaxLen = 1 << 27;  // lengths packed with the row count into 32 bits
 constexpr int kBalancedCtasPerSM = 3;   // the kernel's launch bounds (registers)
 constexpr int kBalancedMinTiles = 8;    // default fewest 16-token tiles per CTA
