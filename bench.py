@@ -55,6 +55,29 @@ def load_peaks():
         return 6650.0, "fallback"
 
 
+def _kernel_of(plan):
+    """The attention kernel a plan launches."""
+    if plan.schedule == 1:
+        return "paged_attention_tc_balanced_kernel"
+    return "paged_attention_tc_kernel" if plan.queries_per_cta == 8 else "paged_attention_kernel"
+
+
+def _launches_of(plan):
+    """Kernel launches of one attention call: the balanced wave and its merge, or the grid and
+    its combine when the grid splits."""
+    return 2 if plan.schedule == 1 else 1 + (plan.num_splits > 1)
+
+
+def _plan_desc(plan):
+    """The launch-shape fields of a plan, for the JSON lines."""
+    d = {"kernel": _kernel_of(plan), "heads_per_cta": plan.heads_per_cta, "stages": plan.stages}
+    if plan.schedule == 1:
+        d.update(schedule="balanced", ctas=plan.balanced_ctas, min_tiles=plan.min_tiles)
+    else:
+        d.update(schedule="items", splits=plan.num_splits, blocks_per_split=plan.blocks_per_split)
+    return d
+
+
 def load_traffic():
     """dram bytes per algorithmic byte of the self-attention kernel, from the committed ncu
     summary (profiles/paged_decode_traffic.json), if one exists."""
@@ -125,7 +148,7 @@ class Step:
         self.out = torch.empty_like(w["q"])
         self.out_c = torch.empty_like(w["qc"])
         plan_s, plan_c = ops.plan_of(self.meta_self), ops.plan_of(self.meta_cross)
-        self.launches = 1 + (1 + (plan_s.num_splits > 1)) + (1 + (plan_c.num_splits > 1))
+        self.launches = 1 + _launches_of(plan_s) + _launches_of(plan_c)  # append + self + cross
         self.plans = (plan_s, plan_c)
 
     def append(self, k_new, v_new, slots):
@@ -436,7 +459,7 @@ def run_sweep(args):
         plan = ops.plan_of(meta)
         print(json.dumps({"point": "self", "batch": B, "ctx": "U[1,4096]", "us": ms * 1e3,
                           "gbs": nb / ms / 1e6, "frac_of_measured_hbm": nb / ms / 1e6 / peak,
-                          "splits": plan.num_splits, "blocks_per_split": plan.blocks_per_split,
+                          "plan": _plan_desc(plan),
                           "cpu_oracle_gbs": cpu_gbs, "cpu_threads": threads,
                           "cpu_sample_seqs": n}), flush=True)
         del w, kc, vc
@@ -1288,7 +1311,7 @@ def main():
             "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "ms_per_step": e2e_ms / e2e_steps, "steps": e2e_steps, "clocks": clocks_e2e.summary()},
             "gpu_launches": launches,
-            "roofline": {"bound": "hbm", "kernel": "self decode: paged_attention_tc_kernel (bf16, head_dim 64) + combine",
+            "roofline": {"bound": "hbm", "kernel": f"self decode: {_kernel_of(plan_s)} (bf16, head_dim 64) + merge",
                          "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                          "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
                          else "fallback 6650 GB/s", "traffic": traffic,
@@ -1296,9 +1319,7 @@ def main():
             "ops_ms": {"append": t_append, "self_decode": t_self, "cross": t_cross},
             "ops_gbs": {"append": nb["append"] / t_append / 1e6, "self_decode": nb["self"] / t_self / 1e6,
                         "cross": nb["cross"] / t_cross / 1e6},
-            "plans": {"self": {"splits": plan_s.num_splits, "blocks_per_split": plan_s.blocks_per_split,
-                               "heads_per_cta": plan_s.heads_per_cta, "stages": plan_s.stages},
-                      "cross": {"splits": plan_c.num_splits, "blocks_per_split": plan_c.blocks_per_split}},
+            "plans": {"self": _plan_desc(plan_s), "cross": _plan_desc(plan_c)},
             "clocks": clocks.summary(),
             "cpu_baseline": cb,
             "decode": decode,
