@@ -286,10 +286,19 @@ __global__ void __launch_bounds__(160, 3) paged_attention_tc_kernel(const AttnPa
   const int bps = p.blocks_per_split;
 
   // the item's independent reads in one round trip: the error word, its query range, its length
+  // and (producer, one table per request) its split's block-table slice, whatever the length
+  // cuts it to - the slice lies inside the table row, and entries past the length go unused
   const unsigned int err_now = load_volatile(p.err);
   const int q_begin = __ldg(p.qsl + r);
   const int q_end = __ldg(p.qsl + r + 1);
   int L = __ldg(p.seq_lens + r);
+  int slice_lo = 0, slice_hi = 0;  // entries lane and lane + 32 of the slice
+  if (producer && !p.row_tables) {
+    const int avail = min(bps, p.table_cols - split * bps);
+    const int32_t* src = p.table + (int64_t)r * p.table_stride + (int64_t)split * bps;
+    if (lane < avail) slice_lo = __ldg(src + lane);
+    if (lane + 32 < avail) slice_hi = __ldg(src + lane + 32);
+  }
   if (err_now & VFL_DEVERR_TIMEOUT) return;  // an earlier CTA gave up waiting
   if (bps < 1 || bps > kMaxBlocksPerSplit || p.stages < 2 || p.stages > kMaxStages) {  // the host checks the plan too
     if (threadIdx.x == 0) report(p.err, VFL_DEVERR_CONTEXT);
@@ -342,7 +351,7 @@ __global__ void __launch_bounds__(160, 3) paged_attention_tc_kernel(const AttnPa
     for (int e = lane; e < nrows * nb; e += 32) {
       const int j = e / nb, i = e - j * nb;
       const int64_t trow = p.row_tables ? (int64_t)(q0 + j) : (int64_t)r;
-      int b = __ldg(p.table + trow * p.table_stride + blk_begin + i);
+      int b = p.row_tables ? __ldg(p.table + trow * p.table_stride + blk_begin + i) : (e < 32 ? slice_lo : slice_hi);
       if (b < 0 || b >= p.num_blocks) {
         report(p.err, VFL_DEVERR_BLOCK_ID);
         b = 0;
