@@ -102,6 +102,28 @@ def test_no_alloc_in_kernel_merge_counters_start_clean(native):
     assert ops.read_device_errors(DEV) == 0
 
 
+def test_no_alloc_balanced_plans_twice(native):
+    """Balanced plans keep their partial records and item directory in the shared scratch; two
+    calls in a row with other lengths (the second finding the first's directory there) both
+    equal the workspace entry point."""
+    from vflorence_b200 import paged_ops as ops
+
+    for call, (seed, n, lo, hi) in enumerate([(41, 40, 1, 4096), (42, 24, 1500, 2000)]):
+        q, kc, vc, qsl, lens, table = _case(seed, n, lo, hi)
+        meta = ops.get_scheduler_metadata(n, H, H, D, lens, torch.bfloat16, qsl, False, "sm100", BS)
+        plan = ops.plan_of(ops.set_schedule(meta, ops.SCHEDULE_BALANCED))
+        assert 0 < plan.workspace_bytes <= 64 * 1024 * 1024
+        d = dict(qsl=qsl.to(DEV), lens=lens.to(DEV), table=table.to(DEV))
+        ws = torch.empty(plan.workspace_bytes, dtype=torch.uint8, device=DEV)
+        want = _run(native, "vfl_attention_with_kv_cache", plan, q, kc, vc, d["qsl"], d["lens"], d["table"], ws)
+        got = _run(native, "vfl_attention_with_kv_cache_no_alloc", plan, q, kc, vc, d["qsl"], d["lens"],
+                   d["table"])
+        torch.cuda.synchronize()
+        assert torch.isfinite(got).all()
+        assert torch.equal(got, want), f"balanced, no-alloc call {call + 1}"  # same plan, same sums
+    assert ops.read_device_errors(DEV) == 0
+
+
 def test_no_alloc_rejects_plans_beyond_its_scratch(native):
     from vflorence_b200 import _native
     from vflorence_b200 import paged_ops as ops
