@@ -156,7 +156,8 @@ int vfl_plan_attention_row_tables(int num_reqs, int num_heads, int num_kv_heads,
  * VFL_SCHEDULE_BALANCED with at least min_tiles 16-token tiles per CTA (0: the default).
  * Updates workspace_bytes; keeps the plan's stage count (the planner gives balanced plans two).
  * VFL_ERR_UNSUPPORTED when the plan cannot be balanced (not the
- * tensor-core kernel, row tables, more than 8 query rows per request or 2048 requests). */
+ * tensor-core kernel, row tables, more than 8 query rows per request, more than 2048 requests,
+ * or a request of 2^24 tokens or more). */
 int vfl_plan_attention_schedule(vfl_attention_plan* plan, int schedule, int min_tiles);
 
 /* replaces vllm_cpu_attn.reshape_and_cache(key, value, k_cache, v_cache, slot_mapping, isa=)

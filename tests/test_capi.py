@@ -255,6 +255,10 @@ def test_plan_balanced_schedule_refused_where_not_built(native):
         with pytest.raises(ValueError, match="balanced"):
             ops.set_schedule(m, ops.SCHEDULE_BALANCED)
         assert ops.plan_of(m).schedule == ops.SCHEDULE_ITEMS
+    huge = ops.get_scheduler_metadata(2, 16, 16, 64, torch.tensor([1 << 24, 5], dtype=torch.int32), torch.bfloat16,
+                                      None, False, "sm100", 16)  # the tile prefix would leave int32
+    with pytest.raises(ValueError, match="balanced"):
+        ops.set_schedule(huge, ops.SCHEDULE_BALANCED)
     with pytest.raises(ValueError, match="schedule"):
         ops.set_schedule(meta(), 2)
     with pytest.raises(ValueError, match="min_tiles"):

@@ -141,8 +141,8 @@ int set_schedule(vfl_attention_plan* plan, int schedule, int min_tiles) {
   if (!balanced_supported(plan))
     return fail(VFL_ERR_UNSUPPORTED,
                 "attention: the balanced schedule needs bf16 with head_dim 64, one block table per request, "
-                "at most %d query rows per request and %d requests",
-                kTcRows, kBalancedMaxReqs);
+                "at most %d query rows per request, %d requests and %d tokens per request",
+                kTcRows, kBalancedMaxReqs, kBalancedMaxLen - 1);
   if (min_tiles < 0) return fail(VFL_ERR_INVALID_ARGUMENT, "attention: min_tiles %d < 0", min_tiles);
   const int hpc = plan->heads_per_cta;
   const int stage_bytes = 2 * hpc * 16 * plan->head_dim * 2;

@@ -566,7 +566,9 @@ constexpr int kTcRows = 8;            // query rows per CTA (the mma N dimension
 
 // Balanced schedule (paged_attention_balanced.cuh).
 constexpr int kBalancedMaxReqs = 2048;  // requests whose lengths and rows fit in shared memory
-constexpr int kBalancedMaxLen = 1 << 27;  // lengths packed with the row count into 32 bits
+constexpr int kBalancedMaxLen = 1 << 24;  // tokens per request: the int32 tile prefix of 2048
+                                          // requests stays below 2^31 (and lengths pack with
+                                          // the row count into 32 bits)
 constexpr int kBalancedCtasPerSM = 3;   // the kernel's launch bounds (registers)
 constexpr int kBalancedMinTiles = 8;    // default fewest 16-token tiles per CTA
 
