@@ -165,6 +165,39 @@ def test_split_k_long_contexts(oracle_lib, dtype):
                            "split-K")
 
 
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16], ids=["f32", "bf16"])
+def test_split_plan_in_a_cuda_graph_follows_the_lengths(oracle_lib, dtype):
+    """A split item-grid plan captured in a CUDA graph: the combine launch, the grid's programmatic
+    dependent, becomes a programmatic edge of the graph. Replays with other device lengths (some
+    zero, some too short to split) equal the oracle."""
+    o = ops()
+    q, kc, vc, qsl, lens, table = random_case(num_reqs=6, heads=16, head_dim=64, block_size=16, max_len=4096,
+                                              min_len=4096, dtype=dtype, seed=12, on_device=True)
+    meta = o.get_scheduler_metadata(6, 16, 16, 64, lens, dtype, qsl, False, "sm100", 16)
+    plan = o.plan_of(meta)
+    assert plan.schedule == o.SCHEDULE_ITEMS and plan.num_splits > 1
+    dq, dl, dt = qsl.to(DEV), lens.to(DEV), table.to(DEV)
+    out = torch.zeros_like(q)
+    o.attention_with_kv_cache(q, kc, vc, out, dq, dl, 0.125, False, dt, meta)  # warm-up outside capture
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        o.attention_with_kv_cache(q, kc, vc, out, dq, dl, 0.125, False, dt, meta)
+    g = torch.Generator().manual_seed(13)
+    for step in range(3):
+        new = torch.randint(0, 4097, (6,), generator=g, dtype=torch.int32)
+        new[step] = 0
+        new[(step + 1) % 6] = 40
+        dl.copy_(new)
+        out.fill_(float("nan"))
+        graph.replay()
+        torch.cuda.synchronize()
+        assert o.read_device_errors(DEV) == 0
+        want = oracle_attn(oracle_lib, q.cpu(), kc.cpu(), vc.cpu(), qsl, new, table, 0.125)
+        assert_attention_close(out.cpu(), want, dtype, f"graph replay {step}")
+    del graph
+
+
 def test_baseline_sweep_b256_against_oracle(oracle_lib):
     # BASELINE config 5 at batch 256: bf16, 16 heads x 64, block 16, contexts U[1, 4096]
     q, kc, vc, qsl, lens, table = random_case(num_reqs=256, heads=16, head_dim=64, block_size=16,
