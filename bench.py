@@ -709,6 +709,32 @@ def run_schedule_sweep(args):
         del k, v
 
 
+def run_profile_topk(args):
+    """The workload of the candidate-selection capture: three calls of the beam-search selection
+    of a cfg-4 step (ROWS rows x the Florence-2 vocabulary of 51289, bf16 logits, k 6, log-softmax
+    plus each row's cumulative log-prob), L2 flushed before each, checked against torch."""
+    from vflorence_b200 import paged_ops as ops
+
+    rows, vocab, k = args.profile_topk, 51289, 6
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    g = torch.Generator(device=device).manual_seed(0)
+    logits = (torch.randn(rows, vocab, generator=g, device=device) * 3).to(DTYPE)
+    cum = torch.randn(rows, generator=g, device=device)
+    flush = torch.empty(192 * 1024 * 1024, dtype=torch.uint8, device=device)
+    for _ in range(3):
+        flush.zero_()
+        vals, idx = ops.row_topk(logits, k, log_softmax=True, row_offset=cum)
+    torch.cuda.synchronize()
+    want_i = torch.sort(logits.float(), dim=1, descending=True, stable=True).indices[:, :k]
+    want_v = torch.log_softmax(logits.float(), -1).gather(1, want_i) + cum[:, None]
+    if not torch.equal(idx.long(), want_i) or float((vals - want_v).abs().max()) > 2e-5:
+        raise RuntimeError("row_topk differs from torch")
+    call = lambda: ops.row_topk(logits, k, log_softmax=True, row_offset=cum)  # noqa: E731
+    print(json.dumps({"point": "profile_topk", "rows": rows, "vocab": vocab, "k": k,
+                      "us_l2_flushed": round(_time_op(call, 10, flush) * 1e3, 2)}))
+
+
 def run_profile_attn(args):
     """The workload of the attention captures: three calls of paged attention for R requests x
     ROWS query rows (beams sharing one request's pages, as the engine's cross-attention) over LEN
@@ -1108,6 +1134,8 @@ def main():
                     help="one decode step of the config's engine inside a profiler range (for ncu)")
     ap.add_argument("--profile-attn", default=None, metavar="R,ROWS,LEN",
                     help="three paged-attention calls of R requests x ROWS rows over LEN tokens (for ncu)")
+    ap.add_argument("--profile-topk", type=int, default=0, metavar="ROWS",
+                    help="three cfg-4 candidate selections of ROWS rows (for ncu), then their time")
     ap.add_argument("--profile-kv-proj", type=int, default=0, metavar="TOKENS",
                     help="three encoder K/V projection calls at TOKENS tokens (for ncu)")
     ap.add_argument("--decode", choices=["cfg1", "cfg2", "cfg3", "cfg4"], default=None,
@@ -1145,6 +1173,9 @@ def main():
         return
     if args.profile_attn:
         run_profile_attn(args)
+        return
+    if args.profile_topk:
+        run_profile_topk(args)
         return
     if args.decode:
         run_decode(args)
