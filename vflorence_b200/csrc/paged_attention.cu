@@ -373,9 +373,9 @@ int vfl_plan_attention(int num_reqs, int num_heads, int num_kv_heads, int head_d
       return plan_fail(plan, fail(VFL_ERR_UNSUPPORTED, "sequence of %lld tokens is too long", (long long)max_seq));
     splits = ceil_div(max_blocks, bps);
   }
-  // a full wave of short items: two stages per CTA, so twice as many CTAs hide each other's
-  // item prologues (measured 3-11 % faster than four stages for items of up to 256 tokens;
-  // mixed, within 10 % either way, at 577-592 tokens)
+  // a full wave of short items: two stages per CTA (measured 3-11 % faster than four stages for
+  // items of up to 256 tokens; mixed, within 10 % either way, at 577-592 tokens). The CTAs per
+  // SM stay at three either way: the kernel's registers, not its shared memory, set them.
   if (base_items >= slots && bps * block_size <= kShortItemTokens && stages > 2) stages = 2;
   splits = splits < 1 ? 1 : splits;
   const int64_t q_chunks = ceil_div(max_q < 1 ? 1 : max_q, (int64_t)qpc);
