@@ -204,10 +204,10 @@ int vfl_attention_with_kv_cache_append(const vfl_attention_plan* plan, const voi
                                        const int32_t* block_table, int64_t table_stride, int32_t table_cols,
                                        float scale, void* workspace, size_t workspace_bytes, void* stream);
 
-/* 1 when vfl_attention_with_kv_cache_append takes this plan: the tensor-core kernel (bf16,
- * head_dim 64) and one new token per query row - causal with at most 8 rows per request (one
- * CTA holds them all, since each row reads the rows before it), row tables, or one row per
- * request. */
+/* 1 when vfl_attention_with_kv_cache_append takes this plan: one new token per query row, and
+ * either one row per request (every dtype and head_dim), or with the tensor-core kernel (bf16,
+ * head_dim 64) causal rows, at most 8 per request (one CTA holds them all, since each row
+ * reads the rows before it), or row tables. */
 int vfl_attention_append_supported(const vfl_attention_plan* plan);
 
 /* No counterpart in the reference (vllm_cpu_attn allocates on the host heap as it likes).

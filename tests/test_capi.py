@@ -377,10 +377,13 @@ def test_attention_append_host_checks(native):
     # more than 8 causal rows of a request span two CTAs, and later rows read earlier rows' tokens
     assert not ops.attention_append_supported(meta([100, 200], [0, 12, 14], causal=True))
     assert not ops.attention_append_supported(meta([100, 200], [0, 3, 5]))               # rows sharing a table
-    assert not ops.attention_append_supported(meta([100, 200], dtype=torch.float32))     # CUDA-core kernel
-    assert not ops.attention_append_supported(meta([100, 200], d=128))
+    # the CUDA-core kernel (float32, other head dims) appends for one row per request only
+    assert ops.attention_append_supported(meta([100, 200], dtype=torch.float32))
+    assert ops.attention_append_supported(meta([100, 200], d=128))
+    assert not ops.attention_append_supported(meta([100, 200], [0, 3, 5], dtype=torch.float32))
+    assert not ops.attention_append_supported(meta([100, 200], [0, 1, 3], causal=True, d=128))
     fake = ctypes.c_void_p(256)
-    bad = ops.plan_of(meta([100, 200], dtype=torch.float32))
+    bad = ops.plan_of(meta([100, 200], [0, 3, 5], dtype=torch.float32))
     st = native.vfl_attention_with_kv_cache_append(ctypes.byref(bad), fake, 1024, fake, 1024, fake, 1024, fake, fake,
                                                    fake, 100, fake, 1024, fake, fake, fake, 16, 16, 0.125, None, 0,
                                                    None)
@@ -394,6 +397,11 @@ def test_attention_append_host_checks(native):
                                                    1024, fake, fake, fake, 100, fake, 1024, fake, fake, fake, 16, 16,
                                                    0.125, None, 0, None)
     assert st == _native.VFL_ERR_INVALID_ARGUMENT  # a key not 16-byte aligned
+    f32 = ops.plan_of(meta([100, 200], dtype=torch.float32))
+    st = native.vfl_attention_with_kv_cache_append(ctypes.byref(f32), fake, 1024, fake, 1026, fake, 1024, fake,
+                                                   fake, fake, 100, fake, 1024, fake, fake, fake, 16, 16, 0.125, None,
+                                                   0, None)
+    assert st == _native.VFL_ERR_INVALID_ARGUMENT  # a float32 key row stride of 1026 elements: not 16-byte
 
 
 def test_cache_ops_refuse_bad_arguments_before_the_device(native):

@@ -378,12 +378,12 @@ def test_row_tables_refused_where_not_built():
 
 # ------------------------------------------------------------- fused KV append + attention
 
-def _appended_case(kind, seed, block_size, max_len, requests):
+def _appended_case(kind, seed, block_size, max_len, requests, dtype=torch.bfloat16, head_dim=64):
     """Pools, tables and one step's new tokens: every query row appends its newest token into
     a block of its own (after copy-on-write no row shares the block it writes)."""
     g = torch.Generator().manual_seed(seed)
     gd = torch.Generator(device=DEV).manual_seed(seed)
-    H, D = 16, 64
+    H, D = 16, head_dim
     if kind == "beams":
         counts = [int(torch.randint(1, 5, (1,), generator=g)) for _ in range(requests)]
     elif kind == "causal":
@@ -415,7 +415,7 @@ def _appended_case(kind, seed, block_size, max_len, requests):
     pool = nxt + 4
     perm = torch.randperm(pool, generator=g).to(torch.int32)
     table = perm[table.long()]
-    kc = torch.randn(pool, H, block_size, D, generator=gd, device=DEV, dtype=torch.bfloat16)
+    kc = torch.randn(pool, H, block_size, D, generator=gd, device=DEV, dtype=dtype)
     vc = torch.randn_like(kc)
     qsl = torch.tensor([0] + torch.tensor(counts).cumsum(0).tolist(), dtype=torch.int32)
     nq = int(qsl[-1])
@@ -426,23 +426,30 @@ def _appended_case(kind, seed, block_size, max_len, requests):
             trow = j if kind == "beams" else r
             pos = int(lens[r]) - 1 if kind != "causal" else int(lens[r]) - (int(qsl[r + 1]) - j)
             slots[j] = int(table[trow, pos // block_size]) * block_size + pos % block_size
-    fused = torch.randn(nq, 3 * H * D, generator=gd, device=DEV, dtype=torch.bfloat16)  # a q/k/v projection
+    fused = torch.randn(nq, 3 * H * D, generator=gd, device=DEV, dtype=dtype)  # a q/k/v projection
     q, key, value = (x.reshape(nq, H, D) for x in fused.chunk(3, dim=-1))
     return q, key, value, kc, vc, qsl, lens, table, slots
 
 
-@pytest.mark.parametrize("kind,seed,block_size,max_len,requests", [
-    ("rows", 1, 16, 200, 40), ("rows", 2, 16, 4000, 9), ("rows", 3, 32, 1500, 17),
-    ("beams", 4, 16, 300, 30), ("beams", 5, 16, 3000, 6), ("causal", 6, 16, 600, 12), ("causal", 7, 32, 2000, 5)])
-def test_attention_append_equals_append_then_attend(kind, seed, block_size, max_len, requests):
+@pytest.mark.parametrize("kind,seed,block_size,max_len,requests,dtype,head_dim", [
+    ("rows", 1, 16, 200, 40, torch.bfloat16, 64), ("rows", 2, 16, 4000, 9, torch.bfloat16, 64),
+    ("rows", 3, 32, 1500, 17, torch.bfloat16, 64), ("beams", 4, 16, 300, 30, torch.bfloat16, 64),
+    ("beams", 5, 16, 3000, 6, torch.bfloat16, 64), ("causal", 6, 16, 600, 12, torch.bfloat16, 64),
+    ("causal", 7, 32, 2000, 5, torch.bfloat16, 64),
+    # the CUDA-core kernel: float32 (BASELINE cfg 1's decoder), and bf16 at other head dims
+    ("rows", 8, 16, 200, 40, torch.float32, 64), ("rows", 9, 16, 4000, 9, torch.float32, 64),
+    ("rows", 10, 32, 1500, 17, torch.float32, 64), ("rows", 11, 16, 900, 12, torch.bfloat16, 128),
+    ("rows", 12, 16, 700, 7, torch.float32, 32)], ids=lambda v: str(v).replace("torch.", ""))
+def test_attention_append_equals_append_then_attend(kind, seed, block_size, max_len, requests, dtype, head_dim):
     """One launch that stores each row's new K/V and attends over it gives the output and the
     pools of reshape_and_cache followed by attention_with_kv_cache, bit for bit (the same plan
     reads the same bytes); long contexts exercise the split that holds the new position."""
     o = ops()
-    q, key, value, kc, vc, qsl, lens, table, slots = _appended_case(kind, seed, block_size, max_len, requests)
+    q, key, value, kc, vc, qsl, lens, table, slots = _appended_case(kind, seed, block_size, max_len, requests,
+                                                                    dtype, head_dim)
     n, h, bs, d = kc.shape
     causal = kind == "causal"
-    meta = o.get_scheduler_metadata(requests, h, h, d, lens, torch.bfloat16, qsl, causal, "sm100", bs,
+    meta = o.get_scheduler_metadata(requests, h, h, d, lens, dtype, qsl, causal, "sm100", bs,
                                     row_tables=kind == "beams")
     assert o.attention_append_supported(meta)
     dq, dl, dt, ds = qsl.to(DEV), lens.to(DEV), table.to(DEV), slots.to(DEV)
@@ -488,7 +495,10 @@ def test_attention_append_refused_where_not_built():
 
     lens = torch.tensor([10, 20], dtype=torch.int32)
     f32 = o.get_scheduler_metadata(2, 16, 16, 64, lens, torch.float32, None, False, "sm100", 16)
-    assert not o.attention_append_supported(f32)
+    assert o.attention_append_supported(f32)  # one row per request: the CUDA-core kernel appends too
+    f32_grouped = o.get_scheduler_metadata(2, 16, 16, 64, lens, torch.float32, torch.tensor([0, 2, 4], dtype=torch.int32),
+                                           False, "sm100", 16)
+    assert not o.attention_append_supported(f32_grouped)
     # several non-causal rows sharing one table would all write its newest position
     grouped = o.get_scheduler_metadata(2, 16, 16, 64, lens, torch.bfloat16, torch.tensor([0, 2, 4], dtype=torch.int32),
                                        False, "sm100", 16)

@@ -69,8 +69,8 @@ def stage_cross(layers, pages, enc_lens, block_size: int, isa: str):
 def decoder_self_attention(query: torch.Tensor, key: torch.Tensor, value: torch.Tensor,
                            k_cache: torch.Tensor, v_cache: torch.Tensor, scale: float) -> torch.Tensor:
     """Write this step's K/V into the paged cache, then attend over each sequence's cache - in
-    one launch where the plan allows it (the tensor-core kernel stores each row's new K/V ahead
-    of reading its last block), else the append kernel and then the attention."""
+    one launch where the plan allows it (the attention kernel stores each row's new K/V ahead of
+    reading the block that holds it), else the append kernel and then the attention."""
     ctx = get_context()
     out = torch.empty_like(query)
     # causal=False is still causal: each sequence queries only its newest token, and the cache

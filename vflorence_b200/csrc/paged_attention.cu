@@ -588,11 +588,12 @@ int vfl_attention_with_kv_cache(const vfl_attention_plan* plan, const void* quer
 int vfl_attention_append_supported(const vfl_attention_plan* plan) {
   // Causal rows read the new tokens of earlier rows: all of a request's rows must be in one CTA
   // (one query chunk), or another CTA's stores would race this one's reads. Rows with their own
-  // tables (beam groups) and single rows read only their own new token.
-  return plan != nullptr && plan->magic == VFL_PLAN_MAGIC && plan->queries_per_cta == kTcRows &&
-                 (plan->causal ? plan->max_q_len <= kTcRows : (plan->row_tables || plan->max_q_len <= 1))
-             ? 1
-             : 0;
+  // tables (beam groups) and single rows read only their own new token. The CUDA-core kernel
+  // (float32, other head dims) appends for one row per request, the decode step's shape.
+  if (plan == nullptr || plan->magic != VFL_PLAN_MAGIC) return 0;
+  if (plan->queries_per_cta == kTcRows)
+    return (plan->causal ? plan->max_q_len <= kTcRows : (plan->row_tables || plan->max_q_len <= 1)) ? 1 : 0;
+  return plan->queries_per_cta == 1 && plan->max_q_len <= 1 ? 1 : 0;
 }
 
 int vfl_attention_with_kv_cache_append(const vfl_attention_plan* plan, const void* query,
@@ -607,16 +608,17 @@ int vfl_attention_with_kv_cache_append(const vfl_attention_plan* plan, const voi
     return fail(VFL_ERR_INVALID_ARGUMENT, "attention_append: plan missing or not built by vfl_plan_attention");
   if (!vfl_attention_append_supported(plan))
     return fail(VFL_ERR_UNSUPPORTED,
-                "attention_append: built for the tensor-core kernel (bf16, head_dim 64), with one new token per "
-                "query row (at most 8 causal rows per request, row tables, or one row per request)");
+                "attention_append: built for one new token per query row: one row per request, or with the "
+                "tensor-core kernel (bf16, head_dim 64) at most 8 causal rows per request or row tables");
   if (plan->num_reqs == 0 || plan->total_q == 0) return attention_run(plan, query, query_token_stride, k_cache,
       v_cache, num_blocks, output, output_token_stride, query_start_loc, seq_lens, block_table, table_stride,
       table_cols, scale, workspace, workspace_bytes, stream, nullptr);
   const int64_t row = (int64_t)plan->num_heads * plan->head_dim;
   if (!key || !value || !slot_mapping)
     return fail(VFL_ERR_INVALID_ARGUMENT, "attention_append: NULL key, value or slot_mapping");
-  if (!aligned16(key) || !aligned16(value) || (key_token_stride * 2) % 16 != 0 ||
-      (value_token_stride * 2) % 16 != 0 || key_token_stride < row || value_token_stride < row)
+  const int64_t es = (int64_t)dtype_size(plan->dtype);
+  if (!aligned16(key) || !aligned16(value) || (key_token_stride * es) % 16 != 0 ||
+      (value_token_stride * es) % 16 != 0 || key_token_stride < row || value_token_stride < row)
     return fail(VFL_ERR_INVALID_ARGUMENT,
                 "attention_append: key/value must be 16-byte aligned with token strides of at least heads x head_dim");
   const AppendSource src{key, key_token_stride, value, value_token_stride, slot_mapping};

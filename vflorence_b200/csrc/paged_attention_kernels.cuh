@@ -63,9 +63,9 @@ struct AttnParams {
   int* ws_arrivals;  // [num_reqs, H / heads_per_cta, q_chunks], zero at launch; null: the
                      // combine kernel merges the partials instead
   int4* ws_desc;     // balanced: [num_reqs, H / heads_per_cta] where each item's pieces went
-  // fused KV append (tensor-core kernel only; null: the caches already hold every token): query
-  // row t's new key / value, [H, D] dense at new_k + t * new_k_stride, go to slot slots[t] (< 0:
-  // none) before the item reads the block that holds them
+  // fused KV append (null: the caches already hold every token): query row t's new key / value,
+  // [H, D] dense at new_k + t * new_k_stride, go to slot slots[t] (< 0: none) before the item
+  // reads the block that holds them
   const void* new_k;
   const void* new_v;
   int64_t new_k_stride;
@@ -88,7 +88,7 @@ struct SmemHeader {
   int consumed;                       // tiles consumed before an abort
   int is_last;                        // this CTA is the last split of its item to finish
   uint64_t appended;                  // fused KV append: every consumer warp stored its head's
-                                      // new K/V (tensor-core kernel)
+                                      // new K/V
 };
 static_assert(sizeof(SmemHeader) <= kHeaderBytes, "header");
 
@@ -247,6 +247,15 @@ __global__ void __launch_bounds__(160, QPC == 1 ? 3 : 2) paged_attention_kernel(
   const int stages = p.stages;
   const int stage_elems = 2 * hpc * TILE;
   const uint32_t head_tile_bytes = TILE * sizeof(T);
+  // fused KV append (one query row per request; the host admits no other plan): the row's new
+  // token is its sequence's newest position L - 1. The split that holds it stores the head
+  // group's K and V there - each consumer warp its own head, while the producer already streams
+  // the earlier tiles - and the producer waits for those stores before the tile that holds the
+  // position. The block is the row's own (copy-on-write ran before the step).
+  const int new_pos = L - 1;
+  const bool appends = QPC == 1 && p.new_k != nullptr && nq == 1 && new_pos >= blk_begin * bs &&
+                       new_pos < (blk_begin + bps) * bs;
+  const int new_tile = new_pos / 16;
 
   // ---- set-up: the producer stages the block-table slice, thread 0 the barriers
   if (producer) {
@@ -267,6 +276,7 @@ __global__ void __launch_bounds__(160, QPC == 1 ? 3 : 2) paged_attention_kernel(
     }
     hdr.abort = 0;
     hdr.consumed = 0;
+    mbar_init(&hdr.appended, hpc);
     fence_barrier_init();
   }
   __syncthreads();
@@ -276,8 +286,17 @@ __global__ void __launch_bounds__(160, QPC == 1 ? 3 : 2) paged_attention_kernel(
     int issued = 0;
     if (lane == 0) {
       const uint64_t policy = l2_evict_first_policy();
+      bool appended = !appends;
       for (int i = 0; i < ntiles; ++i) {
         const int s = i % stages;
+        if (!appended && tile_begin + i >= new_tile) {  // the consumers' stores of the new K/V first
+          appended = true;
+          if (!mbar_wait_bounded(&hdr.appended, 0)) {
+            report(p.err, VFL_DEVERR_TIMEOUT);
+            hdr.abort = 1;
+            break;
+          }
+        }
         if (i >= stages && !mbar_wait_bounded(&hdr.empty[s], ((i / stages) - 1) & 1)) {
           report(p.err, VFL_DEVERR_TIMEOUT);
           hdr.abort = 1;
@@ -346,6 +365,28 @@ __global__ void __launch_bounds__(160, QPC == 1 ? 3 : 2) paged_attention_kernel(
 #pragma unroll
       for (int e = 0; e < VEC; ++e) qr[j][c * VEC + e] = f[e] * p.scale_log2;
     }
+  }
+  if (appends) {  // this warp's head of the row's new token, in 16-byte pieces
+    const int t = q0;
+    const int64_t slot = __ldg(p.slots + t);
+    const int64_t capacity = p.num_blocks * (int64_t)bs;
+    if (slot >= capacity) {
+      if (warp == 0 && lane == 0) report(p.err, VFL_DEVERR_SLOT);
+    } else if (slot >= 0) {  // slot < 0: a padding row, nothing to store
+      const int64_t blk = slot / bs, off = slot - blk * bs;
+      for (int c = lane; c < 2 * DCH; c += 32) {
+        const int kv = c >= DCH, ch = kv ? c - DCH : c;
+        const T* src = static_cast<const T*>(kv ? p.new_v : p.new_k) + t * (kv ? p.new_v_stride : p.new_k_stride) +
+                       h * D + ch * VEC;
+        T* dst = static_cast<T*>(const_cast<void*>(kv ? p.v_cache : p.k_cache)) +
+                 ((blk * p.num_heads + h) * bs + off) * D + ch * VEC;
+        *reinterpret_cast<uint4*>(dst) = ldg_nc_v4(src);
+      }
+    }
+    // the stores above, before the producer's bulk (async proxy) copies of the same block
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&hdr.appended);
   }
   int koff[NCH];
 #pragma unroll

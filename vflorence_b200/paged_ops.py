@@ -263,9 +263,9 @@ def attention_with_kv_cache(query: torch.Tensor, k_cache: torch.Tensor, v_cache:
 
 
 def attention_append_supported(scheduler_metadata: torch.Tensor) -> bool:
-    """Whether ``attention_with_kv_cache_append`` takes this plan (the tensor-core kernel: bf16,
-    head_dim 64; one new token per query row: at most 8 causal rows per request, rows with their
-    own tables, or one row per request)."""
+    """Whether ``attention_with_kv_cache_append`` takes this plan: one new token per query row,
+    and either one row per request (any dtype and head_dim), or with the tensor-core kernel
+    (bf16, head_dim 64) at most 8 causal rows per request or rows with their own tables."""
     return bool(N.lib().vfl_attention_append_supported(ctypes.byref(plan_of(scheduler_metadata))))
 
 
