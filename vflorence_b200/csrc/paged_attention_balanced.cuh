@@ -230,7 +230,10 @@ __global__ void __launch_bounds__(160, 3) paged_attention_tc_balanced_kernel(con
       return b;
     };
     int next_phys = have ? load_chunk(pc, b0) : 0;
-    int u = 0, issued = 0, appends_seen = 0;
+    // lane 0's unit u sits in stage s of ring round u / stages (counters, no division: the
+    // per-tile chain of the issuing thread bounds the tiles in flight)
+    int u = 0, s = 0, round = 0, issued = 0, appends_seen = 0;
+    const int H = p.num_heads;
     bool stop = false;
     bool piece_start = true;
     bool append_wait = false;  // lane 0: this piece's appended stores not yet waited for
@@ -262,8 +265,8 @@ __global__ void __launch_bounds__(160, 3) paged_attention_tc_balanced_kernel(con
       }
       const int h0 = pc.g * hpc;
       const int t_from = max(pc.t_lo, b0 * tpb), t_to = min(pc.t_hi, chunk_end * tpb);
+      int blk = t_from / tpb, sub_tile = t_from - blk * tpb;  // t == blk * tpb + sub_tile
       for (int t = t_from; t < t_to && !stop; ++t) {
-        const int blk = t / tpb;
         const int phys = __shfl_sync(0xffffffffu, phys_lane, blk - b0);
         if (lane == 0) {
           if (append_wait && t >= first_new_tile) {
@@ -275,19 +278,18 @@ __global__ void __launch_bounds__(160, 3) paged_attention_tc_balanced_kernel(con
             }
             ++appends_seen;
           }
-          const int s = u % stages;
-          if (!stop && u >= stages && !mbar_wait_bounded(&hdr.empty[s], ((u / stages) - 1) & 1)) {
+          if (!stop && round > 0 && !mbar_wait_bounded(&hdr.empty[s], (round - 1) & 1)) {
             report(p.err, VFL_DEVERR_TIMEOUT);
             hdr.abort = 1;
             stop = true;
           }
           if (!stop && *reinterpret_cast<volatile int*>(&hdr.abort)) stop = true;
-          if (!stop) {
-            fence_proxy_async_smem();
-            T* ks = s_kv + (size_t)s * stage_elems;
+          if (!stop) {  // no proxy fence: consumers only read stages (as in the item kernel)
+            T* ks = s_kv + s * stage_elems;
             T* vs = ks + hpc * TILE;
             mbar_arrive_expect_tx(&hdr.full[s], 2u * hpc * TILE * sizeof(T));
-            const int row0 = static_cast<int>(((int64_t)phys * p.num_heads + h0) * bs + (t - blk * tpb) * 16);
+            // pool rows [blocks * H * bs, 64]: the tensor maps bound them to int32
+            const int row0 = (phys * H + h0) * bs + sub_tile * 16;
             if (tpb == 1) {  // the head group's tiles are adjacent rows: one box of 16 * hpc rows
               tma_load_2d(ks, &kmap, 0, row0, &hdr.full[s], policy);
               tma_load_2d(vs, &vmap, 0, row0, &hdr.full[s], policy);
@@ -298,9 +300,17 @@ __global__ void __launch_bounds__(160, 3) paged_attention_tc_balanced_kernel(con
               }
             }
             issued = ++u;
+            if (++s == stages) {
+              s = 0;
+              ++round;
+            }
           }
         }
         stop = __shfl_sync(0xffffffffu, stop, 0);
+        if (++sub_tile == tpb) {
+          sub_tile = 0;
+          ++blk;
+        }
       }
       if (piece_ends) {
         pc = nxt;
@@ -335,7 +345,10 @@ __global__ void __launch_bounds__(160, 3) paged_attention_tc_balanced_kernel(con
     tc_load_query(p, (int64_t)s_qb[pc.r] + ln.g, ln.g < nq, pc.g * hpc + warp, ln, bq_next);
   }
   bool aborted = false;
-  int u = 0;
+  int u = 0, s = 0, round = 0;  // unit u sits in stage s of ring round u / stages
+  const uint32_t kt0 = smem_u32(s_kv + warp * TILE);
+  const uint32_t stage_bytes = stage_elems * sizeof(T);
+  const uint32_t v_off = hpc * TILE * sizeof(T);
 #pragma unroll 1
   while (have && !aborted) {
     uint32_t bq[4][2];
@@ -370,8 +383,7 @@ __global__ void __launch_bounds__(160, 3) paged_attention_tc_balanced_kernel(con
     acc.reset();
 #pragma unroll 1
     for (int t = pc.t_lo; t < pc.t_hi; ++t) {
-      const int s = u % stages;
-      if (!mbar_wait_bounded(&hdr.full[s], (u / stages) & 1)) {
+      if (!mbar_wait_bounded(&hdr.full[s], round & 1)) {
         report(p.err, VFL_DEVERR_TIMEOUT);
         if (lane == 0) {
           hdr.abort = 1;
@@ -380,12 +392,15 @@ __global__ void __launch_bounds__(160, 3) paged_attention_tc_balanced_kernel(con
         aborted = true;
         break;
       }
-      const uint32_t kt = smem_u32(s_kv + (size_t)s * stage_elems + warp * TILE);
-      const uint32_t vt = kt + hpc * TILE * sizeof(T);
-      tc_consume_tile(kt, vt, bq, col_on, t * 16, vis_c, p.scale_log2, p_tile, p_tile_u32, ln, acc);
+      const uint32_t kt = kt0 + s * stage_bytes;
+      tc_consume_tile(kt, kt + v_off, bq, col_on, t * 16, vis_c, p.scale_log2, p_tile, p_tile_u32, ln, acc);
       __syncwarp();  // P tile and K/V stage reads done before the next tile reuses them
       if (lane == 0) mbar_arrive(&hdr.empty[s]);
       ++u;
+      if (++s == stages) {
+        s = 0;
+        ++round;
+      }
     }
     if (aborted) break;
     acc.reduce_l();

@@ -287,8 +287,10 @@ __global__ void __launch_bounds__(160, QPC == 1 ? 3 : 2) paged_attention_kernel(
     if (lane == 0) {
       const uint64_t policy = l2_evict_first_policy();
       bool appended = !appends;
+      // tile i sits in stage s of ring round i / stages, tile_begin + i == blk * tpb + sub_tile:
+      // counters, not divisions, on this thread's per-tile chain
+      int s = 0, round = 0, blk = blk_begin, sub_tile = 0;
       for (int i = 0; i < ntiles; ++i) {
-        const int s = i % stages;
         if (!appended && tile_begin + i >= new_tile) {  // the consumers' stores of the new K/V first
           appended = true;
           if (!mbar_wait_bounded(&hdr.appended, 0)) {
@@ -297,18 +299,16 @@ __global__ void __launch_bounds__(160, QPC == 1 ? 3 : 2) paged_attention_kernel(
             break;
           }
         }
-        if (i >= stages && !mbar_wait_bounded(&hdr.empty[s], ((i / stages) - 1) & 1)) {
+        if (round > 0 && !mbar_wait_bounded(&hdr.empty[s], (round - 1) & 1)) {
           report(p.err, VFL_DEVERR_TIMEOUT);
           hdr.abort = 1;
           break;
         }
         if (*reinterpret_cast<volatile int*>(&hdr.abort)) break;
-        fence_proxy_async_smem();
-        const int tile = tile_begin + i;
-        const int blk = tile / tpb;
-        const int sub_tile = tile - blk * tpb;
+        // no proxy fence before the copy: the consumers only read a stage, and their reads
+        // have returned before they arrive on its empty barrier, which this thread waited on
         const int64_t phys = hdr.table[blk - blk_begin];
-        T* ks = s_kv + (size_t)s * stage_elems;
+        T* ks = s_kv + s * stage_elems;
         T* vs = ks + hpc * TILE;
         mbar_arrive_expect_tx(&hdr.full[s], 2u * hpc * head_tile_bytes);
         const int64_t base = ((phys * p.num_heads + h0) * bs + sub_tile * 16) * D;
@@ -327,6 +327,14 @@ __global__ void __launch_bounds__(160, QPC == 1 ? 3 : 2) paged_attention_kernel(
           }
         }
         issued = i + 1;
+        if (++s == stages) {
+          s = 0;
+          ++round;
+        }
+        if (++sub_tile == tpb) {
+          sub_tile = 0;
+          ++blk;
+        }
       }
       griddep_launch_dependents();  // the combine launch may start; it waits for the grid
     }
@@ -408,10 +416,10 @@ __global__ void __launch_bounds__(160, QPC == 1 ? 3 : 2) paged_attention_kernel(
   }
 
   bool aborted = false;
+  int s = 0, round = 0;  // tile i sits in stage s of ring round i / stages
 #pragma unroll 1
   for (int i = 0; i < ntiles; ++i) {
-    const int s = i % stages;
-    if (!mbar_wait_bounded(&hdr.full[s], (i / stages) & 1)) {
+    if (!mbar_wait_bounded(&hdr.full[s], round & 1)) {
       report(p.err, VFL_DEVERR_TIMEOUT);
       if (lane == 0) {
         hdr.abort = 1;
@@ -495,6 +503,10 @@ __global__ void __launch_bounds__(160, QPC == 1 ? 3 : 2) paged_attention_kernel(
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&hdr.empty[s]);  // this warp is done with stage s
+    if (++s == stages) {
+      s = 0;
+      ++round;
+    }
   }
   __syncthreads();  // pairs with the producer's barrier (abort bookkeeping)
   if (aborted || *reinterpret_cast<volatile int*>(&hdr.abort)) return;

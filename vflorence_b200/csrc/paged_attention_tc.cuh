@@ -160,13 +160,23 @@ __device__ __forceinline__ void tc_consume_tile(uint32_t kt, uint32_t vt, const 
                                                 float scale_log2, __nv_bfloat16* p_tile, uint32_t p_tile_u32,
                                                 const TcLane& ln, TcAccum& acc) {
   const int g = ln.g, tq = ln.tq;
-  float sc[4] = {0.f, 0.f, 0.f, 0.f};
+  // Every K fragment load first, S in two accumulators (the even and odd 16-dim steps, two mma
+  // deep instead of four), and the V fragments, which do not depend on P, loaded before the
+  // softmax. (Measured the same as the one-accumulator order: the tile's time is set by the
+  // producer's issue rate and the P exchange, not by this chain.)
+  uint32_t ka[4][4];
 #pragma unroll
-  for (int kk = 0; kk < 4; ++kk) {
-    uint32_t a[4];
-    ldsm_x4(swz(kt, ln.k_row, 2 * kk + ln.k_chunk_hi), a);
-    mma_bf16_16x8x16(sc, a, bq[kk][0], bq[kk][1]);
-  }
+  for (int kk = 0; kk < 4; ++kk) ldsm_x4(swz(kt, ln.k_row, 2 * kk + ln.k_chunk_hi), ka[kk]);
+  float sc[4] = {0.f, 0.f, 0.f, 0.f}, sd[4] = {0.f, 0.f, 0.f, 0.f};
+  mma_bf16_16x8x16(sc, ka[0], bq[0][0], bq[0][1]);
+  mma_bf16_16x8x16(sd, ka[1], bq[1][0], bq[1][1]);
+  mma_bf16_16x8x16(sc, ka[2], bq[2][0], bq[2][1]);
+  mma_bf16_16x8x16(sd, ka[3], bq[3][0], bq[3][1]);
+  uint32_t va[4][4];
+#pragma unroll
+  for (int mt = 0; mt < 4; ++mt) ldsm_x4_trans(swz(vt, ln.v_row, 2 * mt + ln.v_chunk_hi), va[mt]);
+#pragma unroll
+  for (int e = 0; e < 4; ++e) sc[e] += sd[e];
   constexpr float kRescaleSlack = 8.f;
   __nv_bfloat16 pb[4];
 #pragma unroll
@@ -204,11 +214,7 @@ __device__ __forceinline__ void tc_consume_tile(uint32_t kt, uint32_t vt, const 
   asm volatile("ld.shared.b32 %0, [%1];" : "=r"(bp1) : "r"(p_tile_u32 + (g * 16 + 2 * tq + 8) * 2));
   // O^T += V^T . P^T over the tile's 16 tokens, four 16-dim m-tiles
 #pragma unroll
-  for (int mt = 0; mt < 4; ++mt) {
-    uint32_t a[4];
-    ldsm_x4_trans(swz(vt, ln.v_row, 2 * mt + ln.v_chunk_hi), a);
-    mma_bf16_16x8x16(acc.o[mt], a, bp0, bp1);
-  }
+  for (int mt = 0; mt < 4; ++mt) mma_bf16_16x8x16(acc.o[mt], va[mt], bp0, bp1);
 }
 
 // The B operand of S = K.Q^T for query row `row` (g < nq) of head h: dims 16kk + 2tq (+1) and
@@ -379,13 +385,17 @@ __global__ void __launch_bounds__(160, 3) paged_attention_tc_kernel(const AttnPa
     // units: (tile position, distinct block of the position); u counts them across the item
     int issued = 0;
     if (lane == 0) {
+      // One thread issues every copy, so its per-unit bookkeeping is a serial chain that sets
+      // how many tiles a CTA keeps in flight: stage, ring round, block and sub-tile advance by
+      // counters (no division), and row arithmetic stays in 32 bits.
       const uint64_t policy = p.row_tables ? l2_evict_normal_policy() : l2_evict_first_policy();
-      int u = 0;
+      const uint32_t tx_bytes = 2u * hpc * head_tile_bytes;
+      const int H = p.num_heads;
+      int u = 0, s = 0, round = 0;        // unit u sits in stage s of ring round u / stages
+      int blk = blk_begin, sub_tile = 0;  // tile_begin + i == blk * tpb + sub_tile
       bool stop = false, appended = !appends;
       for (int i = 0; i < ntiles && !stop; ++i) {
         const int tile = tile_begin + i;
-        const int blk = tile / tpb;
-        const int sub_tile = tile - blk * tpb;
         if (!appended && tile >= first_new_tile) {  // the consumers' stores of the new K/V first
           appended = true;
           if (!mbar_wait_bounded(&hdr.appended, 0)) {
@@ -400,8 +410,7 @@ __global__ void __launch_bounds__(160, 3) paged_attention_tc_kernel(const AttnPa
         for (int j = tiles.count_and_get(blk - blk_begin, 0, done, &phys, &mask); j < nq;
              j = tiles.count_and_get(blk - blk_begin, j + 1, done, &phys, &mask)) {
           done |= mask;
-          const int s = u % stages;
-          if (u >= stages && !mbar_wait_bounded(&hdr.empty[s], ((u / stages) - 1) & 1)) {
+          if (round > 0 && !mbar_wait_bounded(&hdr.empty[s], (round - 1) & 1)) {
             report(p.err, VFL_DEVERR_TIMEOUT);
             hdr.abort = 1;
             stop = true;
@@ -411,11 +420,14 @@ __global__ void __launch_bounds__(160, 3) paged_attention_tc_kernel(const AttnPa
             stop = true;
             break;
           }
-          fence_proxy_async_smem();
-          T* ks = s_kv + (size_t)s * stage_elems;
+          // No proxy fence before the copy: the consumers only read a stage (ldmatrix), those
+          // reads have returned before their warp arrives on the stage's empty barrier, and
+          // this thread waited on that barrier.
+          T* ks = s_kv + s * stage_elems;
           T* vs = ks + hpc * TILE;
-          mbar_arrive_expect_tx(&hdr.full[s], 2u * hpc * head_tile_bytes);
-          const int row0 = static_cast<int>((phys * p.num_heads + h0) * bs + sub_tile * 16);
+          mbar_arrive_expect_tx(&hdr.full[s], tx_bytes);
+          // rows of the pool seen as [blocks * H * bs, 64]; the tensor maps bound them to int32
+          const int row0 = (static_cast<int>(phys) * H + h0) * bs + sub_tile * 16;
           if (tpb == 1) {  // the head group's tiles are adjacent rows: one box of 16 * hpc rows
             tma_load_2d(ks, &kmap, 0, row0, &hdr.full[s], policy);
             tma_load_2d(vs, &vmap, 0, row0, &hdr.full[s], policy);
@@ -426,6 +438,14 @@ __global__ void __launch_bounds__(160, 3) paged_attention_tc_kernel(const AttnPa
             }
           }
           issued = ++u;
+          if (++s == stages) {
+            s = 0;
+            ++round;
+          }
+        }
+        if (++sub_tile == tpb) {
+          sub_tile = 0;
+          ++blk;
         }
       }
       griddep_launch_dependents();  // the combine launch may start; it waits for the grid
@@ -461,11 +481,14 @@ __global__ void __launch_bounds__(160, 3) paged_attention_tc_kernel(const AttnPa
   const uint32_t p_tile_u32 = smem_u32(p_tile);
 
   bool aborted = false;
-  int u = 0;
+  // unit u sits in stage s of ring round u / stages; tile_begin + i == (blk_begin + bi) * tpb + sub
+  int u = 0, s = 0, round = 0, bi = 0, sub = 0;
+  const uint32_t kt0 = smem_u32(s_kv + warp * TILE);
+  const uint32_t stage_bytes = stage_elems * sizeof(T);
+  const uint32_t v_off = hpc * TILE * sizeof(T);
 #pragma unroll 1
   for (int i = 0; i < ntiles && !aborted; ++i) {
     const int tok0 = (tile_begin + i) * 16;
-    const int bi = (tile_begin + i) / tpb - blk_begin;
     unsigned done = 0;
     int64_t phys_unused;
     unsigned mask;
@@ -473,8 +496,7 @@ __global__ void __launch_bounds__(160, 3) paged_attention_tc_kernel(const AttnPa
     for (int j = tiles.count_and_get(bi, 0, done, &phys_unused, &mask); j < nq;
          j = tiles.count_and_get(bi, j + 1, done, &phys_unused, &mask)) {
       done |= mask;
-      const int s = u % stages;
-      if (!mbar_wait_bounded(&hdr.full[s], (u / stages) & 1)) {
+      if (!mbar_wait_bounded(&hdr.full[s], round & 1)) {
         report(p.err, VFL_DEVERR_TIMEOUT);
         if (lane == 0) {
           hdr.abort = 1;
@@ -483,14 +505,21 @@ __global__ void __launch_bounds__(160, 3) paged_attention_tc_kernel(const AttnPa
         aborted = true;
         break;
       }
-      const uint32_t kt = smem_u32(s_kv + (size_t)s * stage_elems + warp * TILE);
-      const uint32_t vt = kt + hpc * TILE * sizeof(T);
+      const uint32_t kt = kt0 + s * stage_bytes;
       // the rows this unit's block belongs to (every row without row tables)
       const bool row_on[2] = {col_on[0] && ((mask >> (2 * tq)) & 1u), col_on[1] && ((mask >> (2 * tq + 1)) & 1u)};
-      tc_consume_tile(kt, vt, bq, row_on, tok0, vis_c, p.scale_log2, p_tile, p_tile_u32, ln, acc);
+      tc_consume_tile(kt, kt + v_off, bq, row_on, tok0, vis_c, p.scale_log2, p_tile, p_tile_u32, ln, acc);
       __syncwarp();  // P tile and K/V stage reads done before the next tile reuses them
       if (lane == 0) mbar_arrive(&hdr.empty[s]);
       ++u;
+      if (++s == stages) {
+        s = 0;
+        ++round;
+      }
+    }
+    if (++sub == tpb) {
+      sub = 0;
+      ++bi;
     }
   }
   __syncthreads();
